@@ -1,0 +1,160 @@
+/*
+ * tileops_b200.h — C ABI of libtileops_b200.so, the sm_100a kernels behind the
+ * TileOps quantized-linear facade (AWQ W4A16, INT8 W8A8, FP8 e4m3, symmetric INT8).
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are CUDA device pointers on the current device; sizes are int64 element
+ *     counts; tensors are dense row-major unless a stride argument says otherwise.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is
+ *     asynchronous and stream-ordered; nothing is synchronised inside the library.
+ *   - The library never allocates device memory. Kernels that need scratch take a
+ *     caller-owned `workspace` of at least the size its `*_workspace_size` query returns.
+ *   - Return value: TO_OK (0) or a negative TO_E* status; to_last_error_string() gives the
+ *     text of the calling thread's last failure. The Python facade maps TO_EINVAL to
+ *     ValueError, TO_EUNSUPPORTED to NotImplementedError / TypeError and the rest to
+ *     RuntimeError, the exception types the reference raises.
+ *
+ * Each declaration names the reference function (path within the TileOps project,
+ * file:line) whose arithmetic it reproduces. In the reference these run as PyTorch
+ * tensor expressions or TileLang kernels reached through
+ * tileops/runtime/_infra.py:492 (dispatch_compile_quant) and
+ * tileops/runtime/__init__.py:446,488 (invoke_quant_kernel, invoke_per_token_quant_int8_kernel).
+ */
+#ifndef TILEOPS_B200_H_
+#define TILEOPS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TO_API __attribute__((visibility("default")))
+#else
+#define TO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------- */
+#define TO_OK 0
+#define TO_EINVAL (-1)       /* bad shape / value argument           -> ValueError        */
+#define TO_EUNSUPPORTED (-2) /* dtype or option this build rejects    -> TypeError / NIE   */
+#define TO_ECUDA (-3)        /* CUDA runtime / launch failure         -> RuntimeError      */
+#define TO_ETIMEOUT (-4)     /* a bounded device wait gave up         -> RuntimeError      */
+#define TO_ENOSPACE (-5)     /* workspace smaller than *_workspace_size                     */
+
+/* ---- dtype codes ------------------------------------------------------------------- */
+#define TO_F32 0
+#define TO_F16 1
+#define TO_BF16 2
+#define TO_I8 3
+#define TO_E4M3 4 /* float8_e4m3fn (OCP e4m3, finite-only, max 448) */
+#define TO_I32 5
+#define TO_I64 6
+
+/* ---- library / device ---------------------------------------------------------------- */
+TO_API const char* to_version(void);
+/* Text of the calling thread's most recent failure ("" if none). */
+TO_API const char* to_last_error_string(void);
+/* TO_OK when `device` is an sm_100 (B200-class) GPU, else TO_EUNSUPPORTED. */
+TO_API int to_device_check(int device);
+/* Reads (and with clear != 0 resets) the device-side error word that kernels with bounded
+ * waits set when a wait gives up: 0 = no error. Synchronises the current device. */
+TO_API int to_device_error_word(int* value, int clear);
+
+/* ---- symmetric INT8 (tileops/quant.py) ------------------------------------------------
+ * q = clamp(round_half_even(float(x) / scale), -128, 127);  y = out_dtype(float(q) * scale).
+ * Per-channel: x is viewed as [outer, channels, inner] (the channel axis is `dim`), one
+ * fp32 scale per channel, output in the same layout as the input (no permute copies). */
+/* replaces tileops/quant.py:53 quantize_per_tensor (kernel backend/cuda/quant.py:32) */
+TO_API int to_quant_per_tensor_i8(const void* x, int x_dtype, const float* scale, int8_t* q,
+                           int64_t n, void* stream);
+/* replaces tileops/quant.py:96 dequantize_per_tensor (kernel backend/cuda/quant.py:49) */
+TO_API int to_dequant_per_tensor_i8(const int8_t* q, const float* scale, void* y, int y_dtype,
+                             int64_t n, void* stream);
+/* replaces tileops/quant.py:144 quantize_per_channel (kernel backend/cuda/quant.py:65) */
+TO_API int to_quant_per_channel_i8(const void* x, int x_dtype, const float* scale, int8_t* q,
+                            int64_t outer, int64_t channels, int64_t inner, void* stream);
+/* replaces tileops/quant.py:193 dequantize_per_channel (kernel backend/cuda/quant.py:87) */
+TO_API int to_dequant_per_channel_i8(const int8_t* q, const float* scale, void* y, int y_dtype,
+                              int64_t outer, int64_t channels, int64_t inner, void* stream);
+
+/* ---- dynamic quantisation (tileops/quant_int8.py, tileops/quant_fp8.py) ---------------- */
+/* Bytes of workspace the tensor-wide quantisers need (one amax word, padded). */
+TO_API size_t to_input_quant_workspace_size(void);
+/* replaces tileops/quant_int8.py:29 input_to_int8. Arithmetic in x_dtype exactly as the
+ * reference's tensor expression: s = dtype(dtype(1/amax) * 127); q = trunc(clamp(x*s)).
+ * Writes q [n] and dq_scale[0] = 1/float(s). */
+TO_API int to_input_to_int8(const void* x, int x_dtype, int64_t n, int8_t* q, float* dq_scale,
+                     void* workspace, size_t workspace_bytes, void* stream);
+/* replaces tileops/quant_fp8.py:52 input_to_float8 (e4m3fn; same arithmetic with 448). */
+TO_API int to_input_to_fp8(const void* x, int x_dtype, int64_t n, void* q, float* dq_scale,
+                    void* workspace, size_t workspace_bytes, void* stream);
+/* replaces tileops/quant_int8.py:109 per_token_group_quant_int8 and :54 per_token_quant_int8
+ * (group_size = K). x is [n_groups, group_size] contiguous; scales[g] = max(absmax,eps)/127. */
+TO_API int to_per_token_group_quant_i8(const void* x, int x_dtype, int64_t n_groups,
+                                int64_t group_size, float eps, int8_t* q, float* scales,
+                                void* stream);
+/* replaces tileops/quant_fp8.py:83 per_token_group_quant_fp8 (via _quantize_groups_fp8 :66).
+ * ue8m0 != 0 rounds each scale up to a power of two (quant_fp8.py:48). When cm_rows > 0 the
+ * scales are written in the layout the reference's column_major_scales option returns,
+ * s_flat.reshape(..., cm_groups, cm_rows).transpose(-2, -1).contiguous() (quant_fp8.py:129-136):
+ * within each batch of cm_rows x cm_groups scales, flat scale t goes to row t % cm_rows,
+ * column t / cm_rows of a contiguous [cm_rows, cm_groups] array. */
+TO_API int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups,
+                                 int64_t group_size, float eps, int ue8m0, int64_t cm_rows,
+                                 int64_t cm_groups, void* q, float* scales, void* stream);
+
+/* ---- block dequantisation ------------------------------------------------------------- */
+/* replaces tileops/quant_int8.py:136 block_dequant: y[n,k] = float(q[n,k]) * s[n/bn, k/bk]. */
+TO_API int to_block_dequant_i8(const int8_t* q, const float* s, float* y, int64_t n, int64_t k,
+                        int64_t block_n, int64_t block_k, void* stream);
+/* replaces tileops/quant_fp8.py:143 block_dequant (e4m3fn input). */
+TO_API int to_block_dequant_fp8(const void* q, const float* s, float* y, int64_t n, int64_t k,
+                         int64_t block_n, int64_t block_k, void* stream);
+
+/* ---- AWQ W4A16 (tileops/quant_awq.py) --------------------------------------------------
+ * Packed layout: eight 4-bit values per 32-bit word; logical column 8c+i sits in nibble
+ * ORDER[i] of word c with ORDER = (0,4,1,5,2,6,3,7) (quant_awq.py:22). */
+/* replaces quant_awq.py:55 pack_awq_int4: in [rows, 8*cols8] (TO_I32 or TO_I64), out [rows, cols8]. */
+TO_API int to_awq_pack(const void* unpacked, int in_dtype, int32_t* packed, int64_t rows,
+                int64_t cols8, void* stream);
+/* replaces quant_awq.py:41 unpack_awq_int4: in [rows, cols8] (TO_I32 or TO_I64, low 32 bits
+ * used), out int64 [rows, 8*cols8]. */
+TO_API int to_awq_unpack(const void* packed, int in_dtype, int64_t* out, int64_t rows, int64_t cols8,
+                  void* stream);
+/* replaces quant_awq.py:68 awq_dequantize_triton: out[k,n] = s_dtype((w-z) * s) with
+ * qweight [K, N/8], scales [K/G, N] (s_dtype F16/BF16/F32), qzeros [K/G, N/8]. */
+TO_API int to_awq_dequant(const int32_t* qweight, const void* scales, int s_dtype,
+                   const int32_t* qzeros, void* out, int64_t K, int64_t N, int64_t group_size,
+                   void* stream);
+/* replaces quant_awq.py:112 awq_gemm_triton: y [M,N] = x [M,K] @ dequant(W), x and y in
+ * s_dtype (the facade casts x first, as the reference does), fp32 accumulation. Small M
+ * runs the streaming GEMV; larger M the tcgen05 tensor-core GEMM. */
+TO_API size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_t group_size);
+TO_API int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
+                const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
+                int64_t group_size, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- W8A8 block-scaled GEMMs --------------------------------------------------------------
+ * C[m,n] = sum_kb  (sum_{k in kb} A[m,k]*B[n,k]) * a_s[m,kb] * b_s[n/block_n, kb]
+ * A [M,K] row-major, B [N,K] row-major ("NT"), a_s [M, ceil(K/block_k)],
+ * b_s [ceil(N/block_n), ceil(K/block_k)], C [M,N] in c_dtype (F32/F16/BF16).
+ * bias (optional, c_dtype, [N]) is added after the rounding to c_dtype and rounded again,
+ * the order of `output + bias` in apply_w8a8_block_*_linear. */
+/* replaces tileops/quant_int8.py:180 w8a8_block_int8_matmul. acc_out (optional, int32
+ * [M,N]) receives the exact integer dot products sum_k A[m,k]*B[n,k]. */
+TO_API int to_w8a8_i8_gemm(const int8_t* a, const int8_t* b, const float* a_s, const float* b_s,
+                    void* c, int c_dtype, const void* bias, int32_t* acc_out, int64_t M,
+                    int64_t N, int64_t K, int64_t block_n, int64_t block_k, void* stream);
+/* replaces tileops/quant_fp8.py:188 w8a8_block_fp8_matmul (A, B e4m3fn; fp32 accumulation). */
+TO_API int to_w8a8_fp8_gemm(const void* a, const void* b, const float* a_s, const float* b_s,
+                     void* c, int c_dtype, const void* bias, int64_t M, int64_t N, int64_t K,
+                     int64_t block_n, int64_t block_k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEOPS_B200_H_ */

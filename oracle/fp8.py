@@ -1,0 +1,88 @@
+"""FP8 e4m3 oracle (test infrastructure only) -- restates tileops/quant_fp8.py."""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .numerics import e4m3_to_f32, f32_to_e4m3, log2_f32, rounder
+
+FP8_MAX = 448.0  # torch.finfo(torch.float8_e4m3fn).max (quant_fp8.py:39-45)
+
+
+def ue8m0(scale: np.ndarray) -> np.ndarray:
+    """quant_fp8.py:48-49: exp2(ceil(log2(max(s, 1e-30)))) with log2 rounded to fp32."""
+    s = np.maximum(np.asarray(scale, np.float32), np.float32(1e-30))
+    return np.ldexp(np.float32(1.0), np.ceil(log2_f32(s)).astype(np.int32)).astype(np.float32)
+
+
+def input_to_float8(x_f32: np.ndarray, dtype: str):
+    """quant_fp8.py:52-63 in ``dtype``: amax = T(max(amax, 1e-12)); s = T(T(1/amax) * 448);
+    q = e4m3(clamp(T(x * s), -448, 448)); returns (codes, float32(1 / s))."""
+    rnd = rounder(dtype)
+    x = rnd(np.asarray(x_f32, dtype=np.float32))
+    amax = np.float32(np.max(np.abs(x)))
+    amax = rnd(np.maximum(amax, np.float32(1e-12)))
+    r = rnd(np.float32(1.0) / amax)
+    s = rnd(np.float32(r) * np.float32(FP8_MAX))
+    y = np.clip(rnd(x * np.float32(s)), -FP8_MAX, FP8_MAX)
+    return f32_to_e4m3(y), np.float32(np.float32(1.0) / np.float32(s))
+
+
+def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10, use_ue8m0: bool = False,
+                column_major: bool = False):
+    """quant_fp8.py:66-140: scale = max(absmax, eps) / 448 [-> ue8m0];
+    q = e4m3(clamp(x / scale, +-448)). Returns (codes shaped like x, scales [..., K/G]; with
+    column_major, the reference's reshape-then-transpose of the flat scales)."""
+    x = np.asarray(x_f32, dtype=np.float32)
+    lead, k = x.shape[:-1], x.shape[-1]
+    flat = x.reshape(-1, group_size)
+    absmax = np.maximum(np.max(np.abs(flat), axis=-1), np.float32(eps))
+    scale = (absmax / np.float32(FP8_MAX)).astype(np.float32)
+    if use_ue8m0:
+        scale = ue8m0(scale)
+    y = np.clip(flat / scale[:, None], -FP8_MAX, FP8_MAX).astype(np.float32)
+    q = f32_to_e4m3(y).reshape(*lead, k)
+    if column_major:
+        # quant_fp8.py:134-136: s_flat.reshape(..., G_, M).transpose(-2, -1).contiguous()
+        m = x.shape[-2]
+        s = np.ascontiguousarray(np.swapaxes(scale.reshape(*x.shape[:-2], k // group_size, m), -1, -2))
+    else:
+        s = scale.reshape(*lead, k // group_size)
+    return q, s
+
+
+def block_dequant(codes: np.ndarray, s: np.ndarray, block_size) -> np.ndarray:
+    """quant_fp8.py:143-168: y[n, k] = float32(q[n, k]) * s[n // bn, k // bk]."""
+    bn, bk = block_size
+    n, k = codes.shape
+    rows = np.arange(n) // bn
+    cols = np.arange(k) // bk
+    return (e4m3_to_f32(codes) * np.asarray(s, np.float32)[rows][:, cols]).astype(np.float32)
+
+
+def block_matmul(a_codes, b_codes, a_s, b_s, block_size, out_dtype: str) -> np.ndarray:
+    """quant_fp8.py:188-236 with per-k-block sums in float64 (e4m3 products are exact), then
+    scaled: the fp32-accumulated reference of the tolerance."""
+    bn, bk = block_size
+    a = e4m3_to_f32(a_codes).astype(np.float64)
+    b = e4m3_to_f32(b_codes).astype(np.float64)
+    m, k = a.shape
+    n = b.shape[0]
+    kt = -(-k // bk)
+    rows_b = np.arange(n) // bn
+    acc = np.zeros((m, n), dtype=np.float64)
+    for kb in range(kt):
+        sl = slice(kb * bk, min(k, (kb + 1) * bk))
+        acc += (a[:, sl] @ b[:, sl].T) * a_s[:, kb].astype(np.float64)[:, None] * \
+            b_s[rows_b, kb].astype(np.float64)[None, :]
+    return rounder(out_dtype)(acc.astype(np.float32))
+
+
+def block_matmul_reference_cpu(a_codes, b_codes, a_s, b_s, block_size, out_dtype: str):
+    """The reference's CPU algorithm as it runs (fp32 dequant, fp32 GEMM)."""
+    bn, bk = block_size
+    k = a_codes.shape[1]
+    cols = np.arange(k) // bk
+    a_f = e4m3_to_f32(a_codes) * np.asarray(a_s, np.float32)[:, cols]
+    b_f = block_dequant(b_codes, b_s, block_size)
+    return rounder(out_dtype)(a_f @ b_f.T)

@@ -1,0 +1,152 @@
+"""The C-ABI library loads, exports exactly what include/tileops_b200.h declares, and the
+facade validates arguments like the reference before touching a device. No GPU needed:
+no entry point that launches a kernel is called here."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import tileops_b200 as tob
+from tileops_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "tileops_b200.h"
+
+
+def _declared() -> dict[str, int]:
+    text = HEADER.read_text()
+    out = {}
+    for m in re.finditer(r"TO_API\s+[\w\s\*]+?\b(to_\w+)\s*\(([^)]*)\)", text):
+        args = m.group(2).strip()
+        out[m.group(1)] = 0 if args in ("", "void") else len(args.split(","))
+    return out
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not _lib.LIB_PATH.exists():
+        from tileops_b200 import build
+
+        build.build()
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    decl = _declared()
+    assert len(decl) >= 20
+    for name in ("to_awq_gemm", "to_w8a8_i8_gemm", "to_w8a8_fp8_gemm", "to_input_to_fp8",
+                 "to_per_token_group_quant_fp8", "to_quant_per_channel_i8"):
+        assert name in decl
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+
+
+def test_signature_table_matches_header():
+    decl = _declared()
+    assert set(decl) == set(_lib.SIGNATURES), set(decl) ^ set(_lib.SIGNATURES)
+    for name, nargs in decl.items():
+        assert len(_lib.SIGNATURES[name][1]) == nargs, name
+
+
+def test_version_and_error_string(lib):
+    assert "sm_100a" in _lib.version()
+    assert isinstance(_lib.last_error(), str)
+
+
+def test_workspace_queries_need_no_device(lib):
+    assert lib.to_input_quant_workspace_size() >= 4
+    assert lib.to_awq_gemm_workspace_size(1, 4096, 4096, 128) >= 0
+
+
+def test_status_mapping():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.TO_EINVAL, "x")
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.TO_EUNSUPPORTED, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.TO_ECUDA, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.TO_ETIMEOUT, "x")
+
+
+def test_cpu_tensors_are_rejected_not_computed():
+    x = torch.randn(4, 16)
+    with pytest.raises(TypeError, match="CUDA"):
+        tob.per_token_quant_int8(x)
+    with pytest.raises(TypeError, match="CUDA"):
+        tob.input_to_float8(x)
+    with pytest.raises(TypeError, match="CUDA"):
+        tob.pack_awq_int4(torch.zeros(2, 8, dtype=torch.int64))
+
+
+def test_reference_validation_order():
+    # Shape / value errors the reference raises before any compute.
+    with pytest.raises(ValueError, match="divisible by 8"):
+        tob.pack_awq_int4(torch.zeros(2, 7, dtype=torch.int64))
+    with pytest.raises(TypeError, match="int32"):
+        tob.unpack_awq_int4(torch.zeros(2, 7, dtype=torch.float32))
+    with pytest.raises(ValueError, match="must be 2-D"):
+        tob.awq_gemm(torch.zeros(4), torch.zeros(4, 1, dtype=torch.int32),
+                     torch.zeros(1, 8), torch.zeros(1, 1, dtype=torch.int32), 1)
+    with pytest.raises(ValueError, match="power of 2"):
+        tob.awq_gemm(torch.zeros(1, 32), torch.zeros(32, 8, dtype=torch.int32),
+                     torch.zeros(1, 64, dtype=torch.float16), torch.zeros(1, 8, dtype=torch.int32), 3)
+    with pytest.raises(ValueError, match="group_size"):
+        tob.awq_dequantize(torch.zeros(96, 8, dtype=torch.int32), torch.zeros(2, 64),
+                           torch.zeros(2, 8, dtype=torch.int32))
+    with pytest.raises(NotImplementedError, match="tma_aligned_scales"):
+        tob.per_token_group_quant_fp8(torch.zeros(2, 8), 8, tma_aligned_scales=True)
+    with pytest.raises(ValueError, match="divisible"):
+        tob.per_token_group_quant_fp8(torch.zeros(2, 9), 8)
+    with pytest.raises(TypeError, match="int8"):
+        tob.per_token_group_quant_int8(torch.zeros(2, 8), 8, dtype=torch.int16)
+    with pytest.raises(ValueError, match="length 2"):
+        tob.w8a8_block_int8_matmul(torch.zeros(2, 8, dtype=torch.int8),
+                                   torch.zeros(2, 8, dtype=torch.int8), torch.ones(2, 1),
+                                   torch.ones(1, 1), [2, 4, 8])
+    with pytest.raises(TypeError, match="must be int8"):
+        tob.w8a8_block_int8_matmul(torch.zeros(2, 8), torch.zeros(2, 8, dtype=torch.int8),
+                                   torch.ones(2, 1), torch.ones(1, 1), [2, 8])
+    with pytest.raises(TypeError, match="FP8"):
+        tob.w8a8_block_fp8_matmul(torch.zeros(2, 8), torch.zeros(2, 8), torch.ones(2, 1),
+                                  torch.ones(1, 1), [2, 8])
+    with pytest.raises(ValueError, match="input_scale"):
+        tob.apply_w8a8_block_int8_linear(torch.zeros(2, 8), torch.zeros(2, 8, dtype=torch.int8),
+                                         [2, 8], torch.ones(1, 1), input_scale=torch.ones(1))
+    with pytest.raises(TypeError, match="float32"):
+        tob.quantize_per_tensor(torch.zeros(4), torch.ones(1, dtype=torch.float16))
+    with pytest.raises(ValueError, match="positive"):
+        tob.quantize_per_tensor(torch.zeros(4), torch.zeros(1))
+    with pytest.raises(TypeError, match="floating-point"):
+        tob.quantize_per_tensor(torch.zeros(4, dtype=torch.int32), torch.ones(1))
+    with pytest.raises(TypeError, match="out_dtype"):
+        tob.dequantize_per_tensor(torch.zeros(4, dtype=torch.int8), torch.ones(1),
+                                  out_dtype=torch.int32)
+
+
+def test_fp8_dtype_helpers():
+    assert tob.is_fp8(torch.float8_e4m3fn)
+    assert tob.is_fp8(torch.zeros(1, dtype=torch.float8_e4m3fn))
+    assert not tob.is_fp8(torch.float16)
+    assert tob.default_fp8_dtype() == torch.float8_e4m3fn
+    assert tob.get_fp8_min_max() == (-448.0, 448.0)
+    assert tob.get_fp8_min_max(torch.float8_e4m3fnuz) == (-224.0, 224.0)
+
+
+def test_dropin_module_names():
+    import tileops
+    import tileops.quant_awq as qa
+
+    assert tileops.awq_gemm is tob.awq_gemm
+    assert qa.REVERSE_AWQ_ORDER == (0, 4, 1, 5, 2, 6, 3, 7)
+    assert tileops.AWQ_TRITON_SUPPORTED_GROUP_SIZES == [-1, 32, 64, 128]
+    for name in ("block_dequant_fp8", "w8a8_triton_block_scaled_mm", "awq_dequantize_triton",
+                 "apply_w8a8_block_fp8_linear", "dequantize_per_channel"):
+        assert hasattr(tileops, name)

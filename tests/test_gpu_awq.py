@@ -1,0 +1,109 @@
+"""GPU parity of the AWQ kernels: pack/unpack/dequant bit-exact against the reference's
+outputs, GEMV/GEMM within rtol=atol=1e-2 of the fp32-accumulated oracle (the tolerance the
+path is specified to)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import tileops_b200 as tob
+from oracle import awq as oawq
+
+pytestmark = pytest.mark.gpu
+
+RTOL = ATOL = 1e-2
+_DT = {"f16": torch.float16, "bf16": torch.bfloat16}
+
+
+def make_awq(k, n, g, dtype, gen, lo=0.002, hi=0.02):
+    """AWQ weights as the workloads specify them: int4 U{0..15}, zeros U{0..15},
+    scales U(lo, hi), packed in AWQ order (oracle packer, checked against the reference)."""
+    w = torch.randint(0, 16, (k, n), generator=gen, dtype=torch.int64)
+    z = torch.randint(0, 16, (k // g, n), generator=gen, dtype=torch.int64)
+    s = (torch.rand(k // g, n, generator=gen) * (hi - lo) + lo).to(dtype)
+    qw = torch.from_numpy(oawq.pack(w.numpy()))
+    qz = torch.from_numpy(oawq.pack(z.numpy()))
+    return qw, s, qz
+
+
+def test_pack_unpack_golden(cuda, golden):
+    g = golden("awq.npz")
+    c = g["roundtrip"]
+    packed = tob.pack_awq_int4(c.tensor("x", cuda))
+    assert packed.dtype == torch.int32
+    assert np.array_equal(packed.cpu().numpy(), c["packed"])
+    back = tob.unpack_awq_int4(packed)
+    assert back.dtype == torch.int64
+    assert np.array_equal(back.cpu().numpy(), c["unpacked"])
+    c = g["pack_wide"]
+    assert np.array_equal(tob.pack_awq_int4(c.tensor("x", cuda)).cpu().numpy(), c["packed"])
+
+
+def test_pack_unpack_roundtrip_int32_and_int64(cuda):
+    g = torch.Generator().manual_seed(3)
+    x = torch.randint(0, 16, (33, 8 * 129), generator=g, dtype=torch.int64)
+    for dt in (torch.int64, torch.int32):
+        p = tob.pack_awq_int4(x.to(dt).to(cuda))
+        assert np.array_equal(p.cpu().numpy(), oawq.pack(x.numpy()))
+        assert torch.equal(tob.unpack_awq_int4(p).cpu(), x)
+        assert torch.equal(tob.unpack_awq_int4(p.to(torch.int64)).cpu(), x)
+
+
+@pytest.mark.parametrize("name", ["dequant_f16", "dequant_fullk", "dequant_bf16", "dequant_f32"])
+def test_dequant_golden(cuda, golden, name):
+    c = golden("awq.npz")[name]
+    out = tob.awq_dequantize(c.tensor("qweight", cuda), c.tensor("scales", cuda),
+                             c.tensor("qzeros", cuda))
+    assert out.shape == tuple(c["out"].shape)
+    assert np.array_equal(out.float().cpu().numpy(), c["out"])
+
+
+@pytest.mark.parametrize("name", ["gemm_f16", "gemm_f16_m1", "gemm_f16_m3", "gemm_bf16",
+                                  "gemm_bf16_m1", "gemm_f16_fullk"])
+def test_gemm_golden(cuda, golden, name):
+    c = golden("awq.npz")[name]
+    y = tob.awq_gemm(c.tensor("x", cuda), c.tensor("qweight", cuda), c.tensor("scales", cuda),
+                     c.tensor("qzeros", cuda), 1)
+    assert y.dtype == c.tensor("scales").dtype
+    np.testing.assert_allclose(y.float().cpu().numpy(), c["y"], rtol=RTOL, atol=ATOL)
+
+
+def test_split_k_invariance(cuda, golden):
+    c = golden("awq.npz")["gemm_splitk"]
+    args = [c.tensor(f, cuda) for f in ("x", "qweight", "scales", "qzeros")]
+    y1 = tob.awq_gemm(*args, split_k_iters=1)
+    y4 = tob.awq_gemm(*args, split_k_iters=4)
+    assert torch.equal(y1, y4)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("m,k,n,g", [
+    (1, 4096, 4096, 128),     # decode GEMV (the [1,4096] x [4096,4096] G=128 layer)
+    (1, 4096, 6144, 128),     # qkv
+    (2, 14336, 4096, 128),    # down
+    (4, 4096, 28672, 128),    # gate_up
+    (3, 512, 136, 32),        # ragged column count (17 words)
+    (1, 256, 64, 64),
+    (16, 4096, 4096, 128),
+    (64, 1024, 2048, 128),
+    (5, 96, 64, 96),          # G == K not a multiple of 16
+])
+def test_gemm_vs_oracle(cuda, dtype, m, k, n, g):
+    gen = torch.Generator().manual_seed(m * 131 + k + n)
+    qw, s, qz = make_awq(k, n, g, _DT[dtype], gen)
+    x = torch.randn(m, k, generator=gen).to(_DT[dtype])
+    y = tob.awq_gemm(x.to(cuda), qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    want = oawq.gemm(x.float().numpy(), qw.numpy(), s.float().numpy(), qz.numpy(), dtype)
+    np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+
+
+def test_gemm_deterministic(cuda):
+    gen = torch.Generator().manual_seed(9)
+    qw, s, qz = make_awq(4096, 4096, 128, torch.float16, gen)
+    x = torch.randn(1, 4096, generator=gen).half()
+    args = (x.to(cuda), qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    y0 = tob.awq_gemm(*args)
+    for _ in range(3):
+        assert torch.equal(tob.awq_gemm(*args), y0)

@@ -1,0 +1,235 @@
+"""GPU parity of the quantisation kernels against the golden vectors (the reference's own
+outputs) and the CPU oracle: bit-exact for every quantised code and scale."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import tileops_b200 as tob
+from oracle import fp8 as ofp8
+from oracle import int8 as oi8
+from oracle import sym as osym
+
+pytestmark = pytest.mark.gpu
+
+_DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+def _codes(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.float8_e4m3fn:
+        return t.view(torch.uint8).cpu().numpy()
+    return t.cpu().numpy()
+
+
+def _f(t: torch.Tensor) -> np.ndarray:
+    return t.float().cpu().numpy()
+
+
+# ------------------------------------------------------------------ symmetric INT8
+@pytest.mark.parametrize("name", ["q_known", "q_ties", "roundtrip"])
+def test_quantize_per_tensor_golden(cuda, golden, name):
+    c = golden("sym.npz")[name]
+    q = tob.quantize_per_tensor(c.tensor("x", cuda), c.tensor("s", cuda))
+    assert q.dtype == torch.int8
+    assert np.array_equal(q.cpu().numpy(), c["q"])
+
+
+def test_dequantize_per_tensor_golden(cuda, golden):
+    for name in ("dq_known", "roundtrip"):
+        c = golden("sym.npz")[name]
+        y = tob.dequantize_per_tensor(c.tensor("q", cuda), c.tensor("s", cuda))
+        assert np.array_equal(y.cpu().numpy(), c["y"])
+
+
+@pytest.mark.parametrize("name", ["ch_last", "ch_inner"])
+def test_quantize_per_channel_golden(cuda, golden, name):
+    c = golden("sym.npz")[name]
+    q = tob.quantize_per_channel(c.tensor("x", cuda), c.tensor("s", cuda), dim=int(c["dim"]))
+    assert np.array_equal(q.cpu().numpy(), c["q"])
+
+
+def test_dequantize_per_channel_golden(cuda, golden):
+    c = golden("sym.npz")["dq_ch"]
+    y = tob.dequantize_per_channel(c.tensor("q", cuda), c.tensor("s", cuda), dim=int(c["dim"]))
+    assert np.array_equal(y.cpu().numpy(), c["y"])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("shape,dim", [((1000,), None), ((7, 33, 5), 1), ((64, 129), -1),
+                                       ((3, 4, 1031), 0)])
+def test_symmetric_random_vs_oracle(cuda, dtype, shape, dim):
+    g = torch.Generator().manual_seed(hash((dtype, shape)) & 0xFFFF)
+    x = (torch.randn(*shape, generator=g) * 4).to(_DT[dtype])
+    if dim is None:
+        s = torch.tensor([0.037], dtype=torch.float32)
+        q = tob.quantize_per_tensor(x.to(cuda), s.to(cuda))
+        want = osym.quantize(_f(x), s.numpy())
+        y = tob.dequantize_per_tensor(q, s.to(cuda), out_dtype=_DT[dtype])
+        want_y = osym.dequantize(want, s.numpy(), dtype)
+    else:
+        n = shape[dim]
+        s = torch.rand(n, generator=g) * 0.05 + 0.01
+        q = tob.quantize_per_channel(x.to(cuda), s.to(cuda), dim)
+        want = osym.quantize(_f(x), s.numpy(), dim)
+        y = tob.dequantize_per_channel(q, s.to(cuda), dim, out_dtype=_DT[dtype])
+        want_y = osym.dequantize(want, s.numpy(), dtype, dim)
+    assert np.array_equal(q.cpu().numpy(), want)
+    assert np.array_equal(_f(y), want_y)
+
+
+def test_quantize_out_is_returned(cuda):
+    x = torch.randn(10, device=cuda)
+    s = torch.tensor([0.2], device=cuda)
+    out = torch.empty_like(x, dtype=torch.int8)
+    assert tob.quantize_per_tensor(x, s, out=out) is out
+    assert np.array_equal(out.cpu().numpy(), osym.quantize(_f(x), s.cpu().numpy()))
+    out_nc = torch.empty(20, dtype=torch.int8, device=cuda)[::2]
+    assert tob.quantize_per_tensor(x, s, out=out_nc) is out_nc
+    assert np.array_equal(out_nc.cpu().numpy(), out.cpu().numpy())
+
+
+def test_scale_must_be_positive(cuda):
+    with pytest.raises(ValueError):
+        tob.quantize_per_tensor(torch.randn(4, device=cuda), torch.tensor([0.0], device=cuda))
+
+
+def test_empty_inputs(cuda):
+    s = torch.tensor([0.1], device=cuda)
+    assert tob.quantize_per_tensor(torch.empty(0, device=cuda), s).numel() == 0
+    q, sc = tob.per_token_quant_int8(torch.empty(0, 16, device=cuda))
+    assert q.shape == (0, 16) and sc.shape == (0, 1)
+
+
+# ------------------------------------------------------------------ dynamic INT8
+@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16"])
+def test_input_to_int8_golden(cuda, golden, name):
+    c = golden("int8.npz")[name]
+    q, s = tob.input_to_int8(c.tensor("x", cuda))
+    assert q.dtype == torch.int8
+    assert np.array_equal(q.cpu().numpy(), c["q"])
+    assert s.item() == float(c["s"])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("n", [1, 7, 4096, 1 << 20, (1 << 20) + 13])
+def test_input_to_int8_vs_oracle(cuda, dtype, n):
+    g = torch.Generator().manual_seed(n)
+    x = (torch.randn(n, generator=g) * 3).to(_DT[dtype])
+    q, s = tob.input_to_int8(x.to(cuda))
+    wq, ws = oi8.input_to_int8(_f(x), dtype)
+    assert np.array_equal(q.cpu().numpy(), wq)
+    assert np.float32(s.item()) == ws
+
+
+@pytest.mark.parametrize("name", ["token_2d", "token_nd", "token_bf16", "token_1d", "token_wide"])
+def test_per_token_quant_int8_golden(cuda, golden, name):
+    c = golden("int8.npz")[name]
+    q, s = tob.per_token_quant_int8(c.tensor("x", cuda))
+    assert q.shape == tuple(c["q"].shape) and s.shape == tuple(c["s"].shape)
+    assert np.array_equal(q.cpu().numpy(), c["q"])
+    assert np.array_equal(s.cpu().numpy(), c["s"])
+
+
+@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d"])
+def test_per_token_group_quant_int8_golden(cuda, golden, name):
+    c = golden("int8.npz")[name]
+    q, s = tob.per_token_group_quant_int8(c.tensor("x", cuda), int(c["group_size"]))
+    assert np.array_equal(q.cpu().numpy(), c["q"])
+    assert np.array_equal(s.cpu().numpy(), c["s"])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("rows,k,g", [(1, 8, 8), (37, 24, 8), (64, 128, 128), (3, 4096, 4096),
+                                      (5, 16384, 16384), (2, 65536, 65536), (9, 3000, 1000),
+                                      (256, 4096, 128)])
+def test_group_quant_int8_vs_oracle(cuda, dtype, rows, k, g):
+    gen = torch.Generator().manual_seed(rows * 7 + k)
+    x = (torch.randn(rows, k, generator=gen) * 2).to(_DT[dtype])
+    q, s = tob.per_token_group_quant_int8(x.to(cuda), g)
+    wq, ws = oi8.group_quant(_f(x), g)
+    assert np.array_equal(q.cpu().numpy(), wq)
+    assert np.array_equal(s.cpu().numpy(), ws)
+
+
+# ------------------------------------------------------------------ dynamic FP8
+@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16"])
+def test_input_to_float8_golden(cuda, golden, name):
+    c = golden("fp8.npz")[name]
+    q, s = tob.input_to_float8(c.tensor("x", cuda))
+    assert q.dtype == torch.float8_e4m3fn
+    assert np.array_equal(_codes(q), c["q"])
+    assert s.item() == float(c["s"])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("n", [3, 4099, 1 << 21])
+def test_input_to_float8_vs_oracle(cuda, dtype, n):
+    g = torch.Generator().manual_seed(n + 5)
+    x = (torch.randn(n, generator=g) * 7).to(_DT[dtype])
+    q, s = tob.input_to_float8(x.to(cuda))
+    wq, ws = ofp8.input_to_float8(_f(x), dtype)
+    assert np.array_equal(_codes(q), wq)
+    assert np.float32(s.item()) == ws
+
+
+@pytest.mark.parametrize("name", ["group_f32", "group_ue8m0", "group_bf16_token", "group_f16",
+                                  "group_colmajor", "group_colmajor_3d", "group_ue8m0_bf16",
+                                  "ue8m0_edges"])
+def test_per_token_group_quant_fp8_golden(cuda, golden, name):
+    c = golden("fp8.npz")[name]
+    q, s = tob.per_token_group_quant_fp8(c.tensor("x", cuda), int(c["group_size"]),
+                                         column_major_scales=bool(c["column_major"]),
+                                         use_ue8m0=bool(c["ue8m0"]))
+    assert np.array_equal(_codes(q), c["q"])
+    assert s.shape == tuple(c["s"].shape)
+    assert np.array_equal(s.cpu().numpy(), c["s"])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("rows,k,g,ue8m0", [(3, 32, 8, False), (128, 512, 128, True),
+                                            (64, 8192, 8192, False), (7, 7168, 128, True),
+                                            (33, 1536, 96, False)])
+def test_group_quant_fp8_vs_oracle(cuda, dtype, rows, k, g, ue8m0):
+    gen = torch.Generator().manual_seed(rows + k + g)
+    x = (torch.randn(rows, k, generator=gen) * 5).to(_DT[dtype])
+    q, s = tob.per_token_group_quant_fp8(x.to(cuda), g, use_ue8m0=ue8m0)
+    wq, ws = ofp8.group_quant(_f(x), g, use_ue8m0=ue8m0)
+    assert np.array_equal(_codes(q), wq)
+    assert np.array_equal(s.cpu().numpy(), ws)
+
+
+def test_group_quant_fp8_out_q(cuda):
+    x = torch.randn(4, 64, device=cuda)
+    out = torch.empty(4, 64, dtype=torch.float8_e4m3fn, device=cuda)
+    q, s = tob.per_token_group_quant_fp8(x, 16, out_q=out)
+    assert q is out
+    wq, ws = ofp8.group_quant(_f(x), 16)
+    assert np.array_equal(_codes(out), wq)
+
+
+# ------------------------------------------------------------------ block dequant
+def test_block_dequant_int8_golden(cuda, golden):
+    c = golden("int8.npz")["block_dequant"]
+    y = tob.block_dequant(c.tensor("q", cuda), c.tensor("s", cuda), list(c["block"]))
+    assert np.array_equal(y.cpu().numpy(), c["y"])
+
+
+def test_block_dequant_fp8_golden(cuda, golden):
+    c = golden("fp8.npz")["block_dequant"]
+    y = tob.block_dequant_fp8(c.tensor("q", cuda), c.tensor("s", cuda), list(c["block"]))
+    assert np.array_equal(y.cpu().numpy(), c["y"])
+
+
+@pytest.mark.parametrize("n,k,bn,bk", [(300, 1000, 128, 128), (129, 257, 1, 257), (64, 64, 64, 64)])
+def test_block_dequant_vs_oracle(cuda, n, k, bn, bk):
+    g = torch.Generator().manual_seed(n * k)
+    q = torch.randint(-128, 128, (n, k), generator=g, dtype=torch.int8)
+    s = torch.rand(-(-n // bn), -(-k // bk), generator=g) * 0.1 + 0.001
+    y = tob.block_dequant(q.to(cuda), s.to(cuda), [bn, bk])
+    assert np.array_equal(y.cpu().numpy(), oi8.block_dequant(q.numpy(), s.numpy(), (bn, bk)))
+    qf = (torch.randn(n, k, generator=g) * 3).clamp(-448, 448).to(torch.float8_e4m3fn)
+    y = tob.block_dequant_fp8(qf.to(cuda), s.to(cuda), [bn, bk])
+    want = ofp8.block_dequant(qf.view(torch.uint8).numpy(), s.numpy(), (bn, bk))
+    assert np.array_equal(y.cpu().numpy(), want)

@@ -1,0 +1,145 @@
+"""GPU parity of the W8A8 INT8 and FP8 GEMMs: int32 accumulators bit-exact against the
+exact integer GEMM, outputs within tolerance of the fp32-accumulated oracle, against the
+reference's golden outputs, on the reference tests' ragged block shapes and on the
+per-token x per-channel / per-tensor layouts of the large layers."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import tileops_b200 as tob
+from oracle import fp8 as ofp8
+from oracle import int8 as oi8
+
+pytestmark = pytest.mark.gpu
+
+_DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+def _f(t):
+    return t.float().cpu().numpy()
+
+
+def test_int8_golden_small(cuda, golden):
+    c = golden("int8.npz")["w8a8_small"]
+    y = tob.w8a8_block_int8_matmul(c.tensor("a", cuda), c.tensor("b", cuda), c.tensor("a_s", cuda),
+                                   c.tensor("b_s", cuda), list(c["block"]),
+                                   output_dtype=torch.float32)
+    np.testing.assert_allclose(_f(y), c["c"], rtol=1e-4, atol=1e-4)
+
+
+def test_int8_golden_channel(cuda, golden):
+    c = golden("int8.npz")["w8a8_channel"]
+    a, b = c.tensor("a", cuda), c.tensor("b", cuda)
+    y = tob.w8a8_block_int8_matmul(a, b, c.tensor("a_s", cuda), c.tensor("b_s", cuda),
+                                   list(c["block"]), output_dtype=torch.bfloat16)
+    assert y.dtype == torch.bfloat16
+    np.testing.assert_allclose(_f(y), c["c"], rtol=1e-2, atol=1e-2)
+    acc = tob.w8a8_int8_accumulators(a, b)
+    assert np.array_equal(acc.cpu().numpy().astype(np.int64), c["acc"])
+
+
+def test_int8_apply_linear_golden(cuda, golden):
+    c = golden("int8.npz")["apply_linear"]
+    y = tob.apply_w8a8_block_int8_linear(c.tensor("x", cuda), c.tensor("w", cuda),
+                                         list(c["block"]), c.tensor("w_s", cuda),
+                                         bias=c.tensor("bias", cuda))
+    assert y.dtype == torch.float16
+    np.testing.assert_allclose(_f(y), c["y"], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 11008, 4096), (1, 64, 4096), (200, 1000, 512),
+                                   (128, 256, 128), (300, 384, 1024), (17, 4097, 96)])
+def test_int8_accumulators_bit_exact(cuda, m, n, k):
+    g = torch.Generator().manual_seed(m + n + k)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    acc = tob.w8a8_int8_accumulators(a.to(cuda), b.to(cuda))
+    want = oi8.accumulators(a.numpy(), b.numpy())
+    assert np.array_equal(acc.cpu().numpy().astype(np.int64), want)
+
+
+@pytest.mark.parametrize("out", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("m,n,k", [(256, 11008, 4096), (64, 512, 4096), (300, 384, 1024),
+                                   (7, 100, 256)])
+def test_int8_per_channel_vs_oracle(cuda, out, m, n, k):
+    g = torch.Generator().manual_seed(m * n + k)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand(m, 1, generator=g) * 0.045 + 0.005
+    b_s = torch.rand(n, 1, generator=g) * 0.009 + 0.001
+    y = tob.w8a8_block_int8_matmul(a.to(cuda), b.to(cuda), a_s.to(cuda), b_s.to(cuda), [1, k],
+                                   output_dtype=_DT[out])
+    want = oi8.block_matmul(a.numpy(), b.numpy(), a_s.numpy(), b_s.numpy(), (1, k), out)
+    tol = 1e-4 if out == "f32" else 1e-2
+    np.testing.assert_allclose(_f(y), want, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("m,n,k,bn,bk", [(6, 10, 24, 4, 8), (33, 260, 512, 128, 128),
+                                         (128, 256, 384, 128, 128)])
+def test_int8_block_scaled_vs_oracle(cuda, m, n, k, bn, bk):
+    g = torch.Generator().manual_seed(m + 3 * n + k)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    kt = -(-k // bk)
+    a_s = torch.rand(m, kt, generator=g) * 0.05 + 0.001
+    b_s = torch.rand(-(-n // bn), kt, generator=g) * 0.05 + 0.001
+    y = tob.w8a8_block_int8_matmul(a.to(cuda), b.to(cuda), a_s.to(cuda), b_s.to(cuda), [bn, bk],
+                                   output_dtype=torch.float32)
+    want = oi8.block_matmul(a.numpy(), b.numpy(), a_s.numpy(), b_s.numpy(), (bn, bk), "f32")
+    np.testing.assert_allclose(_f(y), want, rtol=1e-4, atol=1e-4)
+
+
+def test_fp8_golden_small(cuda, golden):
+    c = golden("fp8.npz")["w8a8_small"]
+    args = [c.tensor(f, cuda) for f in ("a", "b", "a_s", "b_s")]
+    y = tob.w8a8_block_fp8_matmul(*args, list(c["block"]), output_dtype=torch.float32)
+    y2 = tob.w8a8_triton_block_scaled_mm(*args, list(c["block"]), output_dtype=torch.float32)
+    assert torch.equal(y, y2)
+    np.testing.assert_allclose(_f(y), c["c"], rtol=1e-4, atol=1e-4)
+
+
+def test_fp8_apply_linear_golden(cuda, golden):
+    c = golden("fp8.npz")["apply_linear"]
+    y = tob.apply_w8a8_block_fp8_linear(c.tensor("x", cuda), c.tensor("w", cuda),
+                                        list(c["block"]), c.tensor("w_s", cuda),
+                                        bias=c.tensor("bias", cuda))
+    np.testing.assert_allclose(_f(y), c["y"], rtol=1e-3, atol=1e-3)
+
+
+def test_fp8_layer_golden(cuda, golden):
+    """Dynamic per-token quant of A, per-tensor quant of B, per-token x per-tensor GEMM."""
+    c = golden("fp8.npz")["fp8_layer"]
+    A, B = c.tensor("A", cuda), c.tensor("B", cuda)
+    qa, sa = tob.per_token_group_quant_fp8(A, A.shape[1])
+    qb, sb = tob.input_to_float8(B)
+    assert np.array_equal(qa.view(torch.uint8).cpu().numpy(), c["qa"])
+    assert np.array_equal(qb.view(torch.uint8).cpu().numpy(), c["qb"])
+    y = tob.w8a8_block_fp8_matmul(qa, qb, sa, sb.reshape(1, 1), [B.shape[0], A.shape[1]],
+                                  output_dtype=torch.bfloat16)
+    np.testing.assert_allclose(_f(y), c["c"], rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("m,n,k", [(8192, 8192, 8192), (256, 512, 1024), (130, 200, 4096),
+                                   (1, 128, 256)])
+def test_fp8_per_token_per_tensor_vs_oracle(cuda, m, n, k):
+    g = torch.Generator().manual_seed(m + n + k + 1)
+    A = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    B = torch.randn(n, k, generator=g).to(torch.bfloat16)
+    qa, sa = tob.per_token_group_quant_fp8(A.to(cuda), k)
+    qb, sb = tob.input_to_float8(B.to(cuda))
+    y = tob.w8a8_block_fp8_matmul(qa, qb, sa, sb.reshape(1, 1), [n, k], output_dtype=torch.bfloat16)
+    if m * n * k > 2 ** 33:
+        # Full-size check: a seeded sample of rows against the oracle.
+        rows = torch.randperm(m, generator=g)[:64].sort().values
+        want = ofp8.block_matmul(qa[rows].view(torch.uint8).cpu().numpy(),
+                                 qb.view(torch.uint8).cpu().numpy(), sa[rows].cpu().numpy(),
+                                 sb.reshape(1, 1).cpu().numpy(), (n, k), "bf16")
+        got = _f(y[rows.to(cuda)])
+    else:
+        want = ofp8.block_matmul(qa.view(torch.uint8).cpu().numpy(), qb.view(torch.uint8).cpu().numpy(),
+                                 sa.cpu().numpy(), sb.reshape(1, 1).cpu().numpy(), (n, k), "bf16")
+        got = _f(y)
+    np.testing.assert_allclose(got, want, rtol=1e-2, atol=1e-2)

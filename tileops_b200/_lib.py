@@ -1,0 +1,159 @@
+"""ctypes boundary to libtileops_b200.so (the C ABI declared in include/tileops_b200.h).
+
+This replaces the reference's plugin layer (tileops/runtime/_infra.py:161 BACKEND_PACKAGES,
+:492 dispatch_compile_quant and the invoke_* wrappers in tileops/runtime/__init__.py:446-641):
+instead of JIT-compiling TileLang kernels per target, every op calls one precompiled sm_100a
+entry point with raw device pointers, sizes and the current torch stream. There is no other
+backend and no CPU path: a missing library or a non-CUDA tensor is an error.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).with_name("libtileops_b200.so")
+
+TO_OK = 0
+TO_EINVAL = -1
+TO_EUNSUPPORTED = -2
+TO_ECUDA = -3
+TO_ETIMEOUT = -4
+TO_ENOSPACE = -5
+
+DTYPE_CODES = {
+    torch.float32: 0,
+    torch.float16: 1,
+    torch.bfloat16: 2,
+    torch.int8: 3,
+    torch.float8_e4m3fn: 4,
+    torch.int32: 5,
+    torch.int64: 6,
+}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_F = ctypes.c_float
+_S = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/tileops_b200.h one for one.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "to_version": (ctypes.c_char_p, []),
+    "to_last_error_string": (ctypes.c_char_p, []),
+    "to_device_check": (_I, [_I]),
+    "to_device_error_word": (_I, [ctypes.POINTER(_I), _I]),
+    "to_quant_per_tensor_i8": (_I, [_P, _I, _P, _P, _L, _P]),
+    "to_dequant_per_tensor_i8": (_I, [_P, _P, _P, _I, _L, _P]),
+    "to_quant_per_channel_i8": (_I, [_P, _I, _P, _P, _L, _L, _L, _P]),
+    "to_dequant_per_channel_i8": (_I, [_P, _P, _P, _I, _L, _L, _L, _P]),
+    "to_input_quant_workspace_size": (_S, []),
+    "to_input_to_int8": (_I, [_P, _I, _L, _P, _P, _P, _S, _P]),
+    "to_input_to_fp8": (_I, [_P, _I, _L, _P, _P, _P, _S, _P]),
+    "to_per_token_group_quant_i8": (_I, [_P, _I, _L, _L, _F, _P, _P, _P]),
+    "to_per_token_group_quant_fp8": (_I, [_P, _I, _L, _L, _F, _I, _L, _L, _P, _P, _P]),
+    "to_block_dequant_i8": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),
+    "to_block_dequant_fp8": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),
+    "to_awq_pack": (_I, [_P, _I, _P, _L, _L, _P]),
+    "to_awq_unpack": (_I, [_P, _I, _P, _L, _L, _P]),
+    "to_awq_dequant": (_I, [_P, _P, _I, _P, _P, _L, _L, _L, _P]),
+    "to_awq_gemm_workspace_size": (_S, [_L, _L, _L, _L]),
+    "to_awq_gemm": (_I, [_P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _P, _S, _P]),
+    "to_w8a8_i8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _L, _P]),
+    "to_w8a8_fp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _L, _L, _L, _L, _L, _P]),
+}
+
+_lib: ctypes.CDLL | None = None
+_lock = threading.Lock()
+_checked_devices: set[int] = set()
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once per process and declares every entry point's signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH.name} is not built; run `python -m tileops_b200.build` "
+                    "(tileops_b200 has no CPU or fallback path)"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().to_last_error_string()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, op: str) -> None:
+    """Maps a TO_E* status to the exception type the reference raises for that failure."""
+    if rc == TO_OK:
+        return
+    msg = last_error() or f"{op} failed with status {rc}"
+    if rc == TO_EINVAL:
+        raise ValueError(msg)
+    if rc == TO_EUNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)
+
+
+def ensure_device(t: torch.Tensor, op: str) -> int:
+    """Requires a CUDA tensor on an sm_100 device and makes that device current."""
+    if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+        dev = t.device if isinstance(t, torch.Tensor) else type(t).__name__
+        raise TypeError(f"{op}: tileops_b200 runs on CUDA tensors only (got {dev})")
+    idx = t.device.index if t.device.index is not None else torch.cuda.current_device()
+    if idx not in _checked_devices:
+        check(load().to_device_check(idx), op)
+        _checked_devices.add(idx)
+    if torch.cuda.current_device() != idx:
+        torch.cuda.set_device(idx)
+    return idx
+
+
+def same_device(op: str, ref: torch.Tensor, *others: torch.Tensor | None) -> None:
+    for o in others:
+        if o is not None and o.device != ref.device:
+            raise TypeError(f"{op}: all tensors must be on {ref.device} (got {o.device})")
+
+
+def stream_ptr(device: int | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def dtype_code(dt: torch.dtype, op: str) -> int:
+    try:
+        return DTYPE_CODES[dt]
+    except KeyError:
+        raise TypeError(f"{op}: unsupported dtype {dt}") from None
+
+
+def device_error_word(clear: bool = True) -> int:
+    """Reads the device error word set by kernels whose bounded waits expired (0 = none)."""
+    v = ctypes.c_int(0)
+    check(load().to_device_error_word(ctypes.byref(v), 1 if clear else 0), "device_error_word")
+    return v.value
+
+
+def version() -> str:
+    return load().to_version().decode()

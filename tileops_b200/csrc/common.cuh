@@ -1,0 +1,136 @@
+// Shared host/device helpers for libtileops_b200: status handling, dtype dispatch,
+// exact conversions and vector memory access. sm_100a only.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/tileops_b200.h"
+
+namespace tob {
+
+// ---------------------------------------------------------------- host error plumbing
+// Records a formatted message for to_last_error_string() and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Converts a CUDA runtime error into TO_ECUDA with context.
+int cuda_fail(cudaError_t e, const char* what);
+// Checks the launch that just happened on this thread.
+inline int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TO_OK : cuda_fail(e, what);
+}
+// Number of SMs of the current device (cached per device).
+int sm_count();
+// Device address of the library's error word on the current device (nullptr on failure).
+int* device_error_ptr();
+// Codes kernels write into the error word.
+enum DeviceError : int { kErrNone = 0, kErrWaitTimeout = 1, kErrTmemAlloc = 2 };
+
+inline const char* dtype_name(int dt) {
+  switch (dt) {
+    case TO_F32: return "float32";
+    case TO_F16: return "float16";
+    case TO_BF16: return "bfloat16";
+    case TO_I8: return "int8";
+    case TO_E4M3: return "float8_e4m3fn";
+    case TO_I32: return "int32";
+    case TO_I64: return "int64";
+  }
+  return "unknown";
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline unsigned grid_for(int64_t work_items, int threads, int per_sm = 8) {
+  int64_t blocks = ceil_div(work_items, threads);
+  int64_t cap = (int64_t)sm_count() * per_sm;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (unsigned)blocks;
+}
+
+// Dispatches a runtime float dtype code to a C++ type alias `T`.
+#define TOB_DISPATCH_FLOAT(code, T, ...)                                              \
+  switch (code) {                                                                     \
+    case TO_F32: { using T = float; __VA_ARGS__; } break;                             \
+    case TO_F16: { using T = __half; __VA_ARGS__; } break;                            \
+    case TO_BF16: { using T = __nv_bfloat16; __VA_ARGS__; } break;                    \
+    default:                                                                          \
+      return ::tob::fail(TO_EUNSUPPORTED, "unsupported floating dtype %s",            \
+                         ::tob::dtype_name(code));                                    \
+  }
+
+// ---------------------------------------------------------------- device conversions
+// All conversions round to nearest even, the rounding torch's CPU kernels use.
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Round an fp32 value to the storage type T and back (the value torch holds after a
+// reduced-precision op).
+template <typename T> __device__ __forceinline__ float round_to(float v) {
+  return to_f32<T>(from_f32<T>(v));
+}
+
+// fp32 -> e4m3fn, round to nearest even, saturating to +-448 (cvt.rn.satfinite).
+__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
+  return (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+}
+// Two values at once: low byte = a, high byte = b.
+__device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float a, float b) {
+  return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ float e4m3_to_f32(uint8_t v) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)v, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Round-half-even then clamp to int8, as torch.clamp(torch.round(v), -128, 127).
+__device__ __forceinline__ int8_t rne_clamp_i8(float v) {
+  float r = rintf(v);
+  r = fminf(fmaxf(r, -128.f), 127.f);
+  return (int8_t)(int)r;
+}
+
+// ---------------------------------------------------------------- vector memory access
+template <int BYTES> struct VecT;
+template <> struct VecT<4> { using type = uint32_t; };
+template <> struct VecT<8> { using type = uint2; };
+template <> struct VecT<16> { using type = uint4; };
+
+// Streaming 16-byte global load that does not allocate in L1.
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+template <typename T, int N> struct alignas(sizeof(T) * N) Pack {
+  T v[N];
+};
+
+// Warp-level max reduction across the low `width` lanes groups (width power of two <= 32).
+__device__ __forceinline__ float warp_max(float v, int width) {
+  for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace tob

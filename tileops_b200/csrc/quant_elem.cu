@@ -1,0 +1,495 @@
+// Elementwise and row-wise quantisation kernels (HBM-bound streams):
+//   symmetric INT8 per-tensor / per-channel quantise + dequantise   (tileops/quant.py)
+//   per-token(-group) dynamic INT8 and FP8 e4m3 quantise            (quant_int8.py, quant_fp8.py)
+//   tensor-wide dynamic INT8 / FP8 quantise (amax pass + quantise)  (quant_int8.py:29, quant_fp8.py:52)
+//   block dequantisation of INT8 / FP8 weights                      (quant_int8.py:136, quant_fp8.py:143)
+// Every kernel reads its input once with 16-byte vector loads and a grid sized to the SM
+// count; all float arithmetic is IEEE round-to-nearest-even so results match the
+// reference's torch expressions bit for bit.
+#include "common.cuh"
+
+namespace tob {
+namespace {
+
+constexpr int kThreads = 256;
+
+inline bool aligned_to(const void* p, size_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
+}
+
+template <typename T, int V>
+__device__ __forceinline__ Pack<T, V> ld_pack(const T* p) {
+  return *reinterpret_cast<const Pack<T, V>*>(p);
+}
+template <typename T, int V>
+__device__ __forceinline__ void st_pack(T* p, const Pack<T, V>& v) {
+  *reinterpret_cast<Pack<T, V>*>(p) = v;
+}
+
+// Splits a flat index of a [outer, channels, inner] tensor into (channel, position in inner).
+struct ChannelCursor {
+  int64_t c, r;
+  __device__ __forceinline__ ChannelCursor(int64_t idx, int64_t channels, int64_t inner) {
+    int64_t t = idx / inner;
+    r = idx - t * inner;
+    c = t % channels;
+  }
+  __device__ __forceinline__ void next(int64_t channels, int64_t inner) {
+    if (++r == inner) {
+      r = 0;
+      if (++c == channels) c = 0;
+    }
+  }
+};
+
+// ------------------------------------------------------------------ symmetric INT8
+// q = clamp(rint(float(x) / s), -128, 127). Per-tensor when channels == 1.
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) k_quant_sym(const T* __restrict__ x,
+                                                       const float* __restrict__ scale,
+                                                       int8_t* __restrict__ q, int64_t n,
+                                                       int64_t channels, int64_t inner) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nvec = n / V;
+  const float s0 = __ldg(scale);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    Pack<T, V> v = ld_pack<T, V>(x + i * V);
+    Pack<int8_t, V> o;
+    if (channels == 1) {
+#pragma unroll
+      for (int j = 0; j < V; ++j) o.v[j] = rne_clamp_i8(__fdiv_rn(to_f32(v.v[j]), s0));
+    } else {
+      ChannelCursor cur(i * V, channels, inner);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        o.v[j] = rne_clamp_i8(__fdiv_rn(to_f32(v.v[j]), __ldg(scale + cur.c)));
+        cur.next(channels, inner);
+      }
+    }
+    st_pack<int8_t, V>(q + i * V, o);
+  }
+  for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float s = channels == 1 ? s0 : __ldg(scale + (i / inner) % channels);
+    q[i] = rne_clamp_i8(__fdiv_rn(to_f32(x[i]), s));
+  }
+}
+
+// y = T(float(q) * s).
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) k_dequant_sym(const int8_t* __restrict__ q,
+                                                         const float* __restrict__ scale,
+                                                         T* __restrict__ y, int64_t n,
+                                                         int64_t channels, int64_t inner) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nvec = n / V;
+  const float s0 = __ldg(scale);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    Pack<int8_t, V> v = ld_pack<int8_t, V>(q + i * V);
+    Pack<T, V> o;
+    if (channels == 1) {
+#pragma unroll
+      for (int j = 0; j < V; ++j) o.v[j] = from_f32<T>(__fmul_rn((float)v.v[j], s0));
+    } else {
+      ChannelCursor cur(i * V, channels, inner);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        o.v[j] = from_f32<T>(__fmul_rn((float)v.v[j], __ldg(scale + cur.c)));
+        cur.next(channels, inner);
+      }
+    }
+    st_pack<T, V>(y + i * V, o);
+  }
+  for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float s = channels == 1 ? s0 : __ldg(scale + (i / inner) % channels);
+    y[i] = from_f32<T>(__fmul_rn((float)q[i], s));
+  }
+}
+
+template <typename T>
+int launch_quant_sym(const void* x, const float* scale, int8_t* q, int64_t n, int64_t channels,
+                     int64_t inner, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  unsigned grid = grid_for(ceil_div(n, V), kThreads);
+  if (aligned16(x) && aligned_to(q, V))
+    k_quant_sym<T, V><<<grid, kThreads, 0, st>>>((const T*)x, scale, q, n, channels, inner);
+  else
+    k_quant_sym<T, 1><<<grid, kThreads, 0, st>>>((const T*)x, scale, q, n, channels, inner);
+  return check_launch("quantize int8 (symmetric)");
+}
+
+template <typename T>
+int launch_dequant_sym(const int8_t* q, const float* scale, void* y, int64_t n, int64_t channels,
+                       int64_t inner, cudaStream_t st) {
+  constexpr int V = 8;
+  unsigned grid = grid_for(ceil_div(n, V), kThreads);
+  if (aligned_to(q, V) && aligned_to(y, V * sizeof(T)))
+    k_dequant_sym<T, V><<<grid, kThreads, 0, st>>>(q, scale, (T*)y, n, channels, inner);
+  else
+    k_dequant_sym<T, 1><<<grid, kThreads, 0, st>>>(q, scale, (T*)y, n, channels, inner);
+  return check_launch("dequantize int8 (symmetric)");
+}
+
+// ------------------------------------------------------------------ per-token-group quant
+// One "team" of 2^team_log2 threads per group of G contiguous elements. Each thread keeps up
+// to MAXV vectors of its slice in registers, so x is read from HBM exactly once; groups too
+// large for the register cache re-read the tail (served from L2).
+struct ScaleLayout {
+  int64_t cm_rows;    // > 0: the reference's column_major_scales layout (see scale_offset)
+  int64_t cm_groups;  // groups per row
+};
+
+// Position of group g's scale. Natural order is g. With column_major_scales the reference
+// returns s_flat.reshape(..., G_, M).transpose(-2, -1).contiguous() (quant_fp8.py:129-136):
+// within each batch of M rows x G_ groups, flat scale t lands at row t % M, column t / M of
+// a contiguous [M, G_] tensor.
+__device__ __forceinline__ int64_t scale_offset(int64_t g, const ScaleLayout& sl) {
+  if (sl.cm_rows <= 0) return g;
+  const int64_t per_batch = sl.cm_rows * sl.cm_groups;
+  const int64_t b = g / per_batch;
+  const int64_t t = g - b * per_batch;
+  return b * per_batch + (t % sl.cm_rows) * sl.cm_groups + t / sl.cm_rows;
+}
+
+// 2^ceil(log2(max(s, 1e-30))) with log2 rounded to fp32 first, as torch evaluates
+// torch.exp2(torch.ceil(torch.log2(s))) (quant_fp8.py:48-49).
+__device__ __forceinline__ float ue8m0_round(float s) {
+  s = fmaxf(s, 1e-30f);
+  const float l = (float)log2((double)s);
+  return ldexpf(1.0f, (int)ceilf(l));
+}
+
+template <typename T, bool FP8, int V, int MAXV>
+__global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
+                                                     uint8_t* __restrict__ qout,
+                                                     float* __restrict__ scales, int64_t n_groups,
+                                                     int G, int team_log2, float eps, int ue8m0,
+                                                     ScaleLayout sl) {
+  const int team = 1 << team_log2;
+  const int lane = threadIdx.x & (team - 1);
+  const int teams_per_cta = blockDim.x >> team_log2;
+  const int team_id = threadIdx.x >> team_log2;
+  const int nvec = G / V;
+  __shared__ float red[32];
+  const float qmax = FP8 ? 448.0f : 127.0f;
+
+  for (int64_t g0 = (int64_t)blockIdx.x * teams_per_cta; g0 < n_groups;
+       g0 += (int64_t)gridDim.x * teams_per_cta) {
+    const int64_t g = g0 + team_id;
+    const bool active = g < n_groups;
+    const T* xg = x + g * (int64_t)G;
+    Pack<T, V> cache[MAXV];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int v = lane + i * team;
+      if (active && v < nvec) {
+        cache[i] = ld_pack<T, V>(xg + (int64_t)v * V);
+#pragma unroll
+        for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(to_f32(cache[i].v[j])));
+      }
+    }
+    for (int v = lane + MAXV * team; active && v < nvec; v += team) {
+      Pack<T, V> t = ld_pack<T, V>(xg + (int64_t)v * V);
+#pragma unroll
+      for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(to_f32(t.v[j])));
+    }
+    if (team <= 32) {
+      amax = warp_max(amax, team);
+    } else {
+      amax = warp_max(amax, 32);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+      __syncthreads();
+      float m = 0.f;
+      for (int w = 0; w < (team >> 5); ++w) m = fmaxf(m, red[w]);
+      amax = m;
+      __syncthreads();
+    }
+    // scale = clamp(absmax, min=eps) / qmax  (fp32, IEEE division)
+    float scale = __fdiv_rn(fmaxf(amax, eps), qmax);
+    if (FP8 && ue8m0) scale = ue8m0_round(scale);
+    if (active && lane == 0) scales[scale_offset(g, sl)] = scale;
+
+    uint8_t* qg = qout + g * (int64_t)G;
+    auto emit = [&](int v, const Pack<T, V>& t) {
+      Pack<uint8_t, V> o;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const float y = __fdiv_rn(to_f32(t.v[j]), scale);
+        if (FP8) {
+          o.v[j] = f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
+        } else {
+          o.v[j] = (uint8_t)rne_clamp_i8(y);
+        }
+      }
+      st_pack<uint8_t, V>(qg + (int64_t)v * V, o);
+    };
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int v = lane + i * team;
+      if (active && v < nvec) emit(v, cache[i]);
+    }
+    for (int v = lane + MAXV * team; active && v < nvec; v += team)
+      emit(v, ld_pack<T, V>(xg + (int64_t)v * V));
+  }
+}
+
+template <typename T, bool FP8>
+int launch_group_quant(const void* x, int64_t n_groups, int64_t G, float eps, int ue8m0,
+                       ScaleLayout sl, void* q, float* scales, cudaStream_t st) {
+  constexpr int VV = 16 / sizeof(T);
+  const bool vec = (G % VV == 0) && aligned16(x) && aligned_to(q, VV);
+  const int V = vec ? VV : 1;
+  const int64_t nvec = G / V;
+  const int maxv = vec ? 4 : 8;
+  int64_t want = ceil_div(nvec, maxv);
+  int team_log2 = 0;
+  while ((1 << team_log2) < want && team_log2 < 10) ++team_log2;
+  const int team = 1 << team_log2;
+  const int threads = team > kThreads ? team : kThreads;
+  const int64_t teams_per_cta = threads / team;
+  int64_t blocks = ceil_div(n_groups, teams_per_cta);
+  const int64_t cap = (int64_t)sm_count() * 64;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  if (vec)
+    k_group_quant<T, FP8, VV, 4><<<(unsigned)blocks, threads, 0, st>>>(
+        (const T*)x, (uint8_t*)q, scales, n_groups, (int)G, team_log2, eps, ue8m0, sl);
+  else
+    k_group_quant<T, FP8, 1, 8><<<(unsigned)blocks, threads, 0, st>>>(
+        (const T*)x, (uint8_t*)q, scales, n_groups, (int)G, team_log2, eps, ue8m0, sl);
+  return check_launch(FP8 ? "per_token_group_quant_fp8" : "per_token_group_quant_int8");
+}
+
+// ------------------------------------------------------------------ tensor-wide dynamic quant
+// Pass 1: amax = max |x| folded into one word with atomicMax on the float's bit pattern
+// (non-negative floats order like their unsigned bit patterns).
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) k_absmax(const T* __restrict__ x, int64_t n,
+                                                    unsigned* __restrict__ amax_bits) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nvec = n / V;
+  float m = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    Pack<T, V> v = ld_pack<T, V>(x + i * V);
+#pragma unroll
+    for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f32(v.v[j])));
+  }
+  for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    m = fmaxf(m, fabsf(to_f32(x[i])));
+  m = warp_max(m, 32);
+  __shared__ float red[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) b = fmaxf(b, red[w]);
+    atomicMax(amax_bits, __float_as_uint(b));
+  }
+}
+
+// Pass 2, in the input dtype T exactly as the reference's expression evaluates:
+//   amax = T(max(amax, 1e-12)); s = T(T(1/amax) * qmax); q = cast(clamp(T(x*s), qmin, qmax)).
+// The int8 cast truncates toward zero (torch .to(int8)); the fp8 cast rounds to nearest even.
+template <typename T, bool FP8, int V>
+__global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__ x, int64_t n,
+                                                          const unsigned* __restrict__ amax_bits,
+                                                          uint8_t* __restrict__ q,
+                                                          float* __restrict__ dq_scale) {
+  const float qmax = FP8 ? 448.0f : 127.0f;
+  const float qmin = FP8 ? -448.0f : -128.0f;
+  const float amax = round_to<T>(fmaxf(__uint_as_float(*amax_bits), 1e-12f));
+  const float r = round_to<T>(__frcp_rn(amax));
+  const float s = round_to<T>(__fmul_rn(r, qmax));
+  if (blockIdx.x == 0 && threadIdx.x == 0) *dq_scale = __frcp_rn(s);
+  auto quant1 = [&](float xv) -> uint8_t {
+    float y = round_to<T>(__fmul_rn(xv, s));
+    y = fminf(fmaxf(y, qmin), qmax);
+    if (FP8) return f32_to_e4m3(y);
+    return (uint8_t)(int8_t)(int)y;  // truncation toward zero
+  };
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nvec = n / V;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    Pack<T, V> v = ld_pack<T, V>(x + i * V);
+    Pack<uint8_t, V> o;
+#pragma unroll
+    for (int j = 0; j < V; ++j) o.v[j] = quant1(to_f32(v.v[j]));
+    st_pack<uint8_t, V>(q + i * V, o);
+  }
+  for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    q[i] = quant1(to_f32(x[i]));
+}
+
+template <typename T, bool FP8>
+int launch_tensor_quant(const void* x, int64_t n, void* q, float* dq_scale, unsigned* ws,
+                        cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(unsigned), st);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-wide quant: clear amax word");
+  unsigned grid = grid_for(ceil_div(n, V), kThreads, 4);
+  const bool vec = aligned16(x) && aligned_to(q, V);
+  if (vec)
+    k_absmax<T, V><<<grid, kThreads, 0, st>>>((const T*)x, n, ws);
+  else
+    k_absmax<T, 1><<<grid, kThreads, 0, st>>>((const T*)x, n, ws);
+  int rc = check_launch("tensor-wide quant: amax");
+  if (rc) return rc;
+  grid = grid_for(ceil_div(n, V), kThreads, 8);
+  if (vec)
+    k_tensor_quant<T, FP8, V><<<grid, kThreads, 0, st>>>((const T*)x, n, ws, (uint8_t*)q, dq_scale);
+  else
+    k_tensor_quant<T, FP8, 1><<<grid, kThreads, 0, st>>>((const T*)x, n, ws, (uint8_t*)q, dq_scale);
+  return check_launch("tensor-wide quant: quantize");
+}
+
+// ------------------------------------------------------------------ block dequant
+template <bool FP8>
+__global__ void __launch_bounds__(kThreads) k_block_dequant(const uint8_t* __restrict__ q,
+                                                           const float* __restrict__ s,
+                                                           float* __restrict__ y, int64_t n,
+                                                           int64_t k, int64_t bn, int64_t bk,
+                                                           int64_t k_tiles) {
+  const int64_t total = n * k;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / k;
+    const int64_t c = i - r * k;
+    const uint8_t v = q[i];
+    const float f = FP8 ? e4m3_to_f32(v) : (float)(int8_t)v;
+    y[i] = __fmul_rn(f, __ldg(s + (r / bn) * k_tiles + c / bk));
+  }
+}
+
+int launch_block_dequant(bool fp8, const void* q, const float* s, float* y, int64_t n, int64_t k,
+                         int64_t bn, int64_t bk, cudaStream_t st) {
+  if (n < 0 || k < 0 || bn <= 0 || bk <= 0)
+    return fail(TO_EINVAL, "block_dequant: invalid sizes n=%lld k=%lld block=[%lld,%lld]",
+                (long long)n, (long long)k, (long long)bn, (long long)bk);
+  if (n == 0 || k == 0) return TO_OK;
+  const int64_t kt = ceil_div(k, bk);
+  unsigned grid = grid_for(n * k, kThreads, 8);
+  if (fp8)
+    k_block_dequant<true><<<grid, kThreads, 0, st>>>((const uint8_t*)q, s, y, n, k, bn, bk, kt);
+  else
+    k_block_dequant<false><<<grid, kThreads, 0, st>>>((const uint8_t*)q, s, y, n, k, bn, bk, kt);
+  return check_launch("block_dequant");
+}
+
+}  // namespace
+}  // namespace tob
+
+using namespace tob;
+
+extern "C" {
+
+int to_quant_per_tensor_i8(const void* x, int x_dtype, const float* scale, int8_t* q, int64_t n,
+                           void* stream) {
+  if (n < 0) return fail(TO_EINVAL, "quantize_per_tensor: negative size");
+  if (n == 0) return TO_OK;
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_quant_sym<T>(x, scale, q, n, 1, 1, (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_dequant_per_tensor_i8(const int8_t* q, const float* scale, void* y, int y_dtype, int64_t n,
+                             void* stream) {
+  if (n < 0) return fail(TO_EINVAL, "dequantize_per_tensor: negative size");
+  if (n == 0) return TO_OK;
+  TOB_DISPATCH_FLOAT(y_dtype, T,
+                     return launch_dequant_sym<T>(q, scale, y, n, 1, 1, (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_quant_per_channel_i8(const void* x, int x_dtype, const float* scale, int8_t* q,
+                            int64_t outer, int64_t channels, int64_t inner, void* stream) {
+  if (outer < 0 || channels <= 0 || inner < 0)
+    return fail(TO_EINVAL, "quantize_per_channel: invalid view [%lld,%lld,%lld]",
+                (long long)outer, (long long)channels, (long long)inner);
+  const int64_t n = outer * channels * inner;
+  if (n == 0) return TO_OK;
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_quant_sym<T>(x, scale, q, n, channels, inner,
+                                                (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_dequant_per_channel_i8(const int8_t* q, const float* scale, void* y, int y_dtype,
+                              int64_t outer, int64_t channels, int64_t inner, void* stream) {
+  if (outer < 0 || channels <= 0 || inner < 0)
+    return fail(TO_EINVAL, "dequantize_per_channel: invalid view [%lld,%lld,%lld]",
+                (long long)outer, (long long)channels, (long long)inner);
+  const int64_t n = outer * channels * inner;
+  if (n == 0) return TO_OK;
+  TOB_DISPATCH_FLOAT(y_dtype, T,
+                     return launch_dequant_sym<T>(q, scale, y, n, channels, inner,
+                                                  (cudaStream_t)stream));
+  return TO_OK;
+}
+
+size_t to_input_quant_workspace_size(void) { return 256; }
+
+int to_input_to_int8(const void* x, int x_dtype, int64_t n, int8_t* q, float* dq_scale,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (n <= 0) return fail(TO_EINVAL, "input_to_int8: empty input");
+  if (!workspace || workspace_bytes < sizeof(unsigned))
+    return fail(TO_ENOSPACE, "input_to_int8: workspace of %zu bytes is too small",
+                workspace_bytes);
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_tensor_quant<T, false>(x, n, q, dq_scale, (unsigned*)workspace,
+                                                          (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_input_to_fp8(const void* x, int x_dtype, int64_t n, void* q, float* dq_scale,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (n <= 0) return fail(TO_EINVAL, "input_to_float8: empty input");
+  if (!workspace || workspace_bytes < sizeof(unsigned))
+    return fail(TO_ENOSPACE, "input_to_float8: workspace of %zu bytes is too small",
+                workspace_bytes);
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_tensor_quant<T, true>(x, n, q, dq_scale, (unsigned*)workspace,
+                                                         (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_per_token_group_quant_i8(const void* x, int x_dtype, int64_t n_groups, int64_t group_size,
+                                float eps, int8_t* q, float* scales, void* stream) {
+  if (n_groups < 0 || group_size <= 0 || group_size > (int64_t)1 << 30)
+    return fail(TO_EINVAL, "per_token_group_quant_int8: invalid groups=%lld size=%lld",
+                (long long)n_groups, (long long)group_size);
+  if (n_groups == 0) return TO_OK;
+  ScaleLayout sl{0, 1};
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_group_quant<T, false>(x, n_groups, group_size, eps, 0, sl, q,
+                                                         scales, (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups, int64_t group_size,
+                                 float eps, int ue8m0, int64_t cm_rows, int64_t cm_groups, void* q,
+                                 float* scales, void* stream) {
+  if (n_groups < 0 || group_size <= 0 || group_size > (int64_t)1 << 30)
+    return fail(TO_EINVAL, "per_token_group_quant_fp8: invalid groups=%lld size=%lld",
+                (long long)n_groups, (long long)group_size);
+  if (cm_rows > 0 && (cm_groups <= 0 || n_groups % (cm_rows * cm_groups) != 0))
+    return fail(TO_EINVAL, "per_token_group_quant_fp8: column-major layout %lld x %lld does not "
+                "tile %lld groups", (long long)cm_rows, (long long)cm_groups, (long long)n_groups);
+  if (n_groups == 0) return TO_OK;
+  ScaleLayout sl{cm_rows, cm_groups > 0 ? cm_groups : 1};
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_group_quant<T, true>(x, n_groups, group_size, eps, ue8m0, sl, q,
+                                                        scales, (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_block_dequant_i8(const int8_t* q, const float* s, float* y, int64_t n, int64_t k,
+                        int64_t block_n, int64_t block_k, void* stream) {
+  return launch_block_dequant(false, q, s, y, n, k, block_n, block_k, (cudaStream_t)stream);
+}
+
+int to_block_dequant_fp8(const void* q, const float* s, float* y, int64_t n, int64_t k,
+                         int64_t block_n, int64_t block_k, void* stream) {
+  return launch_block_dequant(true, q, s, y, n, k, block_n, block_k, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,198 @@
+"""AWQ W4A16 facade: pack/unpack, dequantize and ``x @ dequant(W)`` on sm_100a.
+
+Drop-in for tileops/quant_awq.py: same names, arguments, validation order and messages,
+packed layouts (eight int4 per int32 in AWQ nibble order (0,4,1,5,2,6,3,7),
+quant_awq.py:19-22) and scale/zero conventions (``(w - z) * s`` per K-group). The math runs
+in libtileops_b200: the streaming GEMV for small M and the tcgen05 GEMM for prefill.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+# Supported group sizes; -1 is a sentinel and G == K is always accepted (quant_awq.py:19).
+AWQ_TRITON_SUPPORTED_GROUP_SIZES = [-1, 32, 64, 128]
+
+# Nibble position of logical column i inside its packed word (quant_awq.py:22).
+REVERSE_AWQ_ORDER = (0, 4, 1, 5, 2, 6, 3, 7)
+
+
+def _infer_group_size(k: int, num_groups: int) -> int:
+    """quant_awq.py:25-28."""
+    if num_groups <= 0 or k % num_groups != 0:
+        raise ValueError(f"invalid AWQ group layout: K={k}, num_groups={num_groups}")
+    return k // num_groups
+
+
+def _validate_group_size(group_size: int, k: int) -> None:
+    """quant_awq.py:31-38."""
+    if group_size > k:
+        raise ValueError(f"group_size {group_size} must be <= K={k}")
+    if group_size not in AWQ_TRITON_SUPPORTED_GROUP_SIZES and group_size != k:
+        raise ValueError(
+            f"group_size {group_size} not in {AWQ_TRITON_SUPPORTED_GROUP_SIZES} "
+            f"and not full K={k}"
+        )
+
+
+def unpack_awq_int4(packed: torch.Tensor) -> torch.Tensor:
+    """Unpack AWQ words to int64 nibbles in ``[0, 15]``; the last dim grows by 8
+    (quant_awq.py:41-52)."""
+    op = "unpack_awq_int4"
+    if packed.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"unpack_awq_int4: expected int32 packed tensor, got {packed.dtype}")
+    _lib.ensure_device(packed, op)
+    if packed.ndim == 0:
+        raise ValueError(f"{op}: expected at least 1 dimension")
+    p = packed.contiguous()
+    cols8 = p.shape[-1]
+    rows = p.numel() // cols8 if cols8 else 0
+    out = torch.empty(*p.shape[:-1], cols8 * 8, dtype=torch.int64, device=p.device)
+    _lib.call("to_awq_unpack", p.data_ptr(), _lib.DTYPE_CODES[p.dtype], out.data_ptr(), rows,
+              cols8, _lib.stream_ptr())
+    return out
+
+
+def pack_awq_int4(unpacked: torch.Tensor) -> torch.Tensor:
+    """Pack nibbles ``[..., cols]`` (``cols % 8 == 0``) into AWQ int32 words
+    (quant_awq.py:55-65). Only the low 4 bits of each value are kept; words whose top
+    nibble is >= 8 wrap to negative int32 as in the reference."""
+    if unpacked.shape[-1] % 8 != 0:
+        raise ValueError("pack_awq_int4: last dimension must be divisible by 8")
+    op = "pack_awq_int4"
+    _lib.ensure_device(unpacked, op)
+    u = unpacked
+    if u.dtype not in (torch.int32, torch.int64):
+        u = u.to(torch.int64)
+    u = u.contiguous()
+    cols8 = u.shape[-1] // 8
+    rows = u.numel() // (cols8 * 8) if cols8 else 0
+    out = torch.empty(*u.shape[:-1], cols8, dtype=torch.int32, device=u.device)
+    _lib.call("to_awq_pack", u.data_ptr(), _lib.DTYPE_CODES[u.dtype], out.data_ptr(), rows, cols8,
+              _lib.stream_ptr())
+    return out
+
+
+def _as_words(t: torch.Tensor) -> torch.Tensor:
+    # int64 packed words keep their low 32 bits, as the reference's unpack does.
+    if t.dtype == torch.int64:
+        t = t.to(torch.int32)
+    elif t.dtype != torch.int32:
+        raise TypeError(f"unpack_awq_int4: expected int32 packed tensor, got {t.dtype}")
+    return t.contiguous()
+
+
+def awq_dequantize_triton(
+    qweight: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    block_size_x: int = 32,
+    block_size_y: int = 32,
+) -> torch.Tensor:
+    """Dequantize AWQ ``qweight [K, N/8]`` with ``scales [K/G, N]`` and ``zeros [K/G, N/8]``
+    to ``[K, N]`` in ``scales.dtype`` (quant_awq.py:68-109). ``block_size_*`` are accepted
+    for API compatibility."""
+    del block_size_x, block_size_y
+    op = "awq_dequantize_triton"
+    if qweight.ndim != 2 or scales.ndim != 2 or zeros.ndim != 2:
+        raise ValueError("awq_dequantize_triton: qweight, scales, zeros must be 2-D")
+    k, packed_m = qweight.shape
+    m = packed_m * 8
+    num_groups = scales.shape[0]
+    group_size = _infer_group_size(k, num_groups)
+    if k <= 0 or m <= 0:
+        raise ValueError(f"awq_dequantize_triton: invalid shape K={k}, M={m}")
+    if scales.shape[1] != m:
+        raise ValueError(f"awq_dequantize_triton: scales.shape[1]={scales.shape[1]} != M={m}")
+    if zeros.shape != (num_groups, packed_m):
+        raise ValueError(
+            f"awq_dequantize_triton: zeros shape {tuple(zeros.shape)} expected "
+            f"({num_groups}, {packed_m})"
+        )
+    _validate_group_size(group_size, k)
+    _lib.ensure_device(qweight, op)
+    _lib.same_device(op, qweight, scales, zeros)
+    sd = _lib.dtype_code(scales.dtype, op)
+    qw = _as_words(qweight)
+    qz = _as_words(zeros)
+    s = scales.contiguous()
+    out = torch.empty(k, m, dtype=scales.dtype, device=qweight.device)
+    _lib.call("to_awq_dequant", qw.data_ptr(), s.data_ptr(), sd, qz.data_ptr(), out.data_ptr(),
+              k, m, group_size, _lib.stream_ptr())
+    return out
+
+
+def awq_gemm_triton(
+    input: torch.Tensor,
+    qweight: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor,
+    split_k_iters: int,
+    block_size_m: int = 32,
+    block_size_n: int = 32,
+    block_size_k: int = 32,
+) -> torch.Tensor:
+    """AWQ GEMM ``input [M, K] @ dequant(qweight) [K, N]`` in ``scales.dtype``
+    (quant_awq.py:112-155). ``split_k_iters`` is validated as in the reference and does not
+    change the result; the kernel picks its own K split."""
+    del block_size_m, block_size_n, block_size_k
+    op = "awq_gemm_triton"
+    if input.ndim != 2:
+        raise ValueError("awq_gemm_triton: input must be 2-D [M, K]")
+    m, k = input.shape
+    if qweight.shape[0] != k:
+        raise ValueError(f"awq_gemm_triton: qweight rows {qweight.shape[0]} != K={k}")
+    n = qweight.shape[1] * 8
+    num_groups = qzeros.shape[0]
+    group_size = _infer_group_size(k, num_groups)
+    if n <= 0 or m <= 0:
+        raise ValueError(f"awq_gemm_triton: invalid M={m}, N={n}, K={k}")
+    if qweight.shape[1] != n // 8:
+        raise ValueError("awq_gemm_triton: qweight column count mismatch")
+    if qzeros.shape[1] != n // 8:
+        raise ValueError("awq_gemm_triton: qzeros column count mismatch")
+    if scales.shape != (num_groups, n):
+        raise ValueError(
+            f"awq_gemm_triton: scales shape {tuple(scales.shape)} expected "
+            f"({num_groups}, {n})"
+        )
+    if split_k_iters <= 0 or (split_k_iters & (split_k_iters - 1)) != 0:
+        raise ValueError("awq_gemm_triton: split_k_iters must be a positive power of 2")
+    if split_k_iters > 32:
+        raise ValueError("awq_gemm_triton: split_k_iters must be <= 32")
+    _validate_group_size(group_size, k)
+    _lib.ensure_device(input, op)
+    _lib.same_device(op, input, qweight, scales, qzeros)
+    out_dtype = scales.dtype
+    if out_dtype not in (torch.float16, torch.bfloat16):
+        raise NotImplementedError(f"{op}: scales dtype {out_dtype} (fp16 and bf16 are supported)")
+    x = input.to(out_dtype).contiguous()
+    qw = _as_words(qweight)
+    qz = _as_words(qzeros)
+    s = scales.contiguous()
+    y = torch.empty(m, n, dtype=out_dtype, device=input.device)
+    lib = _lib.load()
+    ws_bytes = lib.to_awq_gemm_workspace_size(m, k, n, group_size)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device) if ws_bytes else None
+    _lib.call("to_awq_gemm", x.data_ptr(), qw.data_ptr(), s.data_ptr(),
+              _lib.DTYPE_CODES[out_dtype], qz.data_ptr(), y.data_ptr(), m, k, n, group_size,
+              _lib.ptr(ws), ws_bytes, _lib.stream_ptr())
+    return y
+
+
+# vLLM names kept as primary entry points (quant_awq.py:159-160).
+awq_dequantize = awq_dequantize_triton
+awq_gemm = awq_gemm_triton
+
+__all__ = [
+    "AWQ_TRITON_SUPPORTED_GROUP_SIZES",
+    "REVERSE_AWQ_ORDER",
+    "awq_dequantize",
+    "awq_dequantize_triton",
+    "awq_gemm",
+    "awq_gemm_triton",
+    "pack_awq_int4",
+    "unpack_awq_int4",
+]
