@@ -77,3 +77,14 @@ def cuda():
 
     lib.load()
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(autouse=True)
+def _device_error_word_clear(request):
+    """After every GPU test: no kernel may have left a bounded-wait timeout behind."""
+    yield
+    if request.node.get_closest_marker("gpu") is None or not torch.cuda.is_available():
+        return
+    import tileops_b200._lib as lib
+
+    assert lib.device_error_word(clear=True) == 0, "a kernel's bounded wait expired"

@@ -85,14 +85,14 @@ __global__ void __launch_bounds__(kThreads) k_awq_dequant(const uint32_t* __rest
 // Work split: a CTA owns a column tile of CW packed words (8*CW columns) and a K-chunk; the
 // K-chunks of one column tile form a thread-block cluster and are reduced through
 // distributed shared memory into cluster rank 0 (deterministic order, no global scratch).
-// Inside a CTA, each thread streams WPL consecutive words (16 or 8 bytes) of RUN
-// consecutive rows; the lanes of a row cover CW words so every warp load touches whole
-// 128-byte lines.
+// Inside a CTA, each thread streams WPL consecutive words of RUN consecutive rows; the lanes
+// of a row cover CW words so every warp load touches whole 128-byte lines.
 //
-// Arithmetic (fp16 models): (w - z) is formed exactly in half2 with the 0x6400 magic bias,
-// accumulated against x in half2 over one RUN of rows (all in one quantisation group), then
-// multiplied by the group scale and added to fp32 accumulators. bf16 models dequantise
-// exactly as the reference (bf16((w - z) * s)) and accumulate in fp32.
+// Arithmetic: (w - z) is formed exactly in half2 / bfloat162 with the magic-bias trick
+// (one LOP3 per column pair) and multiplied by the group scale in the model dtype, which is
+// exactly the reference's dequantised weight T((w - z) * s) (quant_awq.py:109). It is then
+// multiplied by x and accumulated in fp32 with sm_100's mixed-precision
+// fma.rn.f32.{f16,bf16} (exact products, fp32 sums, no conversions).
 constexpr int kRun = 16;
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -170,6 +170,27 @@ __device__ __forceinline__ void awq_zero_consts(uint32_t zw, typename Half2Of<T>
   }
 }
 
+// acc0 += lo(d2) * x, acc1 += hi(d2) * x with exact products and one fp32 rounding each.
+template <typename T>
+__device__ __forceinline__ void fma_pair_mixed(uint32_t d2, uint16_t x, float& a0, float& a1) {
+  if constexpr (std::is_same<T, __half>::value) {
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "fma.rn.f32.f16 %0, lo, %3, %0;\n\tfma.rn.f32.f16 %1, hi, %3, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(d2), "h"(x));
+  } else {
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, lo, %3, %0;\n\tfma.rn.f32.bf16 %1, hi, %3, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(d2), "h"(x));
+  }
+}
+
+template <typename H2>
+__device__ __forceinline__ uint32_t bits_of(H2 v) {
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 template <typename T, int MT, int WPL, int CW>
 __global__ void __launch_bounds__(kThreads) k_awq_gemv(const T* __restrict__ x,
                                                       const uint32_t* __restrict__ qw,
@@ -179,7 +200,6 @@ __global__ void __launch_bounds__(kThreads) k_awq_gemv(const T* __restrict__ x,
                                                       int G, int kchunk, int ksplit) {
   using H = Half2Of<T>;
   using H2 = typename H::type;
-  constexpr bool kF16 = std::is_same<T, __half>::value;
   constexpr int LPR = CW / WPL;      // lanes per row
   constexpr int RPW = 32 / LPR;      // rows a warp covers per load
   constexpr int NSLOT = (kThreads / 32) * RPW;
@@ -187,7 +207,7 @@ __global__ void __launch_bounds__(kThreads) k_awq_gemv(const T* __restrict__ x,
 
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // x chunk [MT][kchunk] in T, then the partial sums [MT][CW*8] fp32.
-  T* xs = reinterpret_cast<T*>(smem_raw);
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);
   float* part = reinterpret_cast<float*>(smem_raw + (((size_t)MT * kchunk * sizeof(T) + 15) & ~(size_t)15));
 
   const int words_per_row = N >> 3;
@@ -197,9 +217,10 @@ __global__ void __launch_bounds__(kThreads) k_awq_gemv(const T* __restrict__ x,
   const int ke = min(K, kb + kchunk);
   const int m0 = blockIdx.z * MT;
 
+  const uint16_t* x16 = reinterpret_cast<const uint16_t*>(x);
   for (int i = threadIdx.x; i < MT * kchunk; i += kThreads) {
     const int m = i / kchunk, k = i - m * kchunk;
-    xs[i] = (m0 + m < M && kb + k < K) ? x[(int64_t)(m0 + m) * K + kb + k] : from_f32<T>(0.f);
+    xs[i] = (m0 + m < M && kb + k < K) ? x16[(int64_t)(m0 + m) * K + kb + k] : (uint16_t)0;
   }
   for (int i = threadIdx.x; i < MT * CW * 8; i += kThreads) part[i] = 0.f;
   __syncthreads();
@@ -219,16 +240,7 @@ __global__ void __launch_bounds__(kThreads) k_awq_gemv(const T* __restrict__ x,
   if (col_ok) {
     for (int r0 = kb + slot * kRun; r0 < ke; r0 += NSLOT * kRun) {
       const int g = r0 / G;
-      H2 zc[WPL][4];
-      H2 sp[WPL][4];
-#pragma unroll
-      for (int j = 0; j < WPL; ++j) {
-        awq_zero_consts<T>(__ldg(qz + (int64_t)g * words_per_row + word0 + j), zc[j]);
-        const H2* s2 = reinterpret_cast<const H2*>(scales + (int64_t)g * N + (int64_t)(word0 + j) * 8);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sp[j][i] = s2[i];
-      }
-      // Issue every load of the run before any math: RUN x WPL words in flight per thread.
+      // Issue every load of the run first: RUN x WPL words in flight per thread.
       uint32_t wv[kRun][WPL];
 #pragma unroll
       for (int i = 0; i < kRun; ++i) {
@@ -246,64 +258,33 @@ __global__ void __launch_bounds__(kThreads) k_awq_gemv(const T* __restrict__ x,
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < WPL; ++j) wv[i][j] = 0;  // x is zero there, so any weight works
+          for (int j = 0; j < WPL; ++j) wv[i][j] = 0;  // x is zero there
         }
       }
+      H2 zc[WPL][4], sc[WPL][4];
+      const H2* s2 = reinterpret_cast<const H2*>(scales + (int64_t)g * N + (int64_t)word0 * 8);
+#pragma unroll
+      for (int j = 0; j < WPL; ++j) {
+        awq_zero_consts<T>(__ldg(qz + (int64_t)g * words_per_row + word0 + j), zc[j]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sc[j][q] = s2[j * 4 + q];
+      }
       const int xo = r0 - kb;
-      if constexpr (kF16) {
-        H2 ah[MT][WPL][4];
 #pragma unroll
-        for (int m = 0; m < MT; ++m)
+      for (int i = 0; i < kRun; ++i) {
+        uint16_t xv[MT];
 #pragma unroll
-          for (int j = 0; j < WPL; ++j)
+        for (int m = 0; m < MT; ++m) xv[m] = xs[m * kchunk + xo + i];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) ah[m][j][i] = __float2half2_rn(0.f);
-#pragma unroll
-        for (int i = 0; i < kRun; ++i) {
-          H2 xv[MT];
-#pragma unroll
-          for (int m = 0; m < MT; ++m) xv[m] = __half2half2(xs[m * kchunk + xo + i]);
-#pragma unroll
-          for (int j = 0; j < WPL; ++j) {
-            H2 d[4];
-            awq_word_diff<T>(wv[i][j], zc[j], d);
-#pragma unroll
-            for (int m = 0; m < MT; ++m)
-#pragma unroll
-              for (int q = 0; q < 4; ++q) ah[m][j][q] = __hfma2(d[q], xv[m], ah[m][j][q]);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < WPL; ++j)
+        for (int j = 0; j < WPL; ++j) {
+          H2 d[4];
+          awq_word_diff<T>(wv[i][j], zc[j], d);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const float2 sf = __half22float2(sp[j][q]);
+            const H2 w = __hmul2(d[q], sc[j][q]);  // the reference's dequantised weight pair
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              const float2 a = __half22float2(ah[m][j][q]);
-              acc[m][j * 8 + 2 * q] = fmaf(a.x, sf.x, acc[m][j * 8 + 2 * q]);
-              acc[m][j * 8 + 2 * q + 1] = fmaf(a.y, sf.y, acc[m][j * 8 + 2 * q + 1]);
-            }
-          }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kRun; ++i) {
-          float xv[MT];
-#pragma unroll
-          for (int m = 0; m < MT; ++m) xv[m] = to_f32(xs[m * kchunk + xo + i]);
-#pragma unroll
-          for (int j = 0; j < WPL; ++j) {
-            H2 d[4];
-            awq_word_diff<T>(wv[i][j], zc[j], d);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 wf = __bfloat1622float2(__hmul2(d[q], sp[j][q]));
-#pragma unroll
-              for (int m = 0; m < MT; ++m) {
-                acc[m][j * 8 + 2 * q] = fmaf(wf.x, xv[m], acc[m][j * 8 + 2 * q]);
-                acc[m][j * 8 + 2 * q + 1] = fmaf(wf.y, xv[m], acc[m][j * 8 + 2 * q + 1]);
-              }
-            }
+            for (int m = 0; m < MT; ++m)
+              fma_pair_mixed<T>(bits_of(w), xv[m], acc[m][j * 8 + 2 * q], acc[m][j * 8 + 2 * q + 1]);
           }
         }
       }
@@ -403,13 +384,13 @@ int launch_gemv(const void* x, const int32_t* qw, const void* s, const int32_t* 
   while (ksplit < 8 && tiles * ksplit * 2 <= 2 * sms &&
          K / (ksplit * 2) >= rows_per_run_slot * 8)
     ksplit *= 2;
-  if (MT <= 2 && v4) {
-    if (wide) return launch_gemv_cfg<T, MT, 4, 32>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
-    return launch_gemv_cfg<T, MT, 4, 16>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
-  }
-  if ((words % 2 == 0) && ((uintptr_t)qw % 8 == 0)) {
-    if (wide) return launch_gemv_cfg<T, MT, 2, 32>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
-    return launch_gemv_cfg<T, MT, 2, 16>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
+  // Registers grow with MT x columns per thread: 16 columns per thread up to MT = 2, 8 beyond.
+  (void)v4;
+  if constexpr (MT <= 2) {
+    if ((words % 2 == 0) && ((uintptr_t)qw % 8 == 0)) {
+      if (wide) return launch_gemv_cfg<T, MT, 2, 32>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
+      return launch_gemv_cfg<T, MT, 2, 16>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
+    }
   }
   if (wide) return launch_gemv_cfg<T, MT, 1, 32>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
   return launch_gemv_cfg<T, MT, 1, 16>(x, qw, s, qz, y, M, K, N, G, ksplit, st);

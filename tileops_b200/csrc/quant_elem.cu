@@ -199,8 +199,10 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
       amax = warp_max(amax, 32);
       if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
       __syncthreads();
+      // Several teams of 64..1024 threads can share a CTA; each reads only its own warps.
       float m = 0.f;
-      for (int w = 0; w < (team >> 5); ++w) m = fmaxf(m, red[w]);
+      const int w0 = (team_id * team) >> 5;
+      for (int w = 0; w < (team >> 5); ++w) m = fmaxf(m, red[w0 + w]);
       amax = m;
       __syncthreads();
     }
