@@ -80,3 +80,18 @@ def block_matmul_reference_cpu(a, b, a_s, b_s, block_size, out_dtype: str) -> np
     a_f = a.astype(np.float32) * a_s.astype(np.float32)[:, cols]
     b_f = block_dequant(b, b_s, block_size)
     return rounder(out_dtype)(a_f @ b_f.T)
+
+
+def block_matmul_reference_cpu_torch(a, b, a_s, b_s, block_size, out_dtype):
+    """The reference algorithm (quant_int8.py:223-228: fp32 dequant of both operands, fp32
+    GEMM, cast) on torch CPU tensors, the library the reference itself runs on; used as the
+    timed CPU baseline because it is the fastest faithful CPU restatement available."""
+    import torch
+
+    bn, bk = block_size
+    k = a.shape[1]
+    cols = torch.arange(k) // bk
+    rows = torch.arange(b.shape[0]) // bn
+    a_f = a.to(torch.float32) * a_s.to(torch.float32)[:, cols]
+    b_f = b.to(torch.float32) * b_s.to(torch.float32)[rows][:, cols]
+    return (a_f @ b_f.T).to(out_dtype)

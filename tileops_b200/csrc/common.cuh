@@ -28,7 +28,7 @@ int sm_count();
 // Device address of the library's error word on the current device (nullptr on failure).
 int* device_error_ptr();
 // Codes kernels write into the error word.
-enum DeviceError : int { kErrNone = 0, kErrWaitTimeout = 1, kErrTmemAlloc = 2 };
+enum DeviceError : int { kErrNone = 0, kErrWaitTimeout = 1, kErrTmemAlloc = 2, kErrSmemAlign = 3 };
 
 inline const char* dtype_name(int dt) {
   switch (dt) {

@@ -21,6 +21,9 @@
 // and returns.
 #include <cudaTypedefs.h>
 
+#include <stdlib.h>
+#include <string.h>
+
 #include <mutex>
 #include <unordered_map>
 
@@ -41,9 +44,16 @@ struct Epi {
   int32_t* acc_out;  // optional [M, N] raw int32 accumulators (kind::i8 only)
   int policy_a;      // L2 policy for A loads: 0 normal, 1 evict_first, 2 evict_last
   int policy_b;
+  // Optional timeline for tuning (null in production): per CTA, per K step, the global time
+  // the producer issued the stage, the MMA thread saw it land, and the MMA thread released it.
+  uint64_t* trace;
+  int trace_steps;
+  int tma_store;     // 16-bit C written through shared-memory staging + TMA stores
 };
 
-constexpr int kGemmThreads = 192;
+// warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue (two per TMEM lane quarter)
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 __host__ __device__ constexpr int pow2_at_least(int v) {
   int p = 32;
@@ -65,7 +75,10 @@ struct GemmCfg {
   static constexpr int kAccBufs = (2 * kAccCols <= 512) ? 2 : 1;
   static constexpr int kTmemCols = pow2_at_least(kAccBufs * kAccCols);
   static constexpr size_t kBarrierBytes = 256;
-  static constexpr size_t kSmem = 1024 + (size_t)STAGES * kStageBytes + kBarrierBytes;
+  // Epilogue staging for TMA stores of 16-bit outputs: one 32 x 32 x 2 B slab per warp.
+  static constexpr int kStageOutBytes = 32 * 32 * 2;
+  static constexpr size_t kOutBytes = kEpiWarps * kStageOutBytes;
+  static constexpr size_t kSmem = (size_t)STAGES * kStageBytes + kOutBytes + kBarrierBytes;
   static_assert(kTmemCols <= 512, "TMEM");
   static_assert(kSmem <= 232448, "shared memory");
 };
@@ -94,22 +107,136 @@ __device__ __forceinline__ void store_row_chunk16(T* dst, const float* v, const 
     for (int j = 0; j < 16; j += kVec)
       *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(o + j);
   } else {
-    for (int j = 0; j < valid; ++j) dst[j] = o[j];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < valid) dst[j] = o[j];
   }
 }
+
+// Per-column scales of one tile, preloaded by each epilogue warp while the main loop runs:
+// lane l holds b_s for tile columns 32*i + l in sb[i] (broadcast later with shuffles).
+template <int BN>
+__device__ __forceinline__ void load_tile_col_scales(float (&sb)[(BN + 31) / 32], const Epi& ep,
+                                                     int n0, int N, int lane) {
+#pragma unroll
+  for (int i = 0; i < (BN + 31) / 32; ++i) {
+    const int col = min(n0 + 32 * i + lane, N - 1);
+    const int64_t idx = ep.bn >= N ? 0 : (ep.bn == 1 ? (int64_t)col : (int64_t)col / ep.bn);
+    sb[i] = __ldg(ep.b_s + idx * ep.b_s_ld);
+  }
+}
+
+// sb[i] for a runtime i < (BN + 31) / 32 without dynamic register indexing.
+template <int BN>
+__device__ __forceinline__ float pick_scale(const float (&sb)[(BN + 31) / 32], int i) {
+  float s = sb[0];
+#pragma unroll
+  for (int k = 1; k < (BN + 31) / 32; ++k) s = (i == k) ? sb[k] : s;
+  return s;
+}
+
+// v[j] = acc[j] * (a_s[row] * b_s[col0 + j]) for the 32-column chunk starting at tile column c0.
+template <Kind KD, int BN>
+__device__ __forceinline__ void scale_chunk32(const uint32_t* r, float* v, float sa,
+                                              const float (&sb)[(BN + 31) / 32], int c0) {
+  const float mine = pick_scale<BN>(sb, c0 / 32);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float s = __shfl_sync(0xffffffffu, mine, j);
+    const float a = (KD == Kind::I8) ? (float)(int32_t)r[j] : __uint_as_float(r[j]);
+    v[j] = a * (sa * s);
+  }
+}
+
+// Rounds 32 values to the 16-bit output dtype (pairs packed in pk); a bias is added after
+// that rounding and rounded again, the order of `output + bias` in apply_w8a8_block_*_linear.
+__device__ __forceinline__ void pack_out16(const float* v, uint32_t* pk, const Epi& ep, int col0,
+                                           int valid) {
+  if (ep.bias == nullptr) {  // common case: one paired conversion per two values
+    if (ep.c_dtype == TO_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        __nv_bfloat162 o = __floats2bfloat162_rn(v[j], v[j + 1]);
+        pk[j / 2] = *reinterpret_cast<uint32_t*>(&o);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        __half2 o = __floats2half2_rn(v[j], v[j + 1]);
+        pk[j / 2] = *reinterpret_cast<uint32_t*>(&o);
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    uint16_t lo, hi;
+    if (ep.c_dtype == TO_BF16) {
+      __nv_bfloat16 a = __float2bfloat16_rn(v[j]), b = __float2bfloat16_rn(v[j + 1]);
+      if (ep.bias != nullptr) {
+        const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(ep.bias) + col0;
+        if (j < valid) a = __float2bfloat16_rn(__bfloat162float(a) + __bfloat162float(bias[j]));
+        if (j + 1 < valid) b = __float2bfloat16_rn(__bfloat162float(b) + __bfloat162float(bias[j + 1]));
+      }
+      lo = *reinterpret_cast<uint16_t*>(&a);
+      hi = *reinterpret_cast<uint16_t*>(&b);
+    } else {
+      __half a = __float2half_rn(v[j]), b = __float2half_rn(v[j + 1]);
+      if (ep.bias != nullptr) {
+        const __half* bias = reinterpret_cast<const __half*>(ep.bias) + col0;
+        if (j < valid) a = __float2half_rn(__half2float(a) + __half2float(bias[j]));
+        if (j + 1 < valid) b = __float2half_rn(__half2float(b) + __half2float(bias[j + 1]));
+      }
+      lo = *reinterpret_cast<uint16_t*>(&a);
+      hi = *reinterpret_cast<uint16_t*>(&b);
+    }
+    pk[j / 2] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+}
+
+// Direct row stores of one 32-column chunk (fp32 output, or shapes the TMA path rejects).
+template <Kind KD>
+__device__ __forceinline__ void store_direct(const float* v, const Epi& ep, int64_t off, int col0,
+                                             int valid, int N) {
+  if (ep.c_dtype == TO_BF16) {
+    const __nv_bfloat16* bias = ep.bias ? reinterpret_cast<const __nv_bfloat16*>(ep.bias) + col0 : nullptr;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.c) + off;
+    store_row_chunk16<__nv_bfloat16>(dst, v, bias, min(valid, 16), (N % 8) == 0);
+    if (valid > 16) store_row_chunk16<__nv_bfloat16>(dst + 16, v + 16, bias ? bias + 16 : nullptr, valid - 16, (N % 8) == 0);
+  } else if (ep.c_dtype == TO_F16) {
+    const __half* bias = ep.bias ? reinterpret_cast<const __half*>(ep.bias) + col0 : nullptr;
+    __half* dst = reinterpret_cast<__half*>(ep.c) + off;
+    store_row_chunk16<__half>(dst, v, bias, min(valid, 16), (N % 8) == 0);
+    if (valid > 16) store_row_chunk16<__half>(dst + 16, v + 16, bias ? bias + 16 : nullptr, valid - 16, (N % 8) == 0);
+  } else {
+    const float* bias = ep.bias ? reinterpret_cast<const float*>(ep.bias) + col0 : nullptr;
+    float* dst = reinterpret_cast<float*>(ep.c) + off;
+    store_row_chunk16<float>(dst, v, bias, min(valid, 16), (N % 4) == 0);
+    if (valid > 16) store_row_chunk16<float>(dst + 16, v + 16, bias ? bias + 16 : nullptr, valid - 16, (N % 4) == 0);
+  }
+}
+
+// First K block of tile t. Tiles start at different K offsets so that concurrently running
+// CTAs, which share the A (or B) operand, do not all request the same lines from L2 at the
+// same moment. Integer accumulation is exact in any order; fp32 accumulation order changes
+// only within rounding.
+__device__ __forceinline__ int k_start(int t, int kblocks) { return (int)(((unsigned)t * 5u) % (unsigned)kblocks); }
 
 template <Kind KD, int BM, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC16,
                  int M, int N, int K, Epi ep, int* err) {
   using C = GemmCfg<KD, BM, BN, STAGES>;
   using Tr = KindTraits<KD>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  // The swizzled operand tiles need 1024-byte alignment; the dynamic shared memory window
+  // is declared with that alignment.
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
   uint8_t* sA = smem;
   uint8_t* sB = smem + (size_t)STAGES * C::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + (size_t)STAGES * C::kBBytes);
+  uint8_t* sOut = sB + (size_t)STAGES * C::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::kOutBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -129,47 +256,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull + b, 1);
-      mbar_init(tempty + b, 4);
+      mbar_init(tempty + b, kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (ep.tma_store) {
+      prefetch_tmap(&tmC);
+      prefetch_tmap(&tmC16);
+    }
   }
+  // Every role depends on the 1024-byte alignment of the operand ring; without it the kernel
+  // records an error and does nothing.
+  const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
+  if (misaligned && threadIdx.x == 0 && err) atomicExch(err, (int)kErrSmemAlign);
   if (warp == 0) tmem_alloc<C::kTmemCols>(tmem_holder);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 0) {
+  if (misaligned) {
+    // nothing to do; fall through to the teardown
+  } else if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_a = make_policy(ep.policy_a), pol_b = make_policy(ep.policy_b);
       uint32_t s = 0, ph = 0;
-      uint32_t issued_phase[STAGES];
-      bool issued[STAGES];
-      for (int i = 0; i < STAGES; ++i) issued[i] = false, issued_phase[i] = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;  // per stage: loads issued / their phase
       bool ok = true;
+      int step = 0;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
         const int mt = t % m_tiles, nt = t / m_tiles;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int k0 = k_start(t, kblocks);
+        for (int it = 0; it < kblocks; ++it, ++step) {
+          const int kb = (k0 + it) % kblocks;
           if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
+          if (ep.trace != nullptr && step < ep.trace_steps)
+            ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 0] = globaltimer_ns();
           mbar_arrive_expect_tx(full + s, C::kStageBytes);
           tma_load_2d(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * BM, full + s, pol_a);
           tma_load_2d(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK, nt * BN, full + s, pol_b);
-          issued[s] = true;
-          issued_phase[s] = ph;
+          issued_mask |= 1u << s;
+          issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
       }
       if (!ok) {
         // Unwinding: let every copy this thread started land before the CTA exits.
         for (int i = 0; i < STAGES; ++i)
-          if (issued[i]) {
+          if (issued_mask & (1u << i)) {
             const uint64_t t0 = globaltimer_ns();
-            while (!mbar_try_wait(full + i, issued_phase[i]) &&
+            while (!mbar_try_wait(full + i, (issued_phase >> i) & 1u) &&
                    globaltimer_ns() - t0 < kWaitLimitNs) {
             }
           }
@@ -180,7 +320,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, 128, BN);
       uint32_t s = 0, ph = 0;
-      int i = 0;
+      int i = 0, step = 0;
       bool ok = true, any = false;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++i) {
         const int buf = i % C::kAccBufs;
@@ -188,9 +328,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait(tempty + buf, aph ^ 1, abort_flag, err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(buf * C::kAccCols);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int it = 0; it < kblocks; ++it, ++step) {
           if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
           tc_fence_after();
+          const bool tr = ep.trace != nullptr && step < ep.trace_steps;
+          if (tr) ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 1] = globaltimer_ns();
           const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
           const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
 #pragma unroll
@@ -199,11 +341,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int h = 0; h < C::kHalves; ++h) {
               const uint64_t adesc = smem_desc_kmajor_sw128(a0 + 16384 * h + 32 * k);
-              umma<KD>(d0 + (uint32_t)(h * BN), adesc, bdesc, idesc, (kb | k) != 0);
+              umma<KD>(d0 + (uint32_t)(h * BN), adesc, bdesc, idesc, (it | k) != 0);
             }
           }
           any = true;
           umma_commit(empty + s);
+          if (tr) ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 2] = globaltimer_ns();
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -219,68 +362,100 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // the TMEM lane quarter this warp may read
+    const int q = warp & 3;          // the TMEM lane quarter this warp may read
+    const int eg = (warp - 2) >> 2;  // which of the two warps on that quarter
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int buf = i % C::kAccBufs;
       const uint32_t aph = (uint32_t)(i / C::kAccBufs) & 1u;
+      // Scales of this tile, loaded while the main loop still runs.
+      float sbt[(BN + 31) / 32];
+      load_tile_col_scales<BN>(sbt, ep, (t / m_tiles) * BN, N, lane);
+      float sat[C::kHalves];
+#pragma unroll
+      for (int h = 0; h < C::kHalves; ++h) {
+        const int rr = (t % m_tiles) * BM + h * 128 + q * 32 + lane;
+        sat[h] = rr < M ? __ldg(ep.a_s + (int64_t)rr * ep.a_s_ld) : 0.f;
+      }
       if (!mbar_wait(tfull + buf, aph, abort_flag, err)) break;
       tc_fence_after();
+      // Epilogue timeline (tuning only): slots [2*gridDim.x*steps*3 ...] hold per-CTA
+      // (start, end) of the first tile's epilogue, written by lane 0 of the first epilogue warp.
+      const bool etr = ep.trace != nullptr && i == 0 && warp == 2 && lane == 0;
+      if (etr) ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + blockIdx.x * 2] = globaltimer_ns();
       const int mt = t % m_tiles, nt = t / m_tiles;
+      constexpr int kChunks = (BN + 31) / 32;
 #pragma unroll 1
       for (int h = 0; h < C::kHalves; ++h) {
-        const int row = mt * BM + h * 128 + q * 32 + lane;
+        const int row0 = mt * BM + h * 128 + q * 32;  // first row of this warp's 32-row slab
+        const int row = row0 + lane;
         const bool row_ok = row < M;
-        const float sa = row_ok ? __ldg(ep.a_s + (int64_t)row * ep.a_s_ld) : 0.f;
+        const float sa = (C::kHalves == 1 || h == 0) ? sat[0] : sat[C::kHalves - 1];
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::kAccCols + h * BN + c0),
-                    r);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          if (((h * kChunks + c0 / 32) & 1) != eg) continue;  // the two warps alternate chunks
+          const bool ctr = etr && h == 0 && c0 / 32 < 8;  // per-chunk epilogue timeline
+          uint64_t* ctp = ctr ? ep.trace + (int64_t)gridDim.x * ep.trace_steps * 3 + gridDim.x * 2 +
+                                    ((int64_t)blockIdx.x * 8 + c0 / 32) * 4
+                              : nullptr;
+          if (ctr) ctp[0] = globaltimer_ns();
+          const bool wide = (BN - c0) >= 32;  // BN = 80 ends with a 16-column chunk
+          uint32_t r[32];
+          const uint32_t taddr =
+              tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::kAccCols + h * BN + c0);
+          tmem_ld16(taddr, r);
+          if (wide) tmem_ld16(taddr + 16, r + 16);
           tmem_ld_wait();
+          if (ctr) ctp[1] = globaltimer_ns();
           const int col0 = nt * BN + c0;
-          if (!row_ok || col0 >= N) continue;
-          const int valid = min(16, N - col0);
-          float v[16];
+          if (col0 >= N) continue;
+          const int valid = min(wide ? 32 : 16, N - col0);
+          float v[32];
+          scale_chunk32<KD, BN>(r, v, sa, sbt, c0);
+          if (ctr) ctp[2] = globaltimer_ns();
+          if (KD == Kind::I8 && ep.acc_out != nullptr && row_ok) {
+            int32_t* dst = ep.acc_out + (int64_t)row * N + col0;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int col = min(col0 + j, N - 1);
-            const float sb = __ldg(ep.b_s + (ep.bn == 1 ? (int64_t)col : (int64_t)col / ep.bn) * ep.b_s_ld);
-            const float a = (KD == Kind::I8) ? (float)(int32_t)r[j] : __uint_as_float(r[j]);
-            v[j] = a * (sa * sb);
+            for (int j = 0; j < 32; ++j)
+              if (j < valid) dst[j] = (int32_t)r[j];
           }
-          const int64_t off = (int64_t)row * N + col0;
-          const bool vec_ok = (N % 8) == 0;
-          if (KD == Kind::I8 && ep.acc_out != nullptr) {
-            int32_t* dst = ep.acc_out + off;
-            if (vec_ok && valid == 16) {
+          if (ep.tma_store) {
+            uint8_t* stg = sOut + (size_t)(warp - 2) * C::kStageOutBytes;
+            if (lane == 0) bulk_wait_read<0>();  // the previous store has read the slab
+            __syncwarp();
+            uint32_t pk[16];
+            pack_out16(v, pk, ep, col0, valid);
+            if (wide) {
+              // 64-byte rows, 16-byte chunk c stored at c ^ ((row >> 1) & 3): the layout of a
+              // SWIZZLE_64B TMA box, and free of bank conflicts for these row-per-lane stores.
 #pragma unroll
-              for (int j = 0; j < 16; j += 4)
-                *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+              for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
             } else {
-              for (int j = 0; j < valid; ++j) dst[j] = (int32_t)r[j];
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+                *reinterpret_cast<uint4*>(stg + lane * 32 + (c << 4)) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
             }
-          }
-          if (ep.c_dtype == TO_BF16) {
-            store_row_chunk16<__nv_bfloat16>(
-                reinterpret_cast<__nv_bfloat16*>(ep.c) + off, v,
-                ep.bias ? reinterpret_cast<const __nv_bfloat16*>(ep.bias) + col0 : nullptr, valid,
-                vec_ok);
-          } else if (ep.c_dtype == TO_F16) {
-            store_row_chunk16<__half>(reinterpret_cast<__half*>(ep.c) + off, v,
-                                      ep.bias ? reinterpret_cast<const __half*>(ep.bias) + col0 : nullptr,
-                                      valid, vec_ok);
-          } else {
-            store_row_chunk16<float>(reinterpret_cast<float*>(ep.c) + off, v,
-                                     ep.bias ? reinterpret_cast<const float*>(ep.bias) + col0 : nullptr,
-                                     valid, (N % 4) == 0);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(wide ? &tmC : &tmC16, col0, row0, stg);
+              bulk_commit();
+            }
+            if (ctr) ctp[3] = globaltimer_ns();
+          } else if (row_ok) {
+            store_direct<KD>(v, ep, (int64_t)row * N + col0, col0, valid, N);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
+      if (etr) ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + blockIdx.x * 2 + 1] = globaltimer_ns();
       if (lane == 0) mbar_arrive(tempty + buf);
     }
+    if (ep.tma_store && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
   }
 
   tc_fence_before();
@@ -358,6 +533,27 @@ int make_tmap_kmajor(CUtensorMap* out, const void* ptr, int64_t rows, int64_t co
   return TO_OK;
 }
 
+// Output map for the staged epilogue: C [rows, cols] of 16-bit elements, box = 32 rows x
+// box_cols columns; 32-column boxes read a 64-byte-swizzled staging slab, 16-column (tail)
+// boxes a plain one with 32-byte rows.
+int make_tmap_out16(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int box_cols,
+                    int dtype) {
+  EncodeFn encode = get_encode();
+  if (!encode) return fail(TO_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(out, dtype == TO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      2, const_cast<void*>(ptr), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TO_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return TO_OK;
+}
+
 template <Kind KD, int BM, int BN, int STAGES>
 int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                     cudaStream_t st) {
@@ -369,24 +565,53 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "tcgen05 gemm: shared memory attribute");
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc32, tc16;
   int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, BM);
   if (rc) return rc;
   rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, BN);
   if (rc) return rc;
+  Epi e2 = ep;
+  memset(&tc32, 0, sizeof(tc32));
+  memset(&tc16, 0, sizeof(tc16));
+  if (e2.tma_store) {
+    rc = make_tmap_out16(&tc32, e2.c, M, N, 32, e2.c_dtype);
+    if (!rc) rc = make_tmap_out16(&tc16, e2.c, M, N, 16, e2.c_dtype);
+    if (rc) return rc;
+  }
   const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN);
   const int grid = (int)std::min<int64_t>(tiles, sm_count());
   k_gemm_sm100<KD, BM, BN, STAGES><<<grid, kGemmThreads, C::kSmem, st>>>(
-      ta, tb, (int)M, (int)N, (int)K, ep, device_error_ptr());
+      ta, tb, tc32, tc16, (int)M, (int)N, (int)K, e2, device_error_ptr());
   return check_launch("tcgen05 gemm");
 }
 
 // Tile shapes: large problems take 128 x 256 tiles; small-M layers (M <= 256, the decode /
 // small-batch regime, HBM-bound on B) take the narrowest N tile that still fits every tile
 // in one wave, so all SMs stream B at once.
+// TOB_GEMM_TILE=<BM>x<BN> forces one of the compiled tile shapes (tuning and tests).
+inline int forced_tile() {
+  static int v = [] {
+    const char* e = getenv("TOB_GEMM_TILE");
+    if (!e) return 0;
+    int bm = 0, bn = 0;
+    if (sscanf(e, "%dx%d", &bm, &bn) != 2) return 0;
+    return bm * 1000 + bn;
+  }();
+  return v;
+}
+
 template <Kind KD>
 int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                 cudaStream_t st) {
+  switch (forced_tile()) {
+    case 128256: return launch_gemm_cfg<KD, 128, 256, 4>(a, b, M, N, K, ep, st);
+    case 128128: return launch_gemm_cfg<KD, 128, 128, 6>(a, b, M, N, K, ep, st);
+    case 128064: return launch_gemm_cfg<KD, 128, 64, 8>(a, b, M, N, K, ep, st);
+    case 256128: return launch_gemm_cfg<KD, 256, 128, 4>(a, b, M, N, K, ep, st);
+    case 256080: return launch_gemm_cfg<KD, 256, 80, 5>(a, b, M, N, K, ep, st);
+    case 256064: return launch_gemm_cfg<KD, 256, 64, 5>(a, b, M, N, K, ep, st);
+    default: break;
+  }
   const int64_t sms = sm_count();
   auto tiles = [&](int bm, int bn) { return ceil_div(M, bm) * ceil_div(N, bn); };
   if (M > 256 || tiles(128, 256) >= sms) return launch_gemm_cfg<KD, 128, 256, 4>(a, b, M, N, K, ep, st);
@@ -427,6 +652,18 @@ int w8a8_tc_launch(bool fp8, const void* a, const void* b, const float* a_s, con
   const bool small_m = M <= 256;
   ep.policy_a = small_m ? 2 : 0;
   ep.policy_b = small_m ? 1 : 0;
+  ep.trace = nullptr;
+  ep.trace_steps = 0;
+  ep.tma_store = (c_dtype == TO_BF16 || c_dtype == TO_F16) && (N % 8 == 0) && aligned16(c) &&
+                 getenv("TOB_GEMM_DIRECT_STORE") == nullptr;
+  if (const char* e = getenv("TOB_GEMM_TRACE")) {  // "<device pointer>:<steps>" (tuning only)
+    unsigned long long p = 0;
+    int steps = 0;
+    if (sscanf(e, "%llx:%d", &p, &steps) == 2) {
+      ep.trace = reinterpret_cast<uint64_t*>(p);
+      ep.trace_steps = steps;
+    }
+  }
   if (fp8) return sm100::launch_gemm<sm100::Kind::E4M3>(a, b, M, N, K, ep, st);
   return sm100::launch_gemm<sm100::Kind::I8>(a, b, M, N, K, ep, st);
 }
