@@ -91,6 +91,17 @@ TO_API int to_input_to_int8(const void* x, int x_dtype, int64_t n, int8_t* q, fl
 /* replaces tileops/quant_fp8.py:52 input_to_float8 (e4m3fn; same arithmetic with 448). */
 TO_API int to_input_to_fp8(const void* x, int x_dtype, int64_t n, void* q, float* dq_scale,
                     void* workspace, size_t workspace_bytes, void* stream);
+/* No counterpart in the reference. Same result as to_input_to_fp8, for callers that cannot
+ * hand the library a device workspace: runtimes that reserve all device memory for their own
+ * pool at start-up, so a cudaMalloc during serving fails or fragments it, and foreign-language
+ * bindings that only pass tensor pointers and have no device allocator of their own. Its
+ * scratch (33 KB per GPU, held until the process exits) is built into the library, which caps
+ * n at 134,217,728 elements (TO_EINVAL beyond). It allocates nothing. The first call on each
+ * device looks up the scratch address with that device current; make that first call before
+ * any stream capture. All calls share the one scratch buffer: calls that overlap on the GPU
+ * (several streams or host threads at once) race and must be serialised. */
+TO_API int to_input_to_fp8_noalloc(const void* x, int x_dtype, int64_t n, void* q,
+                                   float* dq_scale, void* stream);
 /* replaces tileops/quant_int8.py:109 per_token_group_quant_int8 and :54 per_token_quant_int8
  * (group_size = K). x is [n_groups, group_size] contiguous; scales[g] = max(absmax,eps)/127. */
 TO_API int to_per_token_group_quant_i8(const void* x, int x_dtype, int64_t n_groups,

@@ -6,6 +6,8 @@
 // Every kernel reads its input once with 16-byte vector loads and a grid sized to the SM
 // count; all float arithmetic is IEEE round-to-nearest-even so results match the
 // reference's torch expressions bit for bit.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace tob {
@@ -377,6 +379,106 @@ int launch_block_dequant(bool fp8, const void* q, const float* s, float* y, int6
   return check_launch("block_dequant");
 }
 
+// ------------------------------------------------------------------ no-allocation variant
+// Scratch of to_input_to_fp8_noalloc: one partial |x| maximum (float bits) per chunk of
+// kNoAllocChunk elements, then the final maximum at index kNoAllocSlots. It is part of the
+// library image, so every GPU that loads the library holds these 33 KB until the process
+// exits. Each call writes every slot it later reads, so nothing needs clearing between calls;
+// two calls that run at the same time on the GPU (different streams or threads) overwrite each
+// other's slots and must not overlap.
+constexpr int kNoAllocSlots = 8192;
+constexpr int64_t kNoAllocChunk = 16384;
+constexpr int64_t kNoAllocMaxElems = (int64_t)kNoAllocSlots * kNoAllocChunk;  // 134,217,728
+static __device__ __align__(256) unsigned g_noalloc_amax[kNoAllocSlots + 64];
+
+// CTA b: max |x| over elements [b * kNoAllocChunk, min(n, (b + 1) * kNoAllocChunk)).
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) k_absmax_chunks(const T* __restrict__ x, int64_t n,
+                                                           unsigned* __restrict__ partial) {
+  const int64_t beg = (int64_t)blockIdx.x * kNoAllocChunk;
+  const int64_t end = min(n, beg + kNoAllocChunk);
+  float m = 0.f;
+  const int64_t vbeg = (beg + V - 1) / V, vend = end / V;
+  for (int64_t i = vbeg + threadIdx.x; i < vend; i += blockDim.x) {
+    Pack<T, V> v = ld_pack<T, V>(x + i * V);
+#pragma unroll
+    for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f32(v.v[j])));
+  }
+  for (int64_t i = beg + threadIdx.x; i < min(end, vbeg * V); i += blockDim.x)
+    m = fmaxf(m, fabsf(to_f32(x[i])));  // head before the first full vector
+  for (int64_t i = max(vend * V, beg) + threadIdx.x; i < end; i += blockDim.x)
+    m = fmaxf(m, fabsf(to_f32(x[i])));  // tail after the last full vector
+  m = warp_max(m, 32);
+  __shared__ float red[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) b = fmaxf(b, red[w]);
+    partial[blockIdx.x] = __float_as_uint(b);
+  }
+}
+
+// One CTA folds the nparts partial maxima into *out.
+__global__ void __launch_bounds__(1024) k_absmax_final(const unsigned* __restrict__ partial,
+                                                      int nparts, unsigned* __restrict__ out) {
+  float m = 0.f;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = fmaxf(m, __uint_as_float(partial[i]));
+  m = warp_max(m, 32);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = fmaxf(b, red[w]);
+    *out = __float_as_uint(b);
+  }
+}
+
+// Device address of g_noalloc_amax on the current device, looked up once per device with
+// that device current (a host-side reference to the array itself is not a device address).
+int noalloc_scratch(unsigned** out) {
+  static std::mutex mu;
+  static unsigned* cached[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "input_to_float8 (no-alloc): cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(TO_EUNSUPPORTED, "input_to_float8 (no-alloc): device %d", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_amax);
+    if (e != cudaSuccess) return cuda_fail(e, "input_to_float8 (no-alloc): cudaGetSymbolAddress");
+    cached[dev] = static_cast<unsigned*>(p);
+  }
+  *out = cached[dev];
+  return TO_OK;
+}
+
+template <typename T>
+int launch_tensor_quant_fp8_noalloc(const void* x, int64_t n, void* q, float* dq_scale,
+                                    unsigned* scratch, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const int nparts = (int)ceil_div(n, kNoAllocChunk);
+  const bool vec = aligned16(x) && aligned_to(q, V);
+  if (vec)
+    k_absmax_chunks<T, V><<<nparts, kThreads, 0, st>>>((const T*)x, n, scratch);
+  else
+    k_absmax_chunks<T, 1><<<nparts, kThreads, 0, st>>>((const T*)x, n, scratch);
+  int rc = check_launch("input_to_float8 (no-alloc): partial amax");
+  if (rc) return rc;
+  unsigned* amax = scratch + kNoAllocSlots;
+  k_absmax_final<<<1, 1024, 0, st>>>(scratch, nparts, amax);
+  rc = check_launch("input_to_float8 (no-alloc): final amax");
+  if (rc) return rc;
+  const unsigned grid = grid_for(ceil_div(n, V), kThreads, 8);
+  if (vec)
+    k_tensor_quant<T, true, V><<<grid, kThreads, 0, st>>>((const T*)x, n, amax, (uint8_t*)q, dq_scale);
+  else
+    k_tensor_quant<T, true, 1><<<grid, kThreads, 0, st>>>((const T*)x, n, amax, (uint8_t*)q, dq_scale);
+  return check_launch("input_to_float8 (no-alloc): quantize");
+}
+
 }  // namespace
 }  // namespace tob
 
@@ -451,6 +553,23 @@ int to_input_to_fp8(const void* x, int x_dtype, int64_t n, void* q, float* dq_sc
   TOB_DISPATCH_FLOAT(x_dtype, T,
                      return launch_tensor_quant<T, true>(x, n, q, dq_scale, (unsigned*)workspace,
                                                          (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_input_to_fp8_noalloc(const void* x, int x_dtype, int64_t n, void* q, float* dq_scale,
+                            void* stream) {
+  if (n <= 0) return fail(TO_EINVAL, "input_to_float8 (no-alloc): empty input");
+  if (n > kNoAllocMaxElems)
+    return fail(TO_EINVAL,
+                "input_to_float8 (no-alloc): %lld elements exceed the built-in scratch limit of "
+                "%lld; use to_input_to_fp8 with a caller workspace for larger tensors",
+                (long long)n, (long long)kNoAllocMaxElems);
+  unsigned* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_tensor_quant_fp8_noalloc<T>(x, n, q, dq_scale, scratch,
+                                                               (cudaStream_t)stream));
   return TO_OK;
 }
 
