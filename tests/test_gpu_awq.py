@@ -99,6 +99,39 @@ def test_gemm_vs_oracle(cuda, dtype, m, k, n, g):
     np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("m,k,n,g", [
+    (128, 512, 768, 32),      # two quantisation groups per K block
+    (300, 1024, 1024, 64),    # M tail
+    (33, 4096, 256, 4096),    # one group over the whole K
+    (512, 8192, 1024, 128),   # the 70B-class up-projection shape, narrowed in N
+    (256, 200, 512, 200),     # K tail (K not a multiple of the K block), G == K
+])
+def test_gemm_tensor_core_vs_oracle(cuda, dtype, m, k, n, g):
+    gen = torch.Generator().manual_seed(m + k * 3 + n)
+    qw, s, qz = make_awq(k, n, g, _DT[dtype], gen)
+    x = torch.randn(m, k, generator=gen).to(_DT[dtype])
+    y = tob.awq_gemm(x.to(cuda), qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    want = oawq.gemm(x.float().numpy(), qw.numpy(), s.float().numpy(), qz.numpy(), dtype)
+    np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+
+
+def test_gemm_prefill_full_size_sampled(cuda):
+    """M=2048, K=8192, N=28672 bf16 (G=128): rows and columns sampled against the oracle."""
+    m, k, n, g = 2048, 8192, 28672, 128
+    gen = torch.Generator().manual_seed(1234 + 3)
+    qw, s, qz = make_awq(k, n, g, torch.bfloat16, gen)
+    x = torch.randn(m, k, generator=gen).bfloat16()
+    y = tob.awq_gemm(x.to(cuda), qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    rows = torch.randperm(m, generator=gen)[:24].sort().values
+    words = torch.randperm(n // 8, generator=gen)[:40].sort().values
+    cols = (words[:, None] * 8 + torch.arange(8)[None, :]).reshape(-1)
+    want = oawq.gemm(x[rows].float().numpy(), qw[:, words].numpy(), s[:, cols].float().numpy(),
+                     qz[:, words].numpy(), "bf16")
+    got = y[rows.to(cuda)][:, cols.to(cuda)].float().cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
 def test_gemm_deterministic(cuda):
     gen = torch.Generator().manual_seed(9)
     qw, s, qz = make_awq(4096, 4096, 128, torch.float16, gen)

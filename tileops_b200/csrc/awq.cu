@@ -12,6 +12,7 @@
 
 #include <type_traits>
 
+#include "awq_common.cuh"
 #include "common.cuh"
 
 namespace cg = cooperative_groups;
@@ -20,6 +21,7 @@ namespace tob {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int64_t kTensorCoreMinM = 32;
 __constant__ int kAwqOrder[8] = {0, 4, 1, 5, 2, 6, 3, 7};
 
 // ------------------------------------------------------------------ pack / unpack
@@ -95,81 +97,6 @@ __global__ void __launch_bounds__(kThreads) k_awq_dequant(const uint32_t* __rest
 // fma.rn.f32.{f16,bf16} (exact products, fp32 sums, no conversions).
 constexpr int kRun = 16;
 
-__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-template <typename T> struct Half2Of;
-template <> struct Half2Of<__half> {
-  using type = __half2;
-  static constexpr uint32_t kMagic = 0x64006400u;  // 1024.0 in each half
-  static __device__ __forceinline__ __half2 from_bits(uint32_t b) {
-    return *reinterpret_cast<__half2*>(&b);
-  }
-  static __device__ __forceinline__ __half2 sixteenth() { return __float2half2_rn(0.0625f); }
-  static __device__ __forceinline__ float magic_f() { return 1024.f; }
-};
-template <> struct Half2Of<__nv_bfloat16> {
-  using type = __nv_bfloat162;
-  static constexpr uint32_t kMagic = 0x43004300u;  // 128.0 in each bf16
-  static __device__ __forceinline__ __nv_bfloat162 from_bits(uint32_t b) {
-    return *reinterpret_cast<__nv_bfloat162*>(&b);
-  }
-  static __device__ __forceinline__ __nv_bfloat162 sixteenth() {
-    return __float2bfloat162_rn(0.0625f);
-  }
-  static __device__ __forceinline__ float magic_f() { return 128.f; }
-};
-
-// Exact (w - z) for the four column pairs of one word: d[i] holds columns (2i, 2i+1).
-// fp16: the 10-bit mantissa of 1024.0 holds a nibble at bits 0-3 or 4-7 of each half, so
-//   two masks per byte suffice; the bits-4-7 pairs come out as 1024 + 16 v and are folded
-//   back with one fma: (1024 + 16 v)/16 - (64 + z) = v - z (exact).
-//   zc[0], zc[2] = (1024 + z) pairs for columns 01/45; zc[1], zc[3] = -(64 + z) for 23/67.
-// bf16: the 7-bit mantissa of 128.0 only holds bits 0-3, so every pair is shifted down first
-//   and zc[i] = (128 + z) pairs for all four.
-template <typename T>
-__device__ __forceinline__ void awq_word_diff(uint32_t word, const typename Half2Of<T>::type* zc,
-                                              typename Half2Of<T>::type* d) {
-  using H = Half2Of<T>;
-  if constexpr (std::is_same<T, __half>::value) {
-    const uint32_t w8 = word >> 8;
-    const auto p01 = H::from_bits(lop3_and_or(word, 0x000F000Fu, H::kMagic));
-    const auto p23 = H::from_bits(lop3_and_or(word, 0x00F000F0u, H::kMagic));
-    const auto p45 = H::from_bits(lop3_and_or(w8, 0x000F000Fu, H::kMagic));
-    const auto p67 = H::from_bits(lop3_and_or(w8, 0x00F000F0u, H::kMagic));
-    const auto q = H::sixteenth();
-    d[0] = __hsub2(p01, zc[0]);
-    d[1] = __hfma2(p23, q, zc[1]);
-    d[2] = __hsub2(p45, zc[2]);
-    d[3] = __hfma2(p67, q, zc[3]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      d[i] = __hsub2(H::from_bits(lop3_and_or(word >> (4 * i), 0x000F000Fu, H::kMagic)), zc[i]);
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ void awq_zero_consts(uint32_t zw, typename Half2Of<T>::type* zc) {
-  using H = Half2Of<T>;
-  if constexpr (std::is_same<T, __half>::value) {
-    const uint32_t z8 = zw >> 8;
-    const auto q = H::sixteenth();
-    // -(64 + z) = -(p * 1/16) with p = 1024 + 16 z (the product is exact)
-    zc[0] = H::from_bits(lop3_and_or(zw, 0x000F000Fu, H::kMagic));
-    zc[1] = __hneg2(__hmul2(H::from_bits(lop3_and_or(zw, 0x00F000F0u, H::kMagic)), q));
-    zc[2] = H::from_bits(lop3_and_or(z8, 0x000F000Fu, H::kMagic));
-    zc[3] = __hneg2(__hmul2(H::from_bits(lop3_and_or(z8, 0x00F000F0u, H::kMagic)), q));
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      zc[i] = H::from_bits(lop3_and_or(zw >> (4 * i), 0x000F000Fu, H::kMagic));
-  }
-}
-
 // acc0 += lo(d2) * x, acc1 += hi(d2) * x with exact products and one fp32 rounding each.
 template <typename T>
 __device__ __forceinline__ void fma_pair_mixed(uint32_t d2, uint16_t x, float& a0, float& a1) {
@@ -184,11 +111,6 @@ __device__ __forceinline__ void fma_pair_mixed(uint32_t d2, uint16_t x, float& a
         : "+f"(a0), "+f"(a1)
         : "r"(d2), "h"(x));
   }
-}
-
-template <typename H2>
-__device__ __forceinline__ uint32_t bits_of(H2 v) {
-  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 template <typename T, int MT, int WPL, int CW>
@@ -418,6 +340,10 @@ int check_awq_shapes(const char* op, int64_t K, int64_t N, int64_t G) {
 
 }  // namespace
 
+int awq_gemm_tc_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
+                       cudaStream_t st);
+
 // Used by the tensor-core GEMM translation unit when it must stream small M.
 int awq_gemv_dispatch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
@@ -508,6 +434,12 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
   if (M <= 0) return fail(TO_EINVAL, "awq_gemm: invalid M=%lld", (long long)M);
   if (!aligned16(scales) || !aligned16(x))
     return fail(TO_EINVAL, "awq_gemm: x and scales must be 16-byte aligned");
+  // Prefill-sized M runs on the tensor cores; small M streams the weights once per 4 rows.
+  if (M >= kTensorCoreMinM) {
+    const int rc = awq_gemm_tc_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N,
+                                      group_size, (cudaStream_t)stream);
+    if (rc != TO_EUNSUPPORTED) return rc;
+  }
   return awq_gemv_dispatch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size,
                            (cudaStream_t)stream);
 }

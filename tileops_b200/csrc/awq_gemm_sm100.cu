@@ -1,0 +1,339 @@
+// AWQ W4A16 GEMM on the sm_100a tensor cores: y[M, N] = x[M, K] @ dequant(W)[K, N]
+// (tileops/quant_awq.py:112-155) for prefill-sized M.
+//
+// The packed int4 weights never exist in HBM as fp16/bf16: each K block of the weight tile is
+// TMA-loaded packed (0.5 B per weight), expanded in shared memory by four dequantising warps
+// into the exact reference weights T((w - z) * s) (quant_awq.py:104-109), and consumed by
+// tcgen05.mma kind::f16 straight from there.
+//
+// Per CTA (persistent, one per SM, 320 threads), tile 128 (M) x 256 (N), K blocks of 64:
+//   warp 0     TMA producer: x tile [128 x 64] (K-major, 128B swizzle), packed weights
+//              [64 rows x 32 words], the block's scale and zero rows          -> full[s]
+//   warps 2-5  dequantise: one packed word (8 columns at one k) -> one 16-byte store into the
+//              B operand, MN-major with the 128-byte swizzle                  -> bready[s]
+//   warp 1     MMA: 4 x tcgen05.mma (K = 16 each), A K-major, B MN-major     -> empty[s], tfull
+//   warps 6-9  epilogue: TMEM -> bf16/fp16 -> 64B-swizzled staging -> TMA store -> tempty
+// Accumulators are double-buffered in TMEM (2 x 256 columns). Waits are bounded (sm100.cuh).
+#include <string.h>
+
+#include <mutex>
+
+#include "awq_common.cuh"
+#include "sm100.cuh"
+
+namespace tob {
+namespace sm100 {
+namespace {
+
+constexpr int kAwqBM = 128, kAwqBN = 256, kAwqBK = 64, kAwqStages = 3;
+constexpr int kAwqThreads = 320;
+constexpr int kAwqABytes = kAwqBM * 128;          // 16 KB x tile
+constexpr int kAwqWBytes = kAwqBK * kAwqBN / 2;   // 8 KB packed weights (64 rows x 32 words)
+constexpr int kAwqBBytes = kAwqBK * kAwqBN * 2;   // 32 KB dequantised weights
+constexpr int kAwqSBytes = 2 * kAwqBN * 2;        // up to 2 scale rows (group 32)
+constexpr int kAwqZBytes = 2 * (kAwqBN / 8) * 4;  // up to 2 zero rows
+constexpr int kAwqSZBytes = 2048;                 // scales + zeros, padded
+constexpr int kAwqStageBytes = kAwqABytes + kAwqWBytes + kAwqBBytes + kAwqSZBytes;
+constexpr int kAwqOutBytes = 4 * 32 * 32 * 2;     // 4 epilogue warps x one 32 x 32 slab
+constexpr size_t kAwqSmem = (size_t)kAwqStages * kAwqStageBytes + kAwqOutBytes + 256;
+static_assert(kAwqSBytes + kAwqZBytes <= kAwqSZBytes, "scale/zero area");
+static_assert(kAwqSmem <= 232448, "shared memory");
+// B operand layout (MN-major, 128B swizzle): 1 KB atoms of 8 k-rows x 64 columns; the 8 atoms
+// of a 64-column strip are contiguous along K, strips are 8 KB apart.
+constexpr uint32_t kAwqBLbo = 8192, kAwqBSbo = 1024;
+
+__device__ __forceinline__ int awq_k_start(int t, int kblocks) {
+  return (int)(((unsigned)t * 5u) % (unsigned)kblocks);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kAwqThreads, 1)
+    k_awq_gemm_sm100(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
+                     const __grid_constant__ CUtensorMap tmY, int M, int N, int K, int G,
+                     int group_rows, int* err) {
+  using H = Half2Of<T>;
+  using H2 = typename H::type;
+  constexpr Kind KD = std::is_same<T, __half>::value ? Kind::F16 : Kind::BF16;
+  using Tr = KindTraits<KD>;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* stage0 = smem_raw;
+  uint8_t* sOut = smem_raw + (size_t)kAwqStages * kAwqStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kAwqOutBytes);
+  uint64_t* bready = full + kAwqStages;
+  uint64_t* empty = bready + kAwqStages;
+  uint64_t* tfull = empty + kAwqStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  auto sA = [&](int s) { return stage0 + (size_t)s * kAwqStageBytes; };
+  auto sW = [&](int s) { return stage0 + (size_t)s * kAwqStageBytes + kAwqABytes; };
+  auto sB = [&](int s) { return stage0 + (size_t)s * kAwqStageBytes + kAwqABytes + kAwqWBytes; };
+  auto sS = [&](int s) {
+    return stage0 + (size_t)s * kAwqStageBytes + kAwqABytes + kAwqWBytes + kAwqBBytes;
+  };
+  auto sZ = [&](int s) { return sS(s) + kAwqSBytes; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + kAwqBM - 1) / kAwqBM, n_tiles = (N + kAwqBN - 1) / kAwqBN;
+  const int tiles = m_tiles * n_tiles;
+  const int kblocks = (K + kAwqBK - 1) / kAwqBK;
+  const uint32_t stage_tx = kAwqABytes + kAwqWBytes + group_rows * (kAwqBN * 2 + (kAwqBN / 8) * 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAwqStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(bready + s, 4);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmX);
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmS);
+    prefetch_tmap(&tmZ);
+    prefetch_tmap(&tmY);
+  }
+  if (warp == 0) tmem_alloc<512>(tmem_holder);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
+  if (misaligned && threadIdx.x == 0 && err) atomicExch(err, (int)kErrSmemAlign);
+
+  if (misaligned) {
+  } else if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_last();  // x and the weight tile are re-read by other CTAs
+      uint32_t s = 0, ph = 0, issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int mt = t % m_tiles, nt = t / m_tiles;
+        const int k0 = awq_k_start(t, kblocks);
+        for (int it = 0; it < kblocks; ++it) {
+          const int kb = (k0 + it) % kblocks;
+          if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(full + s, stage_tx);
+          const int g0 = group_rows == 1 ? (kb * kAwqBK) / G : kb * group_rows;
+          tma_load_2d(sA(s), &tmX, kb * kAwqBK, mt * kAwqBM, full + s, pol);
+          tma_load_2d(sW(s), &tmW, nt * (kAwqBN / 8), kb * kAwqBK, full + s, pol);
+          tma_load_2d(sS(s), &tmS, nt * kAwqBN, g0, full + s, pol);
+          tma_load_2d(sZ(s), &tmZ, nt * (kAwqBN / 8), g0, full + s, pol);
+          issued_mask |= 1u << s;
+          issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
+          if (++s == kAwqStages) { s = 0; ph ^= 1; }
+        }
+      }
+      if (!ok) {
+        for (int i = 0; i < kAwqStages; ++i)
+          if (issued_mask & (1u << i)) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(full + i, (issued_phase >> i) & 1u) &&
+                   globaltimer_ns() - t0 < kWaitLimitNs) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc =
+          make_idesc_major(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, kAwqBM, kAwqBN, 0, 1);
+      uint32_t s = 0, ph = 0;
+      int i = 0;
+      bool ok = true, any = false;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        const uint32_t aph = (uint32_t)(i >> 1) & 1u;
+        if (!mbar_wait(tempty + buf, aph ^ 1, abort_flag, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d0 = tmem + (uint32_t)(buf * kAwqBN);
+        for (int it = 0; it < kblocks; ++it) {
+          if (!mbar_wait(full + s, ph, abort_flag, err) ||
+              !mbar_wait(bready + s, ph, abort_flag, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
+#pragma unroll
+          for (int k = 0; k < kAwqBK / 16; ++k) {
+            const uint64_t adesc = smem_desc_kmajor_sw128(a0 + 32 * k);
+            const uint64_t bdesc = smem_desc_mnmajor_sw128(b0 + 2048 * k, kAwqBLbo, kAwqBSbo);
+            umma<KD>(d0, adesc, bdesc, idesc, (it | k) != 0);
+          }
+          any = true;
+          umma_commit(empty + s);
+          if (++s == kAwqStages) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(tfull + buf);
+      }
+      if (!ok && any) {
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ dequantise
+    // Thread dt owns the 8-column chunk wc = dt % 32 of every row r = dt / 32 + 4 i.
+    const int dt = threadIdx.x - 64;
+    const int wc = dt & 31, r0 = dt >> 5;
+    const int an = wc >> 3, cc = wc & 7;  // 64-column strip and 16-byte chunk within it
+    uint32_t s = 0, ph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      for (int it = 0; it < kblocks; ++it) {
+        if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(sW(s));
+        const uint4* sp = reinterpret_cast<const uint4*>(sS(s));
+        const uint32_t* zp = reinterpret_cast<const uint32_t*>(sZ(s));
+        uint8_t* bp = sB(s);
+        int cur_g = -1;
+        H2 zc[4], sc[4];
+#pragma unroll 4
+        for (int i = 0; i < kAwqBK / 4; ++i) {
+          const int r = r0 + 4 * i;
+          const int gl = group_rows == 1 ? 0 : r / G;  // group row of this k within the block
+          if (gl != cur_g) {
+            cur_g = gl;
+            awq_zero_consts<T>(zp[gl * (kAwqBN / 8) + wc], zc);
+            const uint4 sv = sp[gl * (kAwqBN / 8) + wc];
+            sc[0] = H::from_bits(sv.x);
+            sc[1] = H::from_bits(sv.y);
+            sc[2] = H::from_bits(sv.z);
+            sc[3] = H::from_bits(sv.w);
+          }
+          H2 d[4];
+          awq_word_diff<T>(wp[r * (kAwqBN / 8) + wc], zc, d);
+          uint4 o;
+          o.x = bits_of(__hmul2(d[0], sc[0]));
+          o.y = bits_of(__hmul2(d[1], sc[1]));
+          o.z = bits_of(__hmul2(d[2], sc[2]));
+          o.w = bits_of(__hmul2(d[3], sc[3]));
+          const int rr = r & 7;
+          *reinterpret_cast<uint4*>(bp + an * kAwqBLbo + (r >> 3) * kAwqBSbo + rr * 128 +
+                                    ((cc ^ rr) << 4)) = o;
+        }
+        fence_proxy_async_smem();  // make the generic stores visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bready + s);
+        if (++s == kAwqStages) { s = 0; ph ^= 1; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      const uint32_t aph = (uint32_t)(i >> 1) & 1u;
+      if (!mbar_wait(tfull + buf, aph, abort_flag, err)) break;
+      tc_fence_after();
+      const int mt = t % m_tiles, nt = t / m_tiles;
+      const int row0 = mt * kAwqBM + q * 32;
+      uint8_t* stg = sOut + (size_t)(warp - 6) * (32 * 32 * 2);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kAwqBN; c0 += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kAwqBN + c0);
+        tmem_ld16(taddr, r);
+        tmem_ld16(taddr + 16, r + 16);
+        tmem_ld_wait();
+        if (nt * kAwqBN + c0 >= N) continue;
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float a = __uint_as_float(r[j]), b = __uint_as_float(r[j + 1]);
+          if constexpr (std::is_same<T, __half>::value) {
+            __half2 o = __floats2half2_rn(a, b);
+            pk[j / 2] = bits_of(o);
+          } else {
+            __nv_bfloat162 o = __floats2bfloat162_rn(a, b);
+            pk[j / 2] = bits_of(o);
+          }
+        }
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmY, nt * kAwqBN + c0, row0, stg);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + buf);
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
+template <typename T>
+int launch_awq_gemm(const void* x, const int32_t* qw, const void* s, const int32_t* qz, void* y,
+                    int64_t M, int64_t K, int64_t N, int64_t G, int dtype, cudaStream_t st) {
+  auto kern = k_awq_gemm_sm100<T>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAwqSmem);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "awq tcgen05 gemm: shared memory attribute");
+  const int group_rows = G >= kAwqBK ? 1 : (int)(kAwqBK / G);
+  CUtensorMap tx, tw, ts, tz, ty;
+  int rc = make_tmap_kmajor(&tx, x, M, K, 2, kAwqBM);
+  if (!rc) rc = make_tmap_plain(&tw, qw, K, N / 8, 4, kAwqBN / 8, kAwqBK);
+  if (!rc) rc = make_tmap_plain(&ts, s, K / G, N, 2, kAwqBN, group_rows);
+  if (!rc) rc = make_tmap_plain(&tz, qz, K / G, N / 8, 4, kAwqBN / 8, group_rows);
+  if (!rc) rc = make_tmap_out16(&ty, y, M, N, 32, dtype);
+  if (rc) return rc;
+  const int64_t tiles = ceil_div(M, kAwqBM) * ceil_div(N, kAwqBN);
+  const int grid = (int)std::min<int64_t>(tiles, sm_count());
+  kern<<<grid, kAwqThreads, kAwqSmem, st>>>(tx, tw, ts, tz, ty, (int)M, (int)N, (int)K, (int)G,
+                                            group_rows, device_error_ptr());
+  return check_launch("awq tcgen05 gemm");
+}
+
+}  // namespace
+}  // namespace sm100
+
+// Routes an AWQ GEMM to the tensor-core kernel when the shapes meet its TMA constraints;
+// TO_EUNSUPPORTED (no error recorded) otherwise.
+int awq_gemm_tc_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
+                       cudaStream_t st) {
+  if (s_dtype != TO_F16 && s_dtype != TO_BF16) return TO_EUNSUPPORTED;
+  if (N % 32 != 0 || K % 8 != 0) return TO_EUNSUPPORTED;  // 16-byte TMA row strides
+  if (!(G % 64 == 0 || G == 32 || G == K)) return TO_EUNSUPPORTED;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return TO_EUNSUPPORTED;
+  if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz) || !aligned16(y))
+    return TO_EUNSUPPORTED;
+  if (s_dtype == TO_F16)
+    return sm100::launch_awq_gemm<__half>(x, qw, s, qz, y, M, K, N, G, s_dtype, st);
+  return sm100::launch_awq_gemm<__nv_bfloat16>(x, qw, s, qz, y, M, K, N, G, s_dtype, st);
+}
+
+}  // namespace tob

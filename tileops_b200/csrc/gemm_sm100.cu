@@ -554,6 +554,24 @@ int make_tmap_out16(CUtensorMap* out, const void* ptr, int64_t rows, int64_t col
   return TO_OK;
 }
 
+int make_tmap_plain(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
+                    int box_cols, int box_rows) {
+  EncodeFn encode = get_encode();
+  if (!encode) return fail(TO_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * elem)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(out, elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                      2, const_cast<void*>(ptr), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TO_ECUDA, "cuTensorMapEncodeTiled (plain) failed (%d) for [%lld, %lld] x %d B",
+                (int)r, (long long)rows, (long long)cols, elem);
+  return TO_OK;
+}
+
 template <Kind KD, int BM, int BN, int STAGES>
 int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                     cudaStream_t st) {

@@ -169,6 +169,28 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t addr) {
   return d;
 }
 
+// Shared-memory descriptor of an MN-major tile in the 128-byte-swizzle canonical layout:
+// 1 KB atoms of 8 K-rows x 128 contiguous MN bytes (16-byte chunk c of row r stored at c ^ r),
+// atoms along MN `lbo` bytes apart and 8-row K groups `sbo` bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mnmajor_sw128(uint32_t addr, uint32_t lbo,
+                                                           uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor with explicit operand majors (0 = K-major, 1 = MN-major).
+__host__ __device__ constexpr uint32_t make_idesc_major(uint32_t d_fmt, uint32_t a_fmt,
+                                                        uint32_t b_fmt, int M, int N,
+                                                        uint32_t a_major, uint32_t b_major) {
+  return (d_fmt << 4) | (a_fmt << 7) | (b_fmt << 10) | (a_major << 15) | (b_major << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // Instruction descriptor: dense, K-major A and B.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t d_fmt, uint32_t a_fmt, uint32_t b_fmt,
                                                   int M, int N) {
@@ -177,6 +199,20 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t d_fmt, uint32_t a_fmt
 }
 
 enum class Kind : int { I8 = 0, E4M3 = 1, F16 = 2, BF16 = 3 };
+
+// ------------------------------------------------------------------ host-side tensor maps
+// (defined in gemm_sm100.cu)
+// K-major operand [rows, cols] of `elem`-byte elements as box_rows x 128-byte boxes with the
+// 128-byte swizzle; cached per (pointer, shape, box).
+int make_tmap_kmajor(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
+                     int box_rows);
+// 16-bit output [rows, cols] for staged epilogue stores: 32-row boxes of box_cols columns.
+int make_tmap_out16(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int box_cols,
+                    int dtype);
+// Plain row-major 2-D map without swizzle: box_cols x box_rows elements of `elem` bytes
+// (elem 2 or 4), inner box bytes a multiple of 16.
+int make_tmap_plain(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
+                    int box_cols, int box_rows);
 
 template <Kind K> struct KindTraits;
 template <> struct KindTraits<Kind::I8> {
