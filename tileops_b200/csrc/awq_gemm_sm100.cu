@@ -2,18 +2,21 @@
 // (tileops/quant_awq.py:112-155) for prefill-sized M.
 //
 // The packed int4 weights never exist in HBM as fp16/bf16: each K block of the weight tile is
-// TMA-loaded packed (0.5 B per weight), expanded in shared memory by four dequantising warps
+// TMA-loaded packed (0.5 B per weight), expanded in shared memory by eight dequantising warps
 // into the exact reference weights T((w - z) * s) (quant_awq.py:104-109), and consumed by
 // tcgen05.mma kind::f16 straight from there.
 //
-// Per CTA (persistent, one per SM, 320 threads), tile 128 (M) x 256 (N), K blocks of 64:
-//   warp 0     TMA producer: x tile [128 x 64] (K-major, 128B swizzle), packed weights
-//              [64 rows x 32 words], the block's scale and zero rows          -> full[s]
-//   warps 2-5  dequantise: one packed word (8 columns at one k) -> one 16-byte store into the
-//              B operand, MN-major with the 128-byte swizzle                  -> bready[s]
-//   warp 1     MMA: 4 x tcgen05.mma (K = 16 each), A K-major, B MN-major     -> empty[s], tfull
-//   warps 6-9  epilogue: TMEM -> bf16/fp16 -> 64B-swizzled staging -> TMA store -> tempty
-// Accumulators are double-buffered in TMEM (2 x 256 columns). Waits are bounded (sm100.cuh).
+// Per CTA (persistent, one per SM, 448 threads), tile 128 (M) x 256 (N), K blocks of 64:
+//   warp 0      TMA producer, 5-deep ring: x tile [128 x 64] (K-major, 128B swizzle), packed
+//               weights [64 rows x 32 words], the block's scale and zero rows   -> full[s]
+//   warps 2-9   dequantise into one of two B buffers: one packed word (8 columns at one k) ->
+//               one 16-byte store, MN-major with the 128-byte swizzle          -> bready[b]
+//   warp 1      MMA: 4 x tcgen05.mma (K = 16 each), A K-major, B MN-major
+//               -> empty[s] (ring slot), bfree[b] (B buffer), tfull (tile done)
+//   warps 10-13 epilogue: TMEM -> bf16/fp16 -> 64B-swizzled staging -> TMA store -> tempty
+// The deep TMA ring hides load latency; the separate B buffers let dequantisation of block
+// k+1 overlap the MMAs of block k. Accumulators are double-buffered in TMEM (2 x 256 columns).
+// Waits are bounded (sm100.cuh).
 #include <string.h>
 
 #include <mutex>
@@ -25,17 +28,22 @@ namespace tob {
 namespace sm100 {
 namespace {
 
-constexpr int kAwqBM = 128, kAwqBN = 256, kAwqBK = 64, kAwqStages = 3;
-constexpr int kAwqThreads = 320;
+constexpr int kAwqBM = 128, kAwqBN = 256, kAwqBK = 64;
+constexpr int kAwqStages = 5;   // TMA ring: x tile + packed weights + scale/zero rows
+constexpr int kAwqBBufs = 2;    // dequantised B tiles
+constexpr int kAwqDqWarps = 8;  // dequantising warps
+constexpr int kAwqThreads = 64 + 32 * kAwqDqWarps + 128;
+constexpr int kAwqEpiWarp0 = 2 + kAwqDqWarps;
 constexpr int kAwqABytes = kAwqBM * 128;          // 16 KB x tile
 constexpr int kAwqWBytes = kAwqBK * kAwqBN / 2;   // 8 KB packed weights (64 rows x 32 words)
 constexpr int kAwqBBytes = kAwqBK * kAwqBN * 2;   // 32 KB dequantised weights
 constexpr int kAwqSBytes = 2 * kAwqBN * 2;        // up to 2 scale rows (group 32)
 constexpr int kAwqZBytes = 2 * (kAwqBN / 8) * 4;  // up to 2 zero rows
 constexpr int kAwqSZBytes = 2048;                 // scales + zeros, padded
-constexpr int kAwqStageBytes = kAwqABytes + kAwqWBytes + kAwqBBytes + kAwqSZBytes;
+constexpr int kAwqStageBytes = kAwqABytes + kAwqWBytes + kAwqSZBytes;
 constexpr int kAwqOutBytes = 4 * 32 * 32 * 2;     // 4 epilogue warps x one 32 x 32 slab
-constexpr size_t kAwqSmem = (size_t)kAwqStages * kAwqStageBytes + kAwqOutBytes + 256;
+constexpr size_t kAwqSmem =
+    (size_t)kAwqStages * kAwqStageBytes + (size_t)kAwqBBufs * kAwqBBytes + kAwqOutBytes + 256;
 static_assert(kAwqSBytes + kAwqZBytes <= kAwqSZBytes, "scale/zero area");
 static_assert(kAwqSmem <= 232448, "shared memory");
 // B operand layout (MN-major, 128B swizzle): 1 KB atoms of 8 k-rows x 64 columns; the 8 atoms
@@ -59,22 +67,22 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* stage0 = smem_raw;
-  uint8_t* sOut = smem_raw + (size_t)kAwqStages * kAwqStageBytes;
+  uint8_t* bbase = smem_raw + (size_t)kAwqStages * kAwqStageBytes;
+  uint8_t* sOut = bbase + (size_t)kAwqBBufs * kAwqBBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kAwqOutBytes);
-  uint64_t* bready = full + kAwqStages;
-  uint64_t* empty = bready + kAwqStages;
-  uint64_t* tfull = empty + kAwqStages;
+  uint64_t* empty = full + kAwqStages;
+  uint64_t* bready = empty + kAwqStages;
+  uint64_t* bfree = bready + kAwqBBufs;
+  uint64_t* tfull = bfree + kAwqBBufs;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   auto sA = [&](int s) { return stage0 + (size_t)s * kAwqStageBytes; };
   auto sW = [&](int s) { return stage0 + (size_t)s * kAwqStageBytes + kAwqABytes; };
-  auto sB = [&](int s) { return stage0 + (size_t)s * kAwqStageBytes + kAwqABytes + kAwqWBytes; };
-  auto sS = [&](int s) {
-    return stage0 + (size_t)s * kAwqStageBytes + kAwqABytes + kAwqWBytes + kAwqBBytes;
-  };
+  auto sS = [&](int s) { return stage0 + (size_t)s * kAwqStageBytes + kAwqABytes + kAwqWBytes; };
   auto sZ = [&](int s) { return sS(s) + kAwqSBytes; };
+  auto sB = [&](int b) { return bbase + (size_t)b * kAwqBBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (M + kAwqBM - 1) / kAwqBM, n_tiles = (N + kAwqBN - 1) / kAwqBN;
@@ -85,8 +93,11 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAwqStages; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(bready + s, 4);
       mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < kAwqBBufs; ++b) {
+      mbar_init(bready + b, kAwqDqWarps);
+      mbar_init(bfree + b, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull + b, 1);
@@ -148,7 +159,7 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc =
           make_idesc_major(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, kAwqBM, kAwqBN, 0, 1);
-      uint32_t s = 0, ph = 0;
+      uint32_t s = 0, ph = 0, bb = 0, bph = 0;
       int i = 0;
       bool ok = true, any = false;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++i) {
@@ -159,12 +170,12 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
         const uint32_t d0 = tmem + (uint32_t)(buf * kAwqBN);
         for (int it = 0; it < kblocks; ++it) {
           if (!mbar_wait(full + s, ph, abort_flag, err) ||
-              !mbar_wait(bready + s, ph, abort_flag, err)) {
+              !mbar_wait(bready + bb, bph, abort_flag, err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
+          const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(bb));
 #pragma unroll
           for (int k = 0; k < kAwqBK / 16; ++k) {
             const uint64_t adesc = smem_desc_kmajor_sw128(a0 + 32 * k);
@@ -173,7 +184,9 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
           }
           any = true;
           umma_commit(empty + s);
+          umma_commit(bfree + bb);
           if (++s == kAwqStages) { s = 0; ph ^= 1; }
+          if (++bb == kAwqBBufs) { bb = 0; bph ^= 1; }
         }
         if (!ok) break;
         umma_commit(tfull + buf);
@@ -185,51 +198,86 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
         }
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < kAwqEpiWarp0) {
     // ------------------------------------------------------------ dequantise
-    // Thread dt owns the 8-column chunk wc = dt % 32 of every row r = dt / 32 + 4 i.
+    // Thread dt owns the 8-column chunk wc = dt % 32 of every row r = dt / 32 + 8 i.
+    constexpr int kRowStep = kAwqDqWarps;
     const int dt = threadIdx.x - 64;
     const int wc = dt & 31, r0 = dt >> 5;
     const int an = wc >> 3, cc = wc & 7;  // 64-column strip and 16-byte chunk within it
-    uint32_t s = 0, ph = 0;
+    uint32_t s = 0, ph = 0, bb = 0, bph = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
       for (int it = 0; it < kblocks; ++it) {
-        if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
+        if (!mbar_wait(full + s, ph, abort_flag, err) ||
+            !mbar_wait(bfree + bb, bph ^ 1, abort_flag, err)) {
+          ok = false;
+          break;
+        }
         const uint32_t* wp = reinterpret_cast<const uint32_t*>(sW(s));
         const uint4* sp = reinterpret_cast<const uint4*>(sS(s));
         const uint32_t* zp = reinterpret_cast<const uint32_t*>(sZ(s));
-        uint8_t* bp = sB(s);
-        int cur_g = -1;
-        H2 zc[4], sc[4];
-#pragma unroll 4
-        for (int i = 0; i < kAwqBK / 4; ++i) {
-          const int r = r0 + 4 * i;
-          const int gl = group_rows == 1 ? 0 : r / G;  // group row of this k within the block
-          if (gl != cur_g) {
-            cur_g = gl;
-            awq_zero_consts<T>(zp[gl * (kAwqBN / 8) + wc], zc);
-            const uint4 sv = sp[gl * (kAwqBN / 8) + wc];
-            sc[0] = H::from_bits(sv.x);
-            sc[1] = H::from_bits(sv.y);
-            sc[2] = H::from_bits(sv.z);
-            sc[3] = H::from_bits(sv.w);
+        uint8_t* bp = sB(bb);
+        if (group_rows == 1) {
+          // One quantisation group covers the whole K block: constants once, then every load
+          // of the thread's rows before any arithmetic.
+          H2 zc[4], sc[4];
+          awq_zero_consts<T>(zp[wc], zc);
+          const uint4 sv = sp[wc];
+          sc[0] = H::from_bits(sv.x);
+          sc[1] = H::from_bits(sv.y);
+          sc[2] = H::from_bits(sv.z);
+          sc[3] = H::from_bits(sv.w);
+          uint32_t wv[kAwqBK / kRowStep];
+#pragma unroll
+          for (int i = 0; i < kAwqBK / kRowStep; ++i) wv[i] = wp[(r0 + kRowStep * i) * (kAwqBN / 8) + wc];
+#pragma unroll
+          for (int i = 0; i < kAwqBK / kRowStep; ++i) {
+            const int r = r0 + kRowStep * i;
+            H2 d[4];
+            awq_word_diff<T>(wv[i], zc, d);
+            uint4 o;
+            o.x = bits_of(__hmul2(d[0], sc[0]));
+            o.y = bits_of(__hmul2(d[1], sc[1]));
+            o.z = bits_of(__hmul2(d[2], sc[2]));
+            o.w = bits_of(__hmul2(d[3], sc[3]));
+            const int rr = r & 7;
+            *reinterpret_cast<uint4*>(bp + an * kAwqBLbo + (r >> 3) * kAwqBSbo + rr * 128 +
+                                      ((cc ^ rr) << 4)) = o;
           }
-          H2 d[4];
-          awq_word_diff<T>(wp[r * (kAwqBN / 8) + wc], zc, d);
-          uint4 o;
-          o.x = bits_of(__hmul2(d[0], sc[0]));
-          o.y = bits_of(__hmul2(d[1], sc[1]));
-          o.z = bits_of(__hmul2(d[2], sc[2]));
-          o.w = bits_of(__hmul2(d[3], sc[3]));
-          const int rr = r & 7;
-          *reinterpret_cast<uint4*>(bp + an * kAwqBLbo + (r >> 3) * kAwqBSbo + rr * 128 +
-                                    ((cc ^ rr) << 4)) = o;
+        } else {
+          int cur_g = -1;
+          H2 zc[4], sc[4];
+#pragma unroll
+          for (int i = 0; i < kAwqBK / kRowStep; ++i) {
+            const int r = r0 + kRowStep * i;
+            const int gl = r / G;  // group row of this k within the block
+            if (gl != cur_g) {
+              cur_g = gl;
+              awq_zero_consts<T>(zp[gl * (kAwqBN / 8) + wc], zc);
+              const uint4 sv = sp[gl * (kAwqBN / 8) + wc];
+              sc[0] = H::from_bits(sv.x);
+              sc[1] = H::from_bits(sv.y);
+              sc[2] = H::from_bits(sv.z);
+              sc[3] = H::from_bits(sv.w);
+            }
+            H2 d[4];
+            awq_word_diff<T>(wp[r * (kAwqBN / 8) + wc], zc, d);
+            uint4 o;
+            o.x = bits_of(__hmul2(d[0], sc[0]));
+            o.y = bits_of(__hmul2(d[1], sc[1]));
+            o.z = bits_of(__hmul2(d[2], sc[2]));
+            o.w = bits_of(__hmul2(d[3], sc[3]));
+            const int rr = r & 7;
+            *reinterpret_cast<uint4*>(bp + an * kAwqBLbo + (r >> 3) * kAwqBSbo + rr * 128 +
+                                      ((cc ^ rr) << 4)) = o;
+          }
         }
         fence_proxy_async_smem();  // make the generic stores visible to the tensor core
         __syncwarp();
-        if (lane == 0) mbar_arrive(bready + s);
+        if (lane == 0) mbar_arrive(bready + bb);
         if (++s == kAwqStages) { s = 0; ph ^= 1; }
+        if (++bb == kAwqBBufs) { bb = 0; bph ^= 1; }
       }
     }
   } else {
@@ -243,7 +291,7 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
       tc_fence_after();
       const int mt = t % m_tiles, nt = t / m_tiles;
       const int row0 = mt * kAwqBM + q * 32;
-      uint8_t* stg = sOut + (size_t)(warp - 6) * (32 * 32 * 2);
+      uint8_t* stg = sOut + (size_t)(warp - kAwqEpiWarp0) * (32 * 32 * 2);
 #pragma unroll 1
       for (int c0 = 0; c0 < kAwqBN; c0 += 32) {
         uint32_t r[32];
