@@ -1,25 +1,33 @@
 """Benchmark of the quantized-linear hot path on B200.
 
-Default workload (one step = one pass of the hot path over one batch):
-    INT8 W8A8 layer, M=256 tokens, K=4096, N=11008: int8 activations with per-token fp32
-    scales, int8 weights with per-channel fp32 scales, exact int32 accumulation, bf16 output
-    (tileops.w8a8_block_int8_matmul with block_size=[1, 4096]).
+One step = one pass of the hot path over one batch of synthetic, seeded input. Workloads
+(`--workload`, default `int8`, the configuration the headline metric is quoted on):
+
+  int8         INT8 W8A8 layer M=256 K=4096 N=11008: int8 activations with per-token fp32
+               scales, int8 weights with per-channel fp32 scales, exact int32 accumulation,
+               bf16 out (w8a8_block_int8_matmul, block [1, 4096]). Ranks run independent
+               replicas (weak scaling). HBM-bound: roofline in GB/s.
+  awq_prefill  AWQ W4A16 layer M=2048 K=8192 N=28672 bf16, group 128, output columns sharded
+               over the ranks with an NCCL all-gather of the bf16 output (strong scaling).
+               Tensor-bound: roofline in TFLOP/s.
+  fp8          FP8 layer M=N=K=8192 from bf16: per-token dynamic quantisation of A, tensor-wide
+               quantisation of B, per-token x per-tensor e4m3 GEMM to bf16 (replicas).
+  awq_gemv     AWQ W4A16 decode GEMV x[1, 4096] fp16 @ int4 [4096, 4096], group 128 (replicas).
+  decode       32 layers x {qkv 4096->6144, o 4096->4096, gate_up 4096->28672, down 14336->4096}
+               AWQ int4 group 128, fp16, M tokens (--decode-m, default 16); N-sharded with an
+               all-gather after every linear. HBM GB/s over the weight bytes.
 
 Reported on one JSON line (rank 0):
-  value      device throughput, inputs resident in HBM, CUDA-graph replay of K steps, with a
-             rotating set of weight buffers larger than L2 so every step streams its weights
-             from HBM; TOPS = 2*M*N*K int8 ops / time, summed over ranks (weak scaling: each
-             rank runs its own layer replica; the path has no exchange step in this workload).
-  e2e        the same metric through the public API with host buffers: every step copies the
-             activations and their scales from pinned host memory, runs the layer and copies
-             the bf16 output back (weights stay resident, as in serving).
-  roofline   achieved HBM bandwidth of the GEMM kernel (algorithmic bytes / CUDA-event time)
-             against the measured copy bandwidth in MEASURED_PEAKS.json; traffic = DRAM bytes
-             per launch from the committed ncu summary.
-  cpu_baseline  the reference algorithm (dequantise to fp32, fp32 GEMM) restated on torch
-             CPU tensors, timed on the whole layer on all host cores.
-
---impl reference runs that CPU arm alone on the same metric and config (rank 0 only).
+  value      device throughput of K steps replayed from a CUDA graph, inputs resident in HBM,
+             weights rotated over buffers larger than L2 where a step's working set is smaller
+             than L2; total over ranks; time = max over ranks.
+  e2e        the same metric through the public API with host buffers: each step copies its
+             activations (and their scales) from pinned host memory and reads the output back.
+  roofline   the dominant kernel's algorithmic bytes or FLOPs per launch / its mean duration
+             (CUDA events on its stream, timed in a graph of launches of that kernel alone),
+             against MEASURED_PEAKS.json; traffic = DRAM bytes per launch from profiles/.
+  cpu_baseline  the reference algorithm restated on torch CPU tensors on all host cores.
+`--impl reference` runs that CPU arm alone (rank 0) on the same metric, config and unit.
 Launch: python bench.py [--gpus N --steps K --warmup W]; N>1 under torch.distributed.run.
 """
 
@@ -38,34 +46,27 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-M, K, N = 256, 4096, 11008
 METRIC = "W4A16/W8A8/FP8 GEMM TFLOP/s & GEMV HBM GB/s, % of B200 roofline, 1-8 GPU"
-UNIT = "TOPS"
-OPS = 2 * M * N * K
-# algorithmic bytes per launch: A + B + a_s + b_s + C (bf16)
-BYTES = M * K + N * K + 4 * M + 4 * N + 2 * M * N
-PROFILE = ROOT / "profiles" / "w8a8_int8_m256_k4096_n11008.md"
-WORKLOAD = "int8_w8a8_gemm M=256 K=4096 N=11008 per-token x per-channel scales -> bf16"
 
 
-def peaks() -> tuple[float, str]:
+def measured_peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+            return json.loads(p.read_text()), "measured"
         except Exception:
             pass
-    return 6650.0, "fallback"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def traffic_per_launch():
-    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary, or None."""
-    if not PROFILE.exists():
+def profile_traffic(name: str):
+    """DRAM bytes per launch of a workload's dominant kernel from its committed ncu summary."""
+    path = ROOT / "profiles" / name
+    if not path.exists():
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", PROFILE.read_text())
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", path.read_text())
     return int(m.group(1)) if m else None
 
 
@@ -79,6 +80,7 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.lines: list[str] = []
 
     def __enter__(self):
         try:
@@ -91,7 +93,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -117,70 +118,11 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
-
-
-def make_inputs(device, seed: int, n_weights: int):
-    g = torch.Generator().manual_seed(seed)
-    a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
-    a_s = torch.rand(M, 1, generator=g) * 0.045 + 0.005
-    b_s = torch.rand(N, 1, generator=g) * 0.009 + 0.001
-    weights = []
-    for _ in range(n_weights):
-        b = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
-        weights.append(b.to(device))
-    return a, a_s, weights, b_s.to(device)
-
-
-def cpu_reference(sample_cols: int, threads: int, reps: int = 2):
-    """Times the reference algorithm (fp32 dequant + fp32 GEMM, restated on torch CPU tensors
-    as the reference runs it) on a column sample of the layer; returns (TOPS, s per pass)."""
-    from oracle import int8 as oi8
-
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(1234 + 2)
-    a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
-    b = torch.randint(-127, 128, (sample_cols, K), generator=g, dtype=torch.int8)
-    a_s = torch.rand(M, 1, generator=g) * 0.045 + 0.005
-    b_s = torch.rand(sample_cols, 1, generator=g) * 0.009 + 0.001
-    oi8.block_matmul_reference_cpu_torch(a, b, a_s, b_s, (1, K), torch.bfloat16)  # warm-up
-    times = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        oi8.block_matmul_reference_cpu_torch(a, b, a_s, b_s, (1, K), torch.bfloat16)
-        times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    return 2 * M * sample_cols * K / t / 1e12, t
-
-
-def run_reference_arm(args, rank: int) -> None:
-    if rank != 0:
-        return
-    threads = os.cpu_count() or 1
-    cols = N  # the whole layer per step (about 0.1-0.5 s on a many-core host)
-    vals = []
-    for _ in range(args.warmup):
-        cpu_reference(cols, threads, reps=1)
-    for _ in range(args.steps):
-        v, _ = cpu_reference(cols, threads, reps=1)
-        vals.append(v)
-    value = statistics.median(vals)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic (seeded uniform int8, scales U(0.005,0.05) / U(0.001,0.01))",
-        "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N, "parallelism": "replicas"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"the full layer (N={cols}) per step; torch CPU fp32 dequant + "
-                                   "fp32 GEMM (the reference algorithm)"},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+                "reasons": sorted(reasons)}
 
 
 def graph_of(fn, reps: int):
-    """Captures `reps` calls of fn() into one CUDA graph (after an eager warm-up on a side
+    """Captures `reps` calls of fn(i) into one CUDA graph (after an eager warm-up on a side
     stream, as torch requires)."""
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -194,24 +136,495 @@ def graph_of(fn, reps: int):
     return g
 
 
+def timed_graph_ms(fn, reps: int, warmup: int, dist=None, clock_index=None):
+    """Mean ms per call of fn over a graph of `reps` calls (max over ranks); optionally samples
+    clocks while the GPU is kept busy around the timed replay."""
+    g = graph_of(fn, reps)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(clock_index) if clock_index is not None else None
+    if clk is not None:
+        clk.__enter__()
+        soak = time.perf_counter() + 1.0  # load the GPU so the 100 ms samples see the timed state
+        while time.perf_counter() < soak:
+            g.replay()
+            torch.cuda.synchronize()
+    ev0.record()
+    g.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    if clk is not None:
+        soak = time.perf_counter() + 0.3
+        while time.perf_counter() < soak:
+            g.replay()
+            torch.cuda.synchronize()
+        clk.__exit__(None, None, None)
+    if dist is not None:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del g
+    return ms / reps, (clk.summary() if clk is not None else None)
+
+
+# ====================================================================== workloads
+class Int8Layer:
+    name = "int8"
+    unit = "TOPS"
+    dtype = "int8"
+    bound = "hbm"
+    scaling = "weak"
+    profile = "w8a8_int8_m256_k4096_n11008.md"
+    M, K, N = 256, 4096, 11008
+    data = ("synthetic (seeded uniform int8 in [-127,127]; scales U(0.005,0.05) per token, "
+            "U(0.001,0.01) per channel)")
+    launches_per_step = 1
+
+    def __init__(self, dev, rank, world):
+        import tileops_b200 as tob
+
+        self.tob = tob
+        M, K, N = self.M, self.K, self.N
+        self.kernel_bytes = M * K + N * K + 4 * M + 4 * N + 2 * M * N
+        g = torch.Generator().manual_seed(1234 + 2 + rank)
+        a_cpu = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+        a_s_cpu = torch.rand(M, 1, generator=g) * 0.045 + 0.005
+        self.b_s = (torch.rand(N, 1, generator=g) * 0.009 + 0.001).to(dev)
+        # 6 x 45 MB > 126 MB L2: every step streams its weights from HBM
+        self.weights = [torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(dev)
+                        for _ in range(6)]
+        self.a, self.a_s = a_cpu.to(dev), a_s_cpu.to(dev)
+        self.a_host, self.a_s_host = a_cpu.pin_memory(), a_s_cpu.pin_memory()
+        self.out_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.dev = dev
+
+    def step(self, i):
+        self.tob.w8a8_block_int8_matmul(self.a, self.weights[i % 6], self.a_s, self.b_s,
+                                        [1, self.K], output_dtype=torch.bfloat16)
+
+    kernel_step = step
+
+    def e2e_step(self, i):
+        a = self.a_host.to(self.dev, non_blocking=True)
+        a_s = self.a_s_host.to(self.dev, non_blocking=True)
+        c = self.tob.w8a8_block_int8_matmul(a, self.weights[i % 6], a_s, self.b_s, [1, self.K],
+                                            output_dtype=torch.bfloat16)
+        self.out_host.copy_(c, non_blocking=True)
+
+    def h2d_d2h(self):
+        return self.a_host.numel() + 4 * self.a_s_host.numel(), 2 * self.out_host.numel()
+
+    def total_units(self, world):
+        return world * 2 * self.M * self.N * self.K / 1e12  # tera-ops per step, whole job
+
+    def roofline_units(self):
+        return "hbm", self.kernel_bytes
+
+    def config(self, world):
+        return {"workload": "int8_w8a8_gemm M=256 K=4096 N=11008 per-token x per-channel "
+                            "scales -> bf16", "M": self.M, "K": self.K, "N": self.N,
+                "parallelism": f"replicas x{world}",
+                "l2": "rotating weights: 6 x 45 MB buffers > 126 MB L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        from oracle import int8 as oi8
+
+        torch.set_num_threads(threads)
+        g = torch.Generator().manual_seed(1234 + 2)
+        M, K, N = cls.M, cls.K, cls.N
+        a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+        b = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+        a_s = torch.rand(M, 1, generator=g) * 0.045 + 0.005
+        b_s = torch.rand(N, 1, generator=g) * 0.009 + 0.001
+        run = lambda: oi8.block_matmul_reference_cpu_torch(a, b, a_s, b_s, (1, K), torch.bfloat16)  # noqa: E731
+        return run, 2 * M * N * K / 1e12, ("the full layer per pass; torch CPU fp32 dequant + "
+                                           "fp32 GEMM (reference algorithm)")
+
+
+class AwqPrefill:
+    name = "awq_prefill"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    bound = "tensor"
+    scaling = "strong"
+    profile = "awq_prefill_m2048_k8192_n28672.md"
+    M, K, N, G = 2048, 8192, 28672, 128
+    data = "synthetic (seeded random packed int4 weights and zeros, scales U(0.002,0.02), x N(0,1))"
+    launches_per_step = 1
+
+    def __init__(self, dev, rank, world):
+        import tileops_b200 as tob
+        from tileops_b200 import sharded
+
+        self.tob, self.sharded = tob, sharded
+        M, K, N, G = self.M, self.K, self.N, self.G
+        n_loc = N // world
+        g = torch.Generator().manual_seed(1234 + 3 + 100 * rank)  # this rank's column shard
+        self.qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, n_loc // 8), generator=g,
+                                dtype=torch.int32).to(dev)
+        self.qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // G, n_loc // 8), generator=g,
+                                dtype=torch.int32).to(dev)
+        self.s = (torch.rand(K // G, n_loc, generator=g) * 0.018 + 0.002).bfloat16().to(dev)
+        gx = torch.Generator().manual_seed(1234 + 3)  # the same activations on every rank
+        x_cpu = torch.randn(M, K, generator=gx).bfloat16()
+        self.x = x_cpu.to(dev)
+        self.x_host = x_cpu.pin_memory()
+        self.out_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.flops_per_rank = 2 * M * n_loc * K
+        self.dev, self.world = dev, world
+
+    def _layer(self, x):
+        y = self.tob.awq_gemm(x, self.qw, self.s, self.qz, 1)
+        return self.sharded.gather_columns(y) if self.world > 1 else y
+
+    def step(self, i):
+        self._layer(self.x)
+
+    def kernel_step(self, i):
+        self.tob.awq_gemm(self.x, self.qw, self.s, self.qz, 1)
+
+    def e2e_step(self, i):
+        x = self.x_host.to(self.dev, non_blocking=True)
+        self.out_host.copy_(self._layer(x), non_blocking=True)
+
+    def h2d_d2h(self):
+        return 2 * self.x_host.numel(), 2 * self.out_host.numel()
+
+    def total_units(self, world):
+        return 2 * self.M * self.N * self.K / 1e12  # the whole layer per step
+
+    def roofline_units(self):
+        return "tensor", self.flops_per_rank
+
+    def config(self, world):
+        return {"workload": "awq_w4a16_prefill M=2048 K=8192 N=28672 bf16 group 128, output "
+                            "columns sharded over ranks + NCCL all-gather",
+                "M": self.M, "K": self.K, "N": self.N, "group_size": self.G,
+                "parallelism": f"tp{world} (N-sharded)",
+                "l2": "per step 117 MB of bf16 output plus weights and activations > L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        from oracle import awq as oawq
+
+        torch.set_num_threads(threads)
+        M, K, G = cls.M, cls.K, cls.G
+        n = 1792  # one 16th of the output columns per pass
+        g = torch.Generator().manual_seed(1234 + 3)
+        x = torch.randn(M, K, generator=g).bfloat16()
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, n // 8), generator=g, dtype=torch.int32)
+        qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // G, n // 8), generator=g, dtype=torch.int32)
+        s = (torch.rand(K // G, n, generator=g) * 0.018 + 0.002).bfloat16()
+        run = lambda: oawq.gemm_reference_cpu_torch(x, qw, s, qz, G)  # noqa: E731
+        return run, 2 * M * n * K / 1e12, ("N=1792 of 28672 columns per pass (full M, K); torch "
+                                           "CPU int64 unpack + dequant + bf16 matmul (reference "
+                                           "algorithm)")
+
+
+class Fp8Layer:
+    name = "fp8"
+    unit = "TFLOP/s"
+    dtype = "e4m3"
+    bound = "tensor"
+    scaling = "weak"
+    profile = "fp8_m8192_n8192_k8192.md"
+    M = N = K = 8192
+    data = "synthetic (seeded bf16 N(0,1))"
+    launches_per_step = 4  # group quant, amax, tensor quant, GEMM
+
+    def __init__(self, dev, rank, world):
+        import tileops_b200 as tob
+
+        self.tob = tob
+        g = torch.Generator().manual_seed(1234 + 4 + rank)
+        A_cpu = torch.randn(self.M, self.K, generator=g).bfloat16()
+        self.B = torch.randn(self.N, self.K, generator=g).bfloat16().to(dev)
+        self.A = A_cpu.to(dev)
+        self.A_host = A_cpu.pin_memory()
+        self.out_host = torch.empty(self.M, self.N, dtype=torch.bfloat16).pin_memory()
+        self.dev = dev
+        self.flops = 2 * self.M * self.N * self.K
+        qa, sa = tob.per_token_group_quant_fp8(self.A, self.K)
+        qb, sb = tob.input_to_float8(self.B)
+        self.qa, self.sa, self.qb, self.sb = qa, sa, qb, sb.reshape(1, 1)
+
+    def _layer(self, A):
+        qa, sa = self.tob.per_token_group_quant_fp8(A, self.K)
+        qb, sb = self.tob.input_to_float8(self.B)
+        return self.tob.w8a8_block_fp8_matmul(qa, qb, sa, sb.reshape(1, 1), [self.N, self.K],
+                                              output_dtype=torch.bfloat16)
+
+    def step(self, i):
+        self._layer(self.A)
+
+    def kernel_step(self, i):
+        self.tob.w8a8_block_fp8_matmul(self.qa, self.qb, self.sa, self.sb, [self.N, self.K],
+                                       output_dtype=torch.bfloat16)
+
+    def e2e_step(self, i):
+        A = self.A_host.to(self.dev, non_blocking=True)
+        self.out_host.copy_(self._layer(A), non_blocking=True)
+
+    def h2d_d2h(self):
+        return 2 * self.A_host.numel(), 2 * self.out_host.numel()
+
+    def total_units(self, world):
+        return world * self.flops / 1e12
+
+    def roofline_units(self):
+        return "tensor", self.flops
+
+    def config(self, world):
+        return {"workload": "fp8_e4m3 layer M=N=K=8192: per-token dynamic quant of A, "
+                            "tensor-wide quant of B, scaled GEMM -> bf16",
+                "M": self.M, "N": self.N, "K": self.K, "parallelism": f"replicas x{world}",
+                "l2": "A, B, their fp8 copies and the output are 512 MB per step > L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        from oracle import fp8 as ofp8
+
+        torch.set_num_threads(threads)
+        m = 512  # 512 of the 8192 rows of A per pass (B quantised in full)
+        g = torch.Generator().manual_seed(1234 + 4)
+        A = torch.randn(m, cls.K, generator=g).bfloat16()
+        B = torch.randn(cls.N, cls.K, generator=g).bfloat16()
+        run = lambda: ofp8.layer_reference_cpu_torch(A, B)  # noqa: E731
+        return run, 2 * m * cls.N * cls.K / 1e12, ("M=512 of 8192 rows per pass (full N, K; B "
+                                                   "quantised in full); torch CPU quantise + fp32 "
+                                                   "dequant GEMM (reference algorithm)")
+
+
+class AwqGemv:
+    name = "awq_gemv"
+    unit = "GB/s"
+    dtype = "f16"
+    bound = "hbm"
+    scaling = "weak"
+    profile = "awq_gemv_k4096_n4096.md"
+    K, N, G = 4096, 4096, 128
+    SETS = 48  # 48 x 8.7 MB > L2
+    data = "synthetic (seeded random packed int4, scales U(0.002,0.02), x N(0,1))"
+    launches_per_step = 1
+
+    def __init__(self, dev, rank, world):
+        import tileops_b200 as tob
+
+        self.tob = tob
+        K, N, G = self.K, self.N, self.G
+        g = torch.Generator().manual_seed(1234 + 1 + rank)
+        self.sets = []
+        for _ in range(self.SETS):
+            qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, N // 8), generator=g, dtype=torch.int32)
+            qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // G, N // 8), generator=g, dtype=torch.int32)
+            s = (torch.rand(K // G, N, generator=g) * 0.018 + 0.002).half()
+            self.sets.append((qw.to(dev), s.to(dev), qz.to(dev)))
+        x_cpu = torch.randn(1, K, generator=g).half()
+        self.x = x_cpu.to(dev)
+        self.x_host = x_cpu.pin_memory()
+        self.out_host = torch.empty(1, N, dtype=torch.float16).pin_memory()
+        self.dev = dev
+        self.kernel_bytes = K * N // 2 + (K // G) * N * 2 + (K // G) * N // 2 + 2 * K + 2 * N
+
+    def step(self, i):
+        qw, s, qz = self.sets[i % self.SETS]
+        self.tob.awq_gemm(self.x, qw, s, qz, 1)
+
+    kernel_step = step
+
+    def e2e_step(self, i):
+        qw, s, qz = self.sets[i % self.SETS]
+        x = self.x_host.to(self.dev, non_blocking=True)
+        self.out_host.copy_(self.tob.awq_gemm(x, qw, s, qz, 1), non_blocking=True)
+
+    def h2d_d2h(self):
+        return 2 * self.K, 2 * self.N
+
+    def total_units(self, world):
+        return world * self.kernel_bytes / 1e9  # GB per step, whole job
+
+    def roofline_units(self):
+        return "hbm", self.kernel_bytes
+
+    def config(self, world):
+        return {"workload": "awq_w4a16_gemv x[1,4096] fp16 @ int4 [4096,4096] group 128",
+                "M": 1, "K": self.K, "N": self.N, "group_size": self.G,
+                "parallelism": f"replicas x{world}",
+                "l2": "48 rotating weight sets x 8.7 MB > L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        from oracle import awq as oawq
+
+        torch.set_num_threads(threads)
+        K, N, G = cls.K, cls.N, cls.G
+        g = torch.Generator().manual_seed(1234 + 1)
+        x = torch.randn(1, K, generator=g).half()
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, N // 8), generator=g, dtype=torch.int32)
+        qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // G, N // 8), generator=g, dtype=torch.int32)
+        s = (torch.rand(K // G, N, generator=g) * 0.018 + 0.002).half()
+        byts = K * N // 2 + (K // G) * N * 2 + (K // G) * N // 2 + 2 * K + 2 * N
+        run = lambda: oawq.gemm_reference_cpu_torch(x, qw, s, qz, G)  # noqa: E731
+        return run, byts / 1e9, ("the full GEMV per pass; torch CPU int64 unpack + dequant + fp16 "
+                                 "matmul (reference algorithm)")
+
+
+class Decode:
+    name = "decode"
+    unit = "GB/s"
+    dtype = "f16"
+    bound = "hbm"
+    scaling = "strong"
+    profile = "awq_decode_step.md"
+    LAYERS = 32
+    SHAPES = [(4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096)]  # (K, N) per linear
+    G = 128
+    data = "synthetic (seeded random packed int4 weights, scales U(0.002,0.02), x N(0,1))"
+    launches_per_step = 128
+
+    def __init__(self, dev, rank, world, m=16):
+        import tileops_b200 as tob
+        from tileops_b200 import sharded
+
+        self.tob, self.sharded, self.world, self.dev, self.m = tob, sharded, world, dev, m
+        g = torch.Generator().manual_seed(1234 + 5 + 100 * rank)
+        self.layers = []
+        for _ in range(self.LAYERS):
+            lins = []
+            for (k, n) in self.SHAPES:
+                nl = n // world
+                qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k, nl // 8), generator=g, dtype=torch.int32)
+                qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k // self.G, nl // 8), generator=g,
+                                   dtype=torch.int32)
+                s = (torch.rand(k // self.G, nl, generator=g) * 0.018 + 0.002).half()
+                lins.append((qw.to(dev), s.to(dev), qz.to(dev)))
+            self.layers.append(lins)
+        gx = torch.Generator().manual_seed(1234 + 5)
+        x_cpu = torch.randn(m, 4096, generator=gx).half()
+        self.x = x_cpu.to(dev)
+        self.x_host = x_cpu.pin_memory()
+        self.out_host = torch.empty(m, 4096, dtype=torch.float16).pin_memory()
+        self.weight_bytes = self.LAYERS * sum(
+            k * n // 2 + (k // self.G) * n * 2 + (k // self.G) * n // 2 for k, n in self.SHAPES)
+
+    def _run(self, x):
+        gather = self.sharded.gather_columns if self.world > 1 else (lambda y: y)
+        for qkv, o, gu, down in self.layers:
+            h = gather(self.tob.awq_gemm(x, *qkv, 1))
+            a = gather(self.tob.awq_gemm(h[:, :4096].contiguous(), *o, 1))
+            u = gather(self.tob.awq_gemm(a, *gu, 1))
+            x = gather(self.tob.awq_gemm(u[:, :14336].contiguous(), *down, 1))
+        return x
+
+    def step(self, i):
+        self._run(self.x)
+
+    kernel_step = step
+
+    def e2e_step(self, i):
+        x = self.x_host.to(self.dev, non_blocking=True)
+        self.out_host.copy_(self._run(x), non_blocking=True)
+
+    def h2d_d2h(self):
+        return 2 * self.x_host.numel(), 2 * self.out_host.numel()
+
+    def total_units(self, world):
+        return self.weight_bytes / 1e9  # GB of weights streamed per step, whole job
+
+    def roofline_units(self):
+        return "hbm", self.weight_bytes / self.world
+
+    def config(self, world):
+        return {"workload": f"awq decode step, 32 layers x 4 linears (8B-class), M={self.m} fp16, "
+                            "group 128, N-sharded + all-gather per linear",
+                "M": self.m, "layers": self.LAYERS, "parallelism": f"tp{world} (N-sharded)",
+                "l2": "3.6 GB of weights per step > L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        from oracle import awq as oawq
+
+        torch.set_num_threads(threads)
+        k, n, G = 4096, 4096, cls.G  # one o-projection linear per pass, M=16
+        g = torch.Generator().manual_seed(1234 + 5)
+        x = torch.randn(16, k, generator=g).half()
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k, n // 8), generator=g, dtype=torch.int32)
+        qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k // G, n // 8), generator=g, dtype=torch.int32)
+        s = (torch.rand(k // G, n, generator=g) * 0.018 + 0.002).half()
+        byts = k * n // 2 + (k // G) * n * 2 + (k // G) * n // 2
+        run = lambda: oawq.gemm_reference_cpu_torch(x, qw, s, qz, G)  # noqa: E731
+        return run, byts / 1e9, ("one 4096x4096 linear (M=16) of the 128 per step per pass; "
+                                 "torch CPU reference algorithm")
+
+
+WORKLOADS = {c.name: c for c in (Int8Layer, AwqPrefill, Fp8Layer, AwqGemv, Decode)}
+
+
+def time_cpu(workload_cls, reps: int):
+    threads = os.cpu_count() or 1
+    run, units, sample = workload_cls.cpu_reference(threads)
+    run()  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return units / t, t, threads, sample
+
+
+def run_reference_arm(args, rank: int, wl) -> None:
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        time_cpu(wl, 1)
+    vals, secs = [], []
+    cores, sample = os.cpu_count(), ""
+    for _ in range(args.steps):
+        v, t, cores, sample = time_cpu(wl, 1)
+        vals.append(v)
+        secs.append(t)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": wl.unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
+        "data": wl.data, "config": {"workload": wl.name, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": cores, "kind": "port",
+                         "sample": f"{sample}; median {statistics.median(secs):.3f} s per pass"},
+        "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="int8", choices=sorted(WORKLOADS))
+    ap.add_argument("--decode-m", type=int, default=16)
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+    args.warmup = max(args.warmup, 3)
+    wl_cls = WORKLOADS[args.workload]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference_arm(args, rank)
+        run_reference_arm(args, rank, wl_cls)
         return 0
 
-    import tileops_b200 as tob
     from tileops_b200 import _lib
 
     torch.cuda.set_device(local)
@@ -222,80 +635,29 @@ def main() -> int:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    # Rotating weights: 6 x 45 MB > 126 MB L2, so every step streams its weights from HBM.
-    n_w = 6
-    a_cpu, a_s_cpu, weights, b_s = make_inputs(dev, 1234 + 2 + rank, n_w)
-    a = a_cpu.to(dev)
-    a_s = a_s_cpu.to(dev)
-    outs = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for _ in range(n_w)]
-
-    def step(i):
-        outs[i % n_w] = tob.w8a8_block_int8_matmul(a, weights[i % n_w], a_s, b_s, [1, K],
-                                                   output_dtype=torch.bfloat16)
-
-    # correctness spot check of this configuration against the int32-exact oracle (one row)
-    step(0)
+    wl = wl_cls(dev, rank, world, args.decode_m) if wl_cls is Decode else wl_cls(dev, rank, world)
+    wl.step(0)  # first call: tensor maps, kernel attributes, NCCL communicator
     torch.cuda.synchronize()
 
-    # ---------------- device throughput (graph of K steps, inputs resident)
-    g = graph_of(step, args.steps)
-    for _ in range(args.warmup):
-        g.replay()
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        # Keep the GPU busy with untimed replays for ~1 s around the timed region so the
-        # 100 ms clock samples land under the same load as the K timed steps.
-        soak_until = time.perf_counter() + 1.0
-        while time.perf_counter() < soak_until:
-            g.replay()
-            torch.cuda.synchronize()
-        ev0.record()
-        g.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-        soak_until = time.perf_counter() + 0.3
-        while time.perf_counter() < soak_until:
-            g.replay()
-            torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    ms = ev0.elapsed_time(ev1)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_per_step = ms / args.steps
-    value = world * OPS / (ms_per_step * 1e-3) / 1e12
-    del g
+    # ---------------- device throughput: K steps from one CUDA graph, inputs resident
+    ms_step, clocks = timed_graph_ms(wl.step, args.steps, args.warmup, dist, clock_index=local)
+    value = wl.total_units(world) / (ms_step * 1e-3)
+
+    # ---------------- the dominant kernel alone (roofline)
+    k_ms, _ = timed_graph_ms(wl.kernel_step, min(args.steps, 60), args.warmup, dist)
 
     # ---------------- end to end through the public API with host buffers
-    a_host = a_cpu.pin_memory()
-    a_s_host = a_s_cpu.pin_memory()
-    out_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
-
-    def e2e_step(i):
-        a_d = a_host.to(dev, non_blocking=True)
-        a_s_d = a_s_host.to(dev, non_blocking=True)
-        c = tob.w8a8_block_int8_matmul(a_d, weights[i % n_w], a_s_d, b_s, [1, K],
-                                       output_dtype=torch.bfloat16)
-        out_host.copy_(c, non_blocking=True)
-
     for i in range(args.warmup):
-        e2e_step(i)
+        wl.e2e_step(i)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(args.steps):
-        e2e_step(i)
+        wl.e2e_step(i)
     e1.record()
     torch.cuda.synchronize()
     e_ms = e0.elapsed_time(e1)
@@ -303,37 +665,39 @@ def main() -> int:
         t = torch.tensor([e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
-    e2e_value = world * OPS / (e_ms / args.steps * 1e-3) / 1e12
+    e2e_value = wl.total_units(world) / (e_ms / args.steps * 1e-3)
     assert _lib.device_error_word() == 0
 
     if rank == 0:
-        peak, peak_kind = peaks()
-        achieved = BYTES / (ms_per_step * 1e-3) / 1e9
-        cpu_v, cpu_t = cpu_reference(N, os.cpu_count() or 1, reps=5)
-        clocks = clk.summary()
+        peaks, peak_kind = measured_peaks()
+        bound, per_launch = wl.roofline_units()
+        if bound == "hbm":
+            achieved = per_launch / (k_ms * 1e-3) / 1e9
+            peak, unit, peak_note = float(peaks["hbm_gbs"]), "GB/s", peak_kind
+        else:
+            achieved = per_launch / (k_ms * 1e-3) / 1e12
+            unit = "TFLOP/s"
+            peak = float(peaks["bf16_tflops"])
+            peak_note = peak_kind + " bf16 burst"
+            if wl.name == "fp8":  # dense e4m3 runs at twice the bf16 rate
+                peak, peak_note = 2 * peak, peak_kind + " bf16 burst x2 (e4m3)"
+        cpu_v, cpu_t, cores, sample = time_cpu(wl_cls, 3)
+        h2d, d2h = wl.h2d_d2h()
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (seeded uniform int8 in [-127,127]; scales U(0.005,0.05) per "
-                    "token, U(0.001,0.01) per channel)",
-            "config": {"workload": WORKLOAD, "M": M, "K": K, "N": N,
-                       "parallelism": f"replicas x{world}",
-                       "l2": "rotating weights: 6 x 45 MB buffers > 126 MB L2"},
-            "e2e": {"value": e2e_value, "unit": UNIT,
-                    "h2d_bytes_per_step": a_host.numel() + 4 * a_s_host.numel(),
-                    "d2h_bytes_per_step": 2 * out_host.numel()},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic_per_launch(),
-                         "peak_source": peak_kind,
-                         "algorithmic_bytes_per_launch": BYTES},
-            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": os.cpu_count(),
-                             "kind": "port",
-                             "sample": f"the full layer, median of 5 passes of {cpu_t:.3f} s; "
-                                       "torch CPU fp32 dequant + fp32 GEMM (reference algorithm)"},
-            "gpu_launches": args.steps,
-            "clocks": {"sm_mhz": clocks["sm_mhz"], "sm_max_mhz": clocks["sm_max_mhz"],
-                       "reasons": clocks["reasons"]},
+            "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
+            "dtype": wl.dtype, "data": wl.data, "config": wl.config(world),
+            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                         "frac": achieved / peak, "traffic": profile_traffic(wl.profile),
+                         "peak_source": peak_note, "kernel_ms": k_ms,
+                         "algorithmic_per_launch": per_launch},
+            "cpu_baseline": {"value": cpu_v, "unit": wl.unit, "cores": cores, "kind": "port",
+                             "sample": f"{sample}; median {cpu_t:.3f} s per pass"},
+            "gpu_launches": args.steps * wl.launches_per_step,
+            "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:

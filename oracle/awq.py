@@ -59,3 +59,23 @@ def gemm_reference_cpu(x_f32, qweight, scales_f32, qzeros, dtype: str) -> np.nda
     rnd = rounder(dtype)
     w = dequant(qweight, scales_f32, qzeros, dtype)
     return rnd(rnd(np.asarray(x_f32, dtype=np.float32)) @ w)
+
+
+def gemm_reference_cpu_torch(x, qweight, scales, qzeros, group_size):
+    """The reference algorithm (quant_awq.py:41-52, 104-109, 153-155: int64 unpack of both
+    packed tensors, per-row gathers of zeros and scales, (w - z) * s in scales.dtype, then a
+    matmul in scales.dtype) restated on torch CPU tensors; timed as the CPU baseline."""
+    import torch
+
+    def unpack(p):
+        w = p.to(torch.int64)
+        pieces = [(w >> (4 * sh)) & 0xF for sh in REVERSE_AWQ_ORDER]
+        return torch.stack(pieces, dim=-1).reshape(*p.shape[:-1], p.shape[-1] * 8)
+
+    sd = scales.dtype
+    k = qweight.shape[0]
+    w = unpack(qweight).to(sd)
+    z = unpack(qzeros).to(sd)
+    gidx = torch.arange(k) // group_size
+    weight = (w - z[gidx]) * scales[gidx]
+    return x.to(sd) @ weight

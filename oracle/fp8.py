@@ -86,3 +86,22 @@ def block_matmul_reference_cpu(a_codes, b_codes, a_s, b_s, block_size, out_dtype
     a_f = e4m3_to_f32(a_codes) * np.asarray(a_s, np.float32)[:, cols]
     b_f = block_dequant(b_codes, b_s, block_size)
     return rounder(out_dtype)(a_f @ b_f.T)
+
+
+def layer_reference_cpu_torch(A, B):
+    """The reference algorithm of the dynamic-FP8 layer on torch CPU tensors, timed as the CPU
+    baseline: per-token quantisation of A (quant_fp8.py:66-80), tensor-wide quantisation of B
+    (quant_fp8.py:52-63), then fp32 dequant of both and an fp32 GEMM cast to bf16
+    (quant_fp8.py:231-236)."""
+    import torch
+
+    fp8 = torch.float8_e4m3fn
+    a_f = A.float()
+    a_scale = a_f.abs().amax(dim=-1, keepdim=True).clamp(min=1e-10) / FP8_MAX
+    qa = (a_f / a_scale).clamp(-FP8_MAX, FP8_MAX).to(fp8)
+    amax = B.abs().amax().clamp(min=1e-12)
+    b_scale = amax.reciprocal() * FP8_MAX
+    qb = (B * b_scale).clamp(-FP8_MAX, FP8_MAX).to(fp8)
+    a_deq = qa.float() * a_scale
+    b_deq = qb.float() * b_scale.float().reciprocal()
+    return (a_deq @ b_deq.T).to(torch.bfloat16)
