@@ -62,6 +62,14 @@ TO_API int to_device_check(int device);
 /* Reads (and with clear != 0 resets) the device-side error word that kernels with bounded
  * waits set when a wait gives up: 0 = no error. Synchronises the current device. */
 TO_API int to_device_error_word(int* value, int clear);
+/* Launch overlap for the streaming small-M AWQ kernel (programmatic dependent launch): with
+ * enable = 1, a launch may start reading its weights, zeros and scales while the previous
+ * kernel in the stream is still running; x is read and y written only after that kernel has
+ * completed. Use it for chains of layers whose weights no kernel in the stream writes (a
+ * decode loop); leave it off (the default) when a kernel that writes the weights, such as
+ * to_awq_pack, may be the immediately preceding launch. enable < 0 only queries. Returns the
+ * previous setting. Process-wide. No reference counterpart (a launch-policy extension). */
+TO_API int to_set_launch_overlap(int enable);
 
 /* ---- symmetric INT8 (tileops/quant.py) ------------------------------------------------
  * q = clamp(round_half_even(float(x) / scale), -128, 127);  y = out_dtype(float(q) * scale).

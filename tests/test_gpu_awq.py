@@ -140,3 +140,78 @@ def test_gemm_deterministic(cuda):
     y0 = tob.awq_gemm(*args)
     for _ in range(3):
         assert torch.equal(tob.awq_gemm(*args), y0)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("m,k,n,g", [
+    # TMA-fed register-MMA kernel (3 <= M <= 32, N % 32 == 0, K % 64 == 0)
+    (3, 4096, 28672, 128),    # 32-word column tiles, K split 4
+    (4, 14336, 4096, 128),    # long K: the stage ring wraps, K split 8
+    (8, 4096, 4096, 64),      # one full 8-token tile
+    (9, 2048, 1024, 128),     # two token tiles, 7 of the second padded
+    (16, 1024, 2048, 32),     # group size 32: several group rows per stage
+    (24, 512, 512, 512),      # four token tiles, G == K
+    (32, 1024, 4096, 128),    # the largest M it takes
+    (5, 256, 96, 256),        # 12 words: a partial column tile, G == K
+    # prefetching SIMT stream (M <= 2, and shapes the TMA kernel does not take)
+    (1, 4096, 28672, 128),    # 32-word column tiles
+    (2, 14336, 4096, 128),    # several row blocks per warp
+    (3, 1000, 256, 1000),     # K % 64 != 0, K tail inside the last row block
+    (2, 100, 64, 100),        # K not a multiple of 8 (scalar x staging), G == K
+    (1, 64, 16, 32),          # N = 16: 2 words per row
+    (4, 2048, 4112, 64),      # N % 32 != 0: a partial 16-word column tile
+    # general streaming kernel (M > 4 on shapes the TMA kernel does not take)
+    (6, 200, 96, 200),
+])
+def test_gemv_small_m_vs_oracle(cuda, dtype, m, k, n, g):
+    """The small-M kernels over their tile, token-tile, K-split, group and tail cases."""
+    gen = torch.Generator().manual_seed(m * 7 + k + 3 * n)
+    qw, s, qz = make_awq(k, n, g, _DT[dtype], gen)
+    x = torch.randn(m, k, generator=gen).to(_DT[dtype])
+    y = tob.awq_gemm(x.to(cuda), qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    want = oawq.gemm(x.float().numpy(), qw.numpy(), s.float().numpy(), qz.numpy(), dtype)
+    np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+
+
+def test_gemv_launch_overlap_chain(cuda):
+    """A chain of dependent small-M calls (each output is the next input) gives bit-identical
+    results with launch overlap on and off, eagerly and replayed from a CUDA graph."""
+    gen = torch.Generator().manual_seed(21)
+    dims = [4096, 2048, 4096, 1024, 4096]
+    layers = []
+    for k, n in zip(dims[:-1], dims[1:]):
+        qw, s, qz = make_awq(k, n, 128, torch.float16, gen, lo=0.0005, hi=0.002)
+        layers.append((qw.to(cuda), s.to(cuda), qz.to(cuda)))
+    x = torch.randn(2, dims[0], generator=gen).half().to(cuda)
+    torch.cuda.synchronize()
+
+    def chain(v):
+        for qw, s, qz in layers:
+            v = tob.awq_gemm(v, qw, s, qz, 1)
+        return v
+
+    prev = tob.set_launch_overlap(False)
+    try:
+        ref = chain(x)
+        tob.set_launch_overlap(True)
+        for _ in range(3):
+            assert torch.equal(chain(x), ref)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            chain(x)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = chain(x)
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref)
+        del graph
+    finally:
+        tob.set_launch_overlap(prev)
+    want = x.float().cpu().numpy()
+    for qw, s, qz in layers:
+        want = oawq.gemm(want, qw.cpu().numpy(), s.float().cpu().numpy(), qz.cpu().numpy(), "f16")
+    np.testing.assert_allclose(ref.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)

@@ -43,9 +43,10 @@ from .quant_int8 import (
     w8a8_block_int8_matmul,
     w8a8_int8_accumulators,
 )
-from ._lib import version
+from ._lib import set_launch_overlap, version
 
 __all__ = [
+    "set_launch_overlap",
     "quantize_per_tensor",
     "dequantize_per_tensor",
     "quantize_per_channel",

@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_last_error_string": (ctypes.c_char_p, []),
     "to_device_check": (_I, [_I]),
     "to_device_error_word": (_I, [ctypes.POINTER(_I), _I]),
+    "to_set_launch_overlap": (_I, [_I]),
     "to_quant_per_tensor_i8": (_I, [_P, _I, _P, _P, _L, _P]),
     "to_dequant_per_tensor_i8": (_I, [_P, _P, _P, _I, _L, _P]),
     "to_quant_per_channel_i8": (_I, [_P, _I, _P, _P, _L, _L, _L, _P]),
@@ -158,3 +159,11 @@ def device_error_word(clear: bool = True) -> int:
 
 def version() -> str:
     return load().to_version().decode()
+
+
+def set_launch_overlap(enable: bool) -> bool:
+    """Turns programmatic dependent launch on or off for the small-M AWQ streaming kernel and
+    returns the previous setting. With it on, a call may read its weights while the previous
+    kernel in the stream is still running, so no kernel that writes those weights may be the
+    launch immediately before it (a decode loop over fixed weights is the intended use)."""
+    return bool(load().to_set_launch_overlap(1 if enable else 0))

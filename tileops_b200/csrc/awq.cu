@@ -10,6 +10,8 @@
 // conversion used below (one LOP3 per column pair).
 #include <cooperative_groups.h>
 
+#include <stdlib.h>
+
 #include <type_traits>
 
 #include "awq_common.cuh"
@@ -21,7 +23,10 @@ namespace tob {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int64_t kTensorCoreMinM = 32;
+constexpr int64_t kTensorCoreMinM = 33;
+// M <= 2 streams on CUDA cores (its cost grows with M); 3 <= M <= 32 runs the register-MMA
+// kernel, whose cost is flat in M.
+constexpr int64_t kStreamMaxM = 2;
 __constant__ int kAwqOrder[8] = {0, 4, 1, 5, 2, 6, 3, 7};
 
 // ------------------------------------------------------------------ pack / unpack
@@ -318,15 +323,293 @@ int launch_gemv(const void* x, const int32_t* qw, const void* s, const int32_t* 
   return launch_gemv_cfg<T, MT, 1, 16>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
 }
 
+template <typename T, int MT>
+int launch_gemv_stream(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
+                       void* y, int64_t M, int64_t K, int64_t N, int64_t G, cudaStream_t st);
+
+// A/B switches for measurements: TOB_GEMV_GENERAL=1 routes M <= 4 to the general streaming
+// kernel instead of the prefetching one; TOB_AWQ_SMALL_M=0 skips the TMA-fed small-M kernel.
+bool gemv_stream_enabled() {
+  static const bool on = getenv("TOB_GEMV_GENERAL") == nullptr;
+  return on;
+}
+bool small_m_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("TOB_AWQ_SMALL_M");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
 template <typename T>
 int launch_gemv_any_m(const void* x, const int32_t* qw, const void* s, const int32_t* qz, void* y,
                       int64_t M, int64_t K, int64_t N, int64_t G, cudaStream_t st) {
+  if (M <= 4 && gemv_stream_enabled()) {
+    int rc = TO_EUNSUPPORTED;
+    switch (M) {
+      case 1: rc = launch_gemv_stream<T, 1>(x, qw, s, qz, y, M, K, N, G, st); break;
+      case 2: rc = launch_gemv_stream<T, 2>(x, qw, s, qz, y, M, K, N, G, st); break;
+      case 3: rc = launch_gemv_stream<T, 3>(x, qw, s, qz, y, M, K, N, G, st); break;
+      default: rc = launch_gemv_stream<T, 4>(x, qw, s, qz, y, M, K, N, G, st); break;
+    }
+    if (rc != TO_EUNSUPPORTED) return rc;
+  }
   switch (M) {
     case 1: return launch_gemv<T, 1>(x, qw, s, qz, y, M, K, N, G, st);
     case 2: return launch_gemv<T, 2>(x, qw, s, qz, y, M, K, N, G, st);
     case 3: return launch_gemv<T, 3>(x, qw, s, qz, y, M, K, N, G, st);
     default: return launch_gemv<T, 4>(x, qw, s, qz, y, M, K, N, G, st);  // grid.z covers M / 4
   }
+}
+
+// ------------------------------------------------------------------ streaming GEMV, prefetching
+// The same arithmetic as k_awq_gemv for M <= 4, organised so that the weight stream starts at
+// the first instruction and never drains:
+//   * a column tile is CW packed words (8*CW columns); each lane reads 2 words (8 bytes) of a
+//     row, so a warp load covers RPL = 2*32/CW rows of whole 64- or 128-byte segments;
+//   * a CTA owns a K-chunk of the tile; each of its 8 warps owns a contiguous run of rows,
+//     walked in blocks of RB = RPL*LPT rows (inside one K-group), with the next block's weights,
+//     zeros and scales in flight while the current block is multiplied (two register buffers);
+//   * the first two blocks are requested before griddepcontrol.wait: with launch overlap on,
+//     they stream while the previous kernel in the stream finishes (x and y are only touched
+//     after the wait);
+//   * warp sums -> CTA sums in shared memory (fixed order) -> cluster reduction over the
+//     K-chunks through distributed shared memory into cluster rank 0 (deterministic).
+template <typename T, int CW, int LPT>
+struct GemvBlock {
+  uint2 w[LPT];
+  uint2 z;
+  uint4 s[2];
+};
+
+template <typename T, int MT, int CW, int LPT>
+__global__ void __launch_bounds__(kThreads, 2)
+k_awq_gemv_stream(const T* __restrict__ x, const uint32_t* __restrict__ qw,
+                  const T* __restrict__ scales, const uint32_t* __restrict__ qz,
+                  T* __restrict__ y, int M, int K, int N, int G, int kchunk, int ksplit) {
+  using H = Half2Of<T>;
+  using H2 = typename H::type;
+  constexpr int WPL = 2;
+  constexpr int LPR = CW / WPL;   // lanes per row
+  constexpr int RPL = 32 / LPR;   // rows per warp load
+  constexpr int RB = RPL * LPT;   // rows per block
+  constexpr int COLS = CW * 8;    // columns per CTA
+  using Blk = GemvBlock<T, CW, LPT>;
+
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);  // [MT][kchunk]
+  float* part = reinterpret_cast<float*>(smem_raw + (((size_t)MT * kchunk * 2 + 15) & ~(size_t)15));
+  float* tot = part + 8 * MT * COLS;                      // [MT][COLS]
+
+  const int words = N >> 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rl = lane / LPR, lw = lane - rl * LPR;
+  const int word0 = blockIdx.x * CW + lw * WPL;
+  const bool col_ok = word0 < words;
+  const int kb = blockIdx.y * kchunk;
+  const int rpw = kchunk >> 3;  // rows per warp, a multiple of RB
+  const int wb = kb + warp * rpw;
+  const int we = min(min(K, kb + kchunk), wb + rpw);
+  const int nblk = we > wb ? (we - wb + RB - 1) / RB : 0;
+
+  auto load = [&](Blk& b, int row0) {
+#pragma unroll
+    for (int i = 0; i < LPT; ++i) {
+      const int row = row0 + rl + RPL * i;
+      b.w[i] = (col_ok && row < K) ? ld_stream_v2(qw + (int64_t)row * words + word0)
+                                   : make_uint2(0u, 0u);
+    }
+    const int g = row0 / G;
+    if (col_ok) {
+      b.z = __ldg(reinterpret_cast<const uint2*>(qz + (int64_t)g * words + word0));
+      const uint4* sp = reinterpret_cast<const uint4*>(scales + (int64_t)g * N + (int64_t)word0 * 8);
+      b.s[0] = __ldg(sp);
+      b.s[1] = __ldg(sp + 1);
+    } else {
+      b.z = make_uint2(0u, 0u);
+      b.s[0] = b.s[1] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+
+  float acc[MT][WPL * 8];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < WPL * 8; ++c) acc[m][c] = 0.f;
+
+  auto compute = [&](const Blk& b, int row0) {
+    H2 zc[WPL][4];
+    awq_zero_consts<T>(b.z.x, zc[0]);
+    awq_zero_consts<T>(b.z.y, zc[1]);
+    const H2* sc = reinterpret_cast<const H2*>(&b.s[0]);  // sc[j*4 + q]: columns 8j+2q, +1
+#pragma unroll
+    for (int i = 0; i < LPT; ++i) {
+      const int xo = row0 + rl + RPL * i - kb;
+      uint16_t xv[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) xv[m] = xs[m * kchunk + xo];
+      const uint32_t wv[WPL] = {b.w[i].x, b.w[i].y};
+#pragma unroll
+      for (int j = 0; j < WPL; ++j) {
+        H2 d[4];
+        awq_word_diff<T>(wv[j], zc[j], d);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const H2 wq = __hmul2(d[q], sc[j * 4 + q]);  // the reference's dequantised pair
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            fma_pair_mixed<T>(bits_of(wq), xv[m], acc[m][j * 8 + 2 * q], acc[m][j * 8 + 2 * q + 1]);
+        }
+      }
+    }
+  };
+
+  Blk A, B;
+  if (nblk > 0) load(A, wb);
+  if (nblk > 1) load(B, wb + RB);
+
+  // Everything above reads only the weights; x (and y below) may belong to the previous grid.
+  grid_dependency_wait();
+  const uint16_t* x16 = reinterpret_cast<const uint16_t*>(x);
+  if ((K & 7) == 0) {
+    const int vec = kchunk >> 3;
+    for (int i = threadIdx.x; i < MT * vec; i += kThreads) {
+      const int m = i / vec, k = (i - m * vec) * 8;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (m < M && kb + k < K) v = __ldg(reinterpret_cast<const uint4*>(x16 + (int64_t)m * K + kb + k));
+      *reinterpret_cast<uint4*>(xs + m * kchunk + k) = v;
+    }
+  } else {
+    for (int i = threadIdx.x; i < MT * kchunk; i += kThreads) {
+      const int m = i / kchunk, k = i - m * kchunk;
+      xs[i] = (m < M && kb + k < K) ? x16[(int64_t)m * K + kb + k] : (uint16_t)0;
+    }
+  }
+  __syncthreads();
+  grid_dependents_launch();
+
+#pragma unroll 1
+  for (int bi = 0; bi < nblk; bi += 2) {
+    compute(A, wb + bi * RB);
+    if (bi + 2 < nblk) load(A, wb + (bi + 2) * RB);
+    if (bi + 1 < nblk) {
+      compute(B, wb + (bi + 1) * RB);
+      if (bi + 3 < nblk) load(B, wb + (bi + 3) * RB);
+    }
+  }
+
+  // Sum over the RPL lane-rows of a warp, then over the 8 warps in a fixed order.
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < WPL * 8; ++c) {
+      float v = acc[m][c];
+#pragma unroll
+      for (int o = LPR; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (rl == 0) part[(warp * MT + m) * COLS + lw * WPL * 8 + c] = v;
+    }
+  __syncthreads();
+  for (int i = threadIdx.x; i < MT * COLS; i += kThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w * MT * COLS + i];
+    tot[i] = s;
+  }
+
+  // With a K split, cluster rank r reduces column slice r over all ranks (fixed order) and
+  // stores it, so the remote loads and the stores are spread over the cluster.
+  const int rows = min(M, MT);
+  if (ksplit > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int per = COLS / ksplit;
+    const int c0 = blockIdx.y * per;
+    for (int i = threadIdx.x; i < rows * per; i += kThreads) {
+      const int m = i / per, c = c0 + (i - m * per);
+      float v[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) v[r] = r < ksplit ? cluster.map_shared_rank(tot, r)[m * COLS + c] : 0.f;
+      float s = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) s += v[r];
+      const int col = blockIdx.x * COLS + c;
+      if (col < N) y[(int64_t)m * N + col] = from_f32<T>(s);
+    }
+    cluster.sync();  // peers keep their shared memory until every slice has been read
+  } else {
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * COLS; i += kThreads) {
+      const int m = i / COLS, c = i - m * COLS;
+      const int col = blockIdx.x * COLS + c;
+      if (col < N) y[(int64_t)m * N + col] = from_f32<T>(tot[i]);
+    }
+  }
+}
+
+template <typename T, int MT, int CW, int LPT>
+int launch_gemv_stream_cfg(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
+                           void* y, int64_t M, int64_t K, int64_t N, int64_t G, int ksplit,
+                           cudaStream_t st) {
+  constexpr int RB = (64 / CW) * LPT;
+  const int words = (int)(N / 8);
+  const int tiles = (words + CW - 1) / CW;
+  const int per_cta = 8 * RB;
+  const int kchunk = (int)(ceil_div(ceil_div(K, ksplit), per_cta) * per_cta);
+  ksplit = (int)ceil_div(K, kchunk);
+  const size_t smem = (((size_t)MT * kchunk * 2 + 15) & ~(size_t)15) +
+                      (size_t)9 * MT * CW * 8 * sizeof(float);
+  if (smem > 100 * 1024) return TO_EUNSUPPORTED;
+  auto kern = k_awq_gemv_stream<T, MT, CW, LPT>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "awq_gemv: shared memory attribute");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, ksplit, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = 1;
+  attr[na].val.clusterDim.y = ksplit;
+  attr[na].val.clusterDim.z = 1;
+  ++na;
+  if (launch_overlap()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const T*)x, (const uint32_t*)qw, (const T*)s,
+                                     (const uint32_t*)qz, (T*)y, (int)M, (int)K, (int)N, (int)G,
+                                     kchunk, ksplit);
+  if (e != cudaSuccess) return cuda_fail(e, "awq_gemv launch");
+  return check_launch("awq_gemv");
+}
+
+// M <= 4 with an even number of packed words per row and aligned rows; returns
+// TO_EUNSUPPORTED (nothing launched) for shapes the general streaming kernel must take.
+template <typename T, int MT>
+int launch_gemv_stream(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
+                       void* y, int64_t M, int64_t K, int64_t N, int64_t G, cudaStream_t st) {
+  constexpr int LPT = MT <= 2 ? 8 : 4;
+  const int64_t words = N / 8;
+  if (words % 2 != 0 || (uintptr_t)qw % 8 != 0 || (uintptr_t)qz % 8 != 0 || !aligned16(s))
+    return TO_EUNSUPPORTED;
+  const int64_t sms = sm_count();
+  // Wide tiles (128-byte row segments) when they still give two CTAs per SM at ksplit 8.
+  const bool wide = ceil_div(words, 32) * 8 >= 2 * sms;
+  const int cw = wide ? 32 : 16;
+  const int rb = (64 / cw) * LPT;
+  if (G % rb != 0 && G != K) return TO_EUNSUPPORTED;
+  const int64_t tiles = ceil_div(words, cw);
+  int ksplit = 1;
+  while (ksplit < 8 && tiles * ksplit < 2 * sms && K >= (int64_t)ksplit * 2 * 8 * rb) ksplit *= 2;
+  if (wide) return launch_gemv_stream_cfg<T, MT, 32, LPT>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
+  return launch_gemv_stream_cfg<T, MT, 16, LPT>(x, qw, s, qz, y, M, K, N, G, ksplit, st);
 }
 
 int check_awq_shapes(const char* op, int64_t K, int64_t N, int64_t G) {
@@ -341,6 +624,9 @@ int check_awq_shapes(const char* op, int64_t K, int64_t N, int64_t G) {
 }  // namespace
 
 int awq_gemm_tc_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
+                       cudaStream_t st);
+int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                        const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
                        cudaStream_t st);
 
@@ -434,9 +720,15 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
   if (M <= 0) return fail(TO_EINVAL, "awq_gemm: invalid M=%lld", (long long)M);
   if (!aligned16(scales) || !aligned16(x))
     return fail(TO_EINVAL, "awq_gemm: x and scales must be 16-byte aligned");
-  // Prefill-sized M runs on the tensor cores; small M streams the weights once per 4 rows.
+  // Prefill-sized M runs on the tcgen05 GEMM; 3 <= M <= 32 on the TMA-fed register-MMA
+  // kernel; M <= 2 and the shapes neither takes (ragged N, unaligned rows) on the streaming
+  // SIMT kernels.
   if (M >= kTensorCoreMinM) {
     const int rc = awq_gemm_tc_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N,
+                                      group_size, (cudaStream_t)stream);
+    if (rc != TO_EUNSUPPORTED) return rc;
+  } else if (M > kStreamMaxM && small_m_enabled()) {
+    const int rc = awq_small_m_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N,
                                       group_size, (cudaStream_t)stream);
     if (rc != TO_EUNSUPPORTED) return rc;
   }

@@ -27,6 +27,8 @@ inline int check_launch(const char* what) {
 int sm_count();
 // Device address of the library's error word on the current device (nullptr on failure).
 int* device_error_ptr();
+// Process-wide launch-overlap switch (programmatic dependent launch for streaming kernels).
+bool launch_overlap();
 // Codes kernels write into the error word.
 enum DeviceError : int { kErrNone = 0, kErrWaitTimeout = 1, kErrTmemAlloc = 2, kErrSmemAlign = 3 };
 
@@ -121,6 +123,25 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
+}
+
+// Streaming 8-byte global load that does not allocate in L1. Volatile so that it stays where
+// a prefetching loop issues it (ahead of the arithmetic on the previous block).
+__device__ __forceinline__ uint2 ld_stream_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+
+// Programmatic dependent launch: wait for the preceding grid's memory, and let the next grid
+// (launched with the overlap attribute) start its prologue. Both are no-ops without it.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 template <typename T, int N> struct alignas(sizeof(T) * N) Pack {

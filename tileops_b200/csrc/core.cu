@@ -3,6 +3,7 @@
 #include <stdarg.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -58,6 +59,9 @@ int* device_error_ptr() {
   }
   return cached[dev];
 }
+
+static std::atomic<int> g_launch_overlap{0};
+bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
 }  // namespace tob
 
 extern "C" {
@@ -75,6 +79,11 @@ int to_device_check(int device) {
                      "device %d is sm_%d%d (%s); libtileops_b200 is built for sm_100a only",
                      device, prop.major, prop.minor, prop.name);
   return TO_OK;
+}
+
+int to_set_launch_overlap(int enable) {
+  if (enable < 0) return tob::g_launch_overlap.load();
+  return tob::g_launch_overlap.exchange(enable ? 1 : 0);
 }
 
 int to_device_error_word(int* value, int clear) {

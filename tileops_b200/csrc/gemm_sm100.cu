@@ -556,6 +556,34 @@ int make_tmap_out16(CUtensorMap* out, const void* ptr, int64_t rows, int64_t col
 
 int make_tmap_plain(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
                     int box_cols, int box_rows) {
+  struct Key {
+    const void* p;
+    int64_t rows, cols;
+    int elem, bc, br;
+    bool operator==(const Key& o) const {
+      return p == o.p && rows == o.rows && cols == o.cols && elem == o.elem && bc == o.bc &&
+             br == o.br;
+    }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.p) ^ (size_t)(k.rows * 1315423911u) ^
+             (size_t)(k.cols * 2654435761u) ^ (size_t)(k.bc * 131 + k.br * 7 + k.elem);
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, CUtensorMap, Hash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const Key key{(const char*)ptr + ((int64_t)dev << 56), rows, cols, elem, box_cols, box_rows};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return TO_OK;
+    }
+  }
   EncodeFn encode = get_encode();
   if (!encode) return fail(TO_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -569,6 +597,59 @@ int make_tmap_plain(CUtensorMap* out, const void* ptr, int64_t rows, int64_t col
   if (r != CUDA_SUCCESS)
     return fail(TO_ECUDA, "cuTensorMapEncodeTiled (plain) failed (%d) for [%lld, %lld] x %d B",
                 (int)r, (long long)rows, (long long)cols, elem);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *out);
+  return TO_OK;
+}
+
+// Activations x [M, K] (16-bit, K % 64 == 0) viewed as 64-element blocks: dims
+// {64, M, K/64} with strides {K*2, 128} bytes; one box {64, box_tokens, box_blocks} lands as
+// box_blocks tiles of [box_tokens x 128 B], each in the 128-byte-swizzle layout. Cached.
+int make_tmap_x_blocks(CUtensorMap* out, const void* ptr, int64_t M, int64_t K, int box_tokens,
+                       int box_blocks) {
+  struct Key {
+    const void* p;
+    int64_t m, k;
+    int bt, bb;
+    bool operator==(const Key& o) const {
+      return p == o.p && m == o.m && k == o.k && bt == o.bt && bb == o.bb;
+    }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.p) ^ (size_t)(k.m * 1315423911u) ^
+             (size_t)(k.k * 2654435761u) ^ (size_t)(k.bt * 131 + k.bb);
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, CUtensorMap, Hash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const Key key{(const char*)ptr + ((int64_t)dev << 56), M, K, box_tokens, box_blocks};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return TO_OK;
+    }
+  }
+  EncodeFn encode = get_encode();
+  if (!encode) return fail(TO_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[3] = {64, (cuuint64_t)M, (cuuint64_t)(K / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)(K * 2), 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_tokens, (cuuint32_t)box_blocks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(ptr), dims, strides,
+                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TO_ECUDA, "cuTensorMapEncodeTiled (x blocks) failed (%d) for [%lld, %lld]", (int)r,
+                (long long)M, (long long)K);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *out);
   return TO_OK;
 }
 

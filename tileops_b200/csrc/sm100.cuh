@@ -107,6 +107,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int
       : "memory");
 }
 
+// 3-D tiled load (coordinates innermost first), completing `bytes` on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, int x, int y, int z,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // 2-D tiled store of a box from this CTA's shared memory to global (bulk-group completion).
 // Rows / columns outside the tensor are clipped by the hardware.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, int x, int y, const void* src) {
@@ -128,7 +138,9 @@ __device__ __forceinline__ void bulk_wait_read() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
-// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
+// Orders this thread's generic-proxy shared-memory accesses before later async-proxy ones:
+// stores before a tensor-core or TMA-store read of them, and loads before a TMA load that
+// refills the same buffer once it has been released.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -213,6 +225,10 @@ int make_tmap_out16(CUtensorMap* out, const void* ptr, int64_t rows, int64_t col
 // (elem 2 or 4), inner box bytes a multiple of 16.
 int make_tmap_plain(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
                     int box_cols, int box_rows);
+// 16-bit activations [M, K] (K % 64 == 0) as {64, M, K/64} blocks: a box of box_tokens rows x
+// box_blocks 64-element blocks lands as box_blocks [box_tokens x 128 B] 128-byte-swizzled tiles.
+int make_tmap_x_blocks(CUtensorMap* out, const void* ptr, int64_t M, int64_t K, int box_tokens,
+                       int box_blocks);
 
 template <Kind K> struct KindTraits;
 template <> struct KindTraits<Kind::I8> {
