@@ -434,6 +434,9 @@ class AwqGemv:
         self.out_host = torch.empty(1, N, dtype=torch.float16).pin_memory()
         self.dev = dev
         self.kernel_bytes = K * N // 2 + (K // G) * N * 2 + (K // G) * N // 2 + 2 * K + 2 * N
+        # Consecutive calls overlap through programmatic dependent launch: a call streams its
+        # weights while the previous one finishes (no kernel in the chain writes weights).
+        tob.set_launch_overlap(True)
 
     def step(self, i):
         qw, s, qz = self.sets[i % self.SETS]
@@ -459,7 +462,8 @@ class AwqGemv:
         return {"workload": "awq_w4a16_gemv x[1,4096] fp16 @ int4 [4096,4096] group 128",
                 "M": 1, "K": self.K, "N": self.N, "group_size": self.G,
                 "parallelism": f"replicas x{world}",
-                "l2": "48 rotating weight sets x 8.7 MB > L2"}
+                "l2": "48 rotating weight sets x 8.7 MB > L2",
+                "launch_overlap": "programmatic dependent launch between consecutive calls"}
 
     @classmethod
     def cpu_reference(cls, threads):
@@ -515,6 +519,7 @@ class Decode:
         self.out_host = torch.empty(m, 4096, dtype=torch.float16).pin_memory()
         self.weight_bytes = self.LAYERS * sum(
             k * n // 2 + (k // self.G) * n * 2 + (k // self.G) * n // 2 for k, n in self.SHAPES)
+        tob.set_launch_overlap(True)  # layer i+1 streams its weights while layer i finishes
 
     def _run(self, x):
         gather = self.sharded.gather_columns if self.world > 1 else (lambda y: y)
@@ -547,7 +552,8 @@ class Decode:
         return {"workload": f"awq decode step, 32 layers x 4 linears (8B-class), M={self.m} fp16, "
                             "group 128, N-sharded + all-gather per linear",
                 "M": self.m, "layers": self.LAYERS, "parallelism": f"tp{world} (N-sharded)",
-                "l2": "3.6 GB of weights per step > L2"}
+                "l2": "3.6 GB of weights per step > L2",
+                "launch_overlap": "programmatic dependent launch between consecutive layers"}
 
     @classmethod
     def cpu_reference(cls, threads):

@@ -143,3 +143,54 @@ def test_fp8_per_token_per_tensor_vs_oracle(cuda, m, n, k):
                                  sa.cpu().numpy(), sb.reshape(1, 1).cpu().numpy(), (n, k), "bf16")
         got = _f(y)
     np.testing.assert_allclose(got, want, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("m,n,k", [(129, 320, 384), (256, 1000, 640), (200, 11008, 4096)])
+def test_int8_ksplit_pair_vs_oracle(cuda, m, n, k):
+    """128 < M <= 256 layers whose 256 x 160 tiles fit one wave of CTA pairs split K over a
+    cluster pair (odd K-block counts included): int32 accumulators bit-exact, scaled outputs
+    against the oracle, and identical results across calls."""
+    g = torch.Generator().manual_seed(7 * m + n + k)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand(m, 1, generator=g) * 0.045 + 0.005
+    b_s = torch.rand(n, 1, generator=g) * 0.009 + 0.001
+    acc = tob.w8a8_int8_accumulators(a.to(cuda), b.to(cuda))
+    assert np.array_equal(acc.cpu().numpy().astype(np.int64), oi8.accumulators(a.numpy(), b.numpy()))
+    args = (a.to(cuda), b.to(cuda), a_s.to(cuda), b_s.to(cuda), [1, k])
+    y = tob.w8a8_block_int8_matmul(*args, output_dtype=torch.bfloat16)
+    want = oi8.block_matmul(a.numpy(), b.numpy(), a_s.numpy(), b_s.numpy(), (1, k), "bf16")
+    np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)
+    assert torch.equal(tob.w8a8_block_int8_matmul(*args, output_dtype=torch.bfloat16), y)
+
+
+def test_int8_ksplit_pair_fused_bias(cuda):
+    """apply_w8a8_block_int8_linear with an fp16 bias on a K-split pair: the bias is added
+    after rounding to fp16 and rounded again, as in the reference."""
+    from oracle.numerics import rounder
+
+    m, n, k = 200, 1000, 512
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(m, k, generator=g).half()
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    w_s = torch.rand(n, 1, generator=g) * 0.009 + 0.001
+    bias = torch.randn(n, generator=g).half()
+    y = tob.apply_w8a8_block_int8_linear(x.to(cuda), w.to(cuda), [1, k], w_s.to(cuda),
+                                         bias=bias.to(cuda))
+    q, s = oi8.group_quant(x.float().numpy(), k)
+    mm = oi8.block_matmul(q, w.numpy(), s, w_s.numpy(), (1, k), "f16")
+    want = rounder("f16")(mm + bias.float().numpy())
+    np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("m,n,k", [(200, 3000, 1024), (256, 11008, 512)])
+def test_fp8_ksplit_pair_vs_oracle(cuda, m, n, k):
+    g = torch.Generator().manual_seed(m + n + 2 * k)
+    A = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    B = torch.randn(n, k, generator=g).to(torch.bfloat16)
+    qa, sa = tob.per_token_group_quant_fp8(A.to(cuda), k)
+    qb, sb = tob.input_to_float8(B.to(cuda))
+    y = tob.w8a8_block_fp8_matmul(qa, qb, sa, sb.reshape(1, 1), [n, k], output_dtype=torch.bfloat16)
+    want = ofp8.block_matmul(qa.view(torch.uint8).cpu().numpy(), qb.view(torch.uint8).cpu().numpy(),
+                             sa.cpu().numpy(), sb.reshape(1, 1).cpu().numpy(), (n, k), "bf16")
+    np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)

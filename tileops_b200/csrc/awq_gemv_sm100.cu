@@ -103,14 +103,6 @@ __device__ __forceinline__ void consumer_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(32 * kSmConsumers) : "memory");
 }
 
-// Cluster-wide barrier with release/acquire ordering of shared memory. The warp is first
-// reconverged (the producer warp's lane 0 arrives here long after its other lanes), so the
-// aligned barrier counts each warp once, after all of its stores.
-__device__ __forceinline__ void cluster_sync_all() {
-  __syncwarp();
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 
 // Grid: (column tiles of CW = 8*WPQ packed words, K-chunks); the K-chunks of a column tile
 // form one cluster. NT = 8-token tiles of M (1, 2 or 4 for M <= 8, 16, 32).

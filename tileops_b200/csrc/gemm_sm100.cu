@@ -19,6 +19,7 @@
 // Every wait is bounded (sm100.cuh, kWaitLimitNs); on expiry the kernel records the error
 // word, unwinds every role, waits (bounded) for its in-flight copies and MMAs, frees its TMEM
 // and returns.
+#include <cooperative_groups.h>
 #include <cudaTypedefs.h>
 
 #include <stdlib.h>
@@ -222,11 +223,193 @@ __device__ __forceinline__ void store_direct(const float* v, const Epi& ep, int6
 // only within rounding.
 __device__ __forceinline__ int k_start(int t, int kblocks) { return (int)(((unsigned)t * 5u) % (unsigned)kblocks); }
 
+// Output tile t -> (M tile, N tile). Tiles run in bands of kTileBand M tiles, M fastest within a
+// band: the ~148 tiles in flight then share ~16 M tiles of A and ~9 N tiles of B, so each band
+// streams B once and keeps its A rows in L2, instead of re-reading all of A on every wave (the
+// plain M-fastest order does that once M spans more tiles than a wave). Problems of at most
+// kTileBand M tiles keep the plain order.
+constexpr int kTileBand = 16;
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int band_tiles = kTileBand * n_tiles;
+  const int band = t / band_tiles;
+  const int rows = min(kTileBand, m_tiles - band * kTileBand);  // M tiles in this band
+  const int local = t - band * band_tiles;
+  mt = band * kTileBand + local % rows;
+  nt = local / rows;
+}
+
+// Bytes of one 128-row half's partial sums in the exchange layout [chunk][j / 4][row][4] (32-bit
+// words; 16-column tail chunks leave their upper half unused).
+template <int BN>
+__host__ __device__ constexpr int ks2_xfer_bytes() {
+  return ((BN + 31) / 32) * 8 * 128 * 16;
+}
+
+// Epilogue of a K-split pair (see k_gemm_sm100): 8 warps, two per TMEM lane quarter q, taking
+// alternate 32-column chunks. Each CTA stages its partial sums of the peer's half in its own
+// (idle) operand ring, then one bulk copy moves them into the peer's ring, completing on the
+// peer's recv_bar; the staging layout makes every warp store and load one contiguous
+// 512-byte row (no bank conflicts).
 template <Kind KD, int BM, int BN, int STAGES>
+__device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_t* tfull,
+                                             uint64_t* recv_bar,
+                                             volatile int* abort_flag, int* err, const Epi& ep,
+                                             const CUtensorMap* tmC, const CUtensorMap* tmC16,
+                                             int M, int N, int m_tiles, int n_tiles, int t,
+                                             int rank, int warp, int lane) {
+  using C = GemmCfg<KD, BM, BN, STAGES>;
+  constexpr int kXfer = ks2_xfer_bytes<BN>();
+  constexpr int kRecvOff = (kXfer + 1023) & ~1023;
+  // Output slabs for the TMA stores, one per (chunk, lane quarter), after the exchange areas:
+  // no store has to wait for an earlier one to release its slab.
+  constexpr int kOutOff = kRecvOff + ((kXfer + 1023) & ~1023);
+  static_assert((size_t)kOutOff + (size_t)((BN + 31) / 32) * 4 * C::kStageOutBytes <=
+                    (size_t)STAGES * C::kStageBytes,
+                "the staged and received partial sums and the output slabs must fit in the ring");
+  const int q = warp & 3;          // the TMEM lane quarter this warp may read
+  const int eg = (warp - 2) >> 2;  // which of the two warps on that quarter
+  const int mine = rank, other = rank ^ 1;
+  int mt, nt;
+  tile_coords(t, m_tiles, n_tiles, mt, nt);
+  float sbt[(BN + 31) / 32];
+  load_tile_col_scales<BN>(sbt, ep, nt * BN, N, lane);
+  const int row0 = mt * BM + mine * 128 + q * 32;  // first row of this warp's 32-row slab
+  const int row = row0 + lane;
+  const bool row_ok = row < M;
+  const float sa = row_ok ? __ldg(ep.a_s + (int64_t)row * ep.a_s_ld) : 0.f;
+  uint32_t* stage = reinterpret_cast<uint32_t*>(sA);             // partial sums for the peer
+  uint32_t* recv = reinterpret_cast<uint32_t*>(sA + kRecvOff);   // the peer's, for this CTA
+  auto slot = [&](int c, int jj) { return ((c * 8 + jj) * 128 + q * 32 + lane) * 4; };
+
+  // Tuning timeline (null in production): per CTA, the chunk-trace slots of the regular
+  // epilogue hold entry, accumulator ready, barrier 1, copy issued, received and end.
+  uint64_t* ptr = (ep.trace != nullptr && warp == 2 && lane == 0)
+                      ? ep.trace + (int64_t)gridDim.x * ep.trace_steps * 3 + gridDim.x * 2 +
+                            (int64_t)blockIdx.x * 32
+                      : nullptr;
+  if (ptr) ptr[0] = globaltimer_ns();
+  const bool ok = mbar_wait(tfull, 0, abort_flag, err);
+  tc_fence_after();
+  if (ptr) ptr[1] = globaltimer_ns();
+  if (ok) {
+    // The main loop is done, so this CTA's ring is free: stage the peer's half.
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      if (((c0 / 32) & 1) != eg) continue;
+      const bool wide = (BN - c0) >= 32;
+      uint32_t r[32];
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(other * BN + c0);
+      tmem_ld16(taddr, r);
+      if (wide) tmem_ld16(taddr + 16, r + 16);
+      tmem_ld_wait();
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj)
+        if (jj < (wide ? 8 : 4))
+          *reinterpret_cast<uint4*>(stage + slot(c0 / 32, jj)) =
+              make_uint4(r[4 * jj], r[4 * jj + 1], r[4 * jj + 2], r[4 * jj + 3]);
+    }
+  }
+  fence_proxy_async_smem();  // the staged words are read by the bulk copy (async proxy)
+  cluster_sync_all();        // 1: both halves staged; both rings free to receive
+  if (ptr) ptr[2] = globaltimer_ns();
+  if (warp == 2 && lane == 0) {
+    const uint32_t dst = mapa_shared(smem_u32(recv), (uint32_t)other);
+    const uint32_t bar = mapa_shared(smem_u32(recv_bar), (uint32_t)other);
+    constexpr int kPiece = 16384;  // bytes per copy
+#pragma unroll 1
+    for (int off = 0; off < kXfer; off += kPiece)
+      bulk_copy_to_peer(dst + off, reinterpret_cast<uint8_t*>(stage) + off,
+                        (uint32_t)min(kPiece, kXfer - off), bar);
+  }
+  if (ptr) ptr[3] = globaltimer_ns();
+  const bool got = mbar_wait(recv_bar, 0, abort_flag, err);
+  if (ptr) ptr[4] = globaltimer_ns();
+  // 2 (split): this CTA's copy has landed in the peer once the peer arrives; the peer's shared
+  // memory may be released only after that, so the wait is at the very end.
+  cluster_arrive_release();
+  if (ok && got) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      if (((c0 / 32) & 1) != eg) continue;
+      const bool wide = (BN - c0) >= 32;
+      uint32_t r[32];
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(mine * BN + c0);
+      tmem_ld16(taddr, r);
+      if (wide) tmem_ld16(taddr + 16, r + 16);
+      tmem_ld_wait();
+      // Rank 0's partial sum comes first in every element, whichever CTA adds it up.
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        if (jj >= (wide ? 8 : 4)) continue;
+        const uint4 pv = *reinterpret_cast<const uint4*>(recv + slot(c0 / 32, jj));
+        const uint32_t p[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t& d = r[4 * jj + e];
+          if (KD == Kind::I8) {
+            d = (uint32_t)((int32_t)d + (int32_t)p[e]);
+          } else {
+            const float lo = rank == 0 ? __uint_as_float(d) : __uint_as_float(p[e]);
+            const float hi = rank == 0 ? __uint_as_float(p[e]) : __uint_as_float(d);
+            d = __float_as_uint(lo + hi);
+          }
+        }
+      }
+      const int col0 = nt * BN + c0;
+      if (col0 >= N) continue;
+      const int valid = min(wide ? 32 : 16, N - col0);
+      float v[32];
+      scale_chunk32<KD, BN>(r, v, sa, sbt, c0);
+      if (KD == Kind::I8 && ep.acc_out != nullptr && row_ok) {
+        int32_t* dst = ep.acc_out + (int64_t)row * N + col0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < valid) dst[j] = (int32_t)r[j];
+      }
+      if (ep.tma_store) {
+        uint8_t* stg = sA + kOutOff + (size_t)((c0 / 32) * 4 + q) * C::kStageOutBytes;
+        uint32_t pk[16];
+        pack_out16(v, pk, ep, col0, valid);
+        if (wide) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            *reinterpret_cast<uint4*>(stg + lane * 32 + (c << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(wide ? tmC : tmC16, col0, row0, stg);
+          bulk_commit();
+        }
+      } else if (row_ok) {
+        store_direct<KD>(v, ep, (int64_t)row * N + col0, col0, valid, N);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (ep.tma_store && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+  if (ptr) ptr[5] = globaltimer_ns();
+  cluster_wait_acquire();
+}
+
+// KS2: the two CTAs of a (2,1,1) cluster share one BM = 256 tile and split its K blocks in
+// half, so each SM streams half of the tile's A and B rows. Each CTA then finalises one
+// 128-row half: it sends its partial sums of the other half into the peer's (by then idle)
+// operand ring through distributed shared memory and adds the peer's partial sums to its own.
+// int32 sums stay exact; fp32 sums are added in a fixed order. One tile per CTA pair.
+template <Kind KD, int BM, int BN, int STAGES, bool KS2>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC16,
                  int M, int N, int K, Epi ep, int* err) {
+  static_assert(!KS2 || BM == 256, "the K-split pair finalises one 128-row half per CTA");
   using C = GemmCfg<KD, BM, BN, STAGES>;
   using Tr = KindTraits<KD>;
   // The swizzled operand tiles need 1024-byte alignment; the dynamic shared memory window
@@ -241,15 +424,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* recv_bar = drain + 1;  // K-split pair: the peer's partial sums have landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
   const int tiles = m_tiles * n_tiles;
   const int kblocks = (K + C::kBK - 1) / C::kBK;
+  // Tiles this CTA visits (t0, t0 + tstride, ...) and its K blocks [kb_lo, kb_lo + kb_n).
+  const int rank = KS2 ? (int)(blockIdx.x & 1) : 0;
+  const int t0 = KS2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstride = KS2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int kb_lo = KS2 ? rank * (kblocks / 2) : 0;
+  const int kb_n = KS2 ? (rank ? kblocks - kblocks / 2 : kblocks / 2) : kblocks;
 
+  // Every role depends on the 1024-byte alignment of the operand ring; without it the kernel
+  // records an error and does nothing.
+  const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
+  // The producer thread initialises the barriers and at once requests the first ring of
+  // stages of its first tile (no stage has a previous use to wait for), so the operand stream
+  // starts while the MMA warp allocates tensor memory.
+  int pre = 0;  // stages of the first tile already requested
+  uint64_t pol_a = 0, pol_b = 0;
   if (threadIdx.x == 0) {
+    if (KS2 && ep.trace != nullptr)  // tuning timeline: kernel entry of this CTA
+      ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + gridDim.x * 2 + blockIdx.x * 32 + 6] =
+          globaltimer_ns();
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
@@ -259,20 +460,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(tempty + b, kEpiWarps);
     }
     mbar_init(drain, 1);
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    if (KS2) mbar_arrive_expect_tx(recv_bar, (uint32_t)ks2_xfer_bytes<BN>());
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (ep.tma_store) {
       prefetch_tmap(&tmC);
       prefetch_tmap(&tmC16);
     }
+    if (misaligned) {
+      if (err) atomicExch(err, (int)kErrSmemAlign);
+    } else if (t0 < tiles) {
+      pol_a = make_policy(ep.policy_a);
+      pol_b = make_policy(ep.policy_b);
+      int mt, nt;
+      tile_coords(t0, m_tiles, n_tiles, mt, nt);
+      const int k0 = k_start(t0, kb_n);
+      pre = min(STAGES, kb_n);
+      for (int it = 0; it < pre; ++it) {
+        const int kb = kb_lo + (k0 + it) % kb_n;
+        if (ep.trace != nullptr && it < ep.trace_steps)
+          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
+        mbar_arrive_expect_tx(full + it, C::kStageBytes);
+        tma_load_2d(sA + (size_t)it * C::kABytes, &tmA, kb * C::kBK, mt * BM, full + it, pol_a);
+        tma_load_2d(sB + (size_t)it * C::kBBytes, &tmB, kb * C::kBK, nt * BN, full + it, pol_b);
+      }
+    }
   }
-  // Every role depends on the 1024-byte alignment of the operand ring; without it the kernel
-  // records an error and does nothing.
-  const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
-  if (misaligned && threadIdx.x == 0 && err) atomicExch(err, (int)kErrSmemAlign);
-  if (warp == 0) tmem_alloc<C::kTmemCols>(tmem_holder);
+  if (warp == 1) tmem_alloc<C::kTmemCols>(tmem_holder);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -280,19 +497,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (misaligned) {
     // nothing to do; fall through to the teardown
+    if constexpr (KS2) {
+      cluster_sync_all();
+      cluster_arrive_release();
+      cluster_wait_acquire();
+    }
   } else if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint64_t pol_a = make_policy(ep.policy_a), pol_b = make_policy(ep.policy_b);
-      uint32_t s = 0, ph = 0;
-      uint32_t issued_mask = 0, issued_phase = 0;  // per stage: loads issued / their phase
+      uint32_t s = (uint32_t)(pre % STAGES), ph = pre == STAGES ? 1u : 0u;
+      // per stage: loads issued / their phase (the pre-issued ring is phase 0)
+      uint32_t issued_mask = (1u << pre) - 1u, issued_phase = 0;
       bool ok = true;
-      int step = 0;
-      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-        const int mt = t % m_tiles, nt = t / m_tiles;
-        const int k0 = k_start(t, kblocks);
-        for (int it = 0; it < kblocks; ++it, ++step) {
-          const int kb = (k0 + it) % kblocks;
+      int step = pre;
+      for (int t = t0; ok && t < tiles; t += tstride) {
+        int mt, nt;
+        tile_coords(t, m_tiles, n_tiles, mt, nt);
+        const int k0 = k_start(t, kb_n);
+        for (int it = (t == t0 ? pre : 0); it < kb_n; ++it, ++step) {
+          const int kb = kb_lo + (k0 + it) % kb_n;
           if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
           if (ep.trace != nullptr && step < ep.trace_steps)
             ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 0] = globaltimer_ns();
@@ -308,12 +531,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // Unwinding: let every copy this thread started land before the CTA exits.
         for (int i = 0; i < STAGES; ++i)
           if (issued_mask & (1u << i)) {
-            const uint64_t t0 = globaltimer_ns();
+            const uint64_t tw = globaltimer_ns();
             while (!mbar_try_wait(full + i, (issued_phase >> i) & 1u) &&
-                   globaltimer_ns() - t0 < kWaitLimitNs) {
+                   globaltimer_ns() - tw < kWaitLimitNs) {
             }
           }
       }
+    }
+    if constexpr (KS2) {  // the pair's epilogue barriers (see ks2_epilogue)
+      cluster_sync_all();
+      cluster_arrive_release();
+      cluster_wait_acquire();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -322,13 +550,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t s = 0, ph = 0;
       int i = 0, step = 0;
       bool ok = true, any = false;
-      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++i) {
+      for (int t = t0; ok && t < tiles; t += tstride, ++i) {
         const int buf = i % C::kAccBufs;
         const uint32_t aph = (uint32_t)(i / C::kAccBufs) & 1u;
         if (!mbar_wait(tempty + buf, aph ^ 1, abort_flag, err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(buf * C::kAccCols);
-        for (int it = 0; it < kblocks; ++it, ++step) {
+        for (int it = 0; it < kb_n; ++it, ++step) {
           if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
           tc_fence_after();
           const bool tr = ep.trace != nullptr && step < ep.trace_steps;
@@ -355,26 +583,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok && any) {
         // Unwinding: wait (bounded) until the MMAs already issued have finished with TMEM.
         umma_commit(drain);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        const uint64_t tw = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - tw < kWaitLimitNs) {
         }
       }
     }
+    if constexpr (KS2) {
+      cluster_sync_all();
+      cluster_arrive_release();
+      cluster_wait_acquire();
+    }
+  } else if constexpr (KS2) {
+    // ------------------------------------------------------------ epilogue, K-split pair
+    ks2_epilogue<KD, BM, BN, STAGES>(tmem, sA, tfull, recv_bar, abort_flag, err, ep, &tmC, &tmC16,
+                                     M, N, m_tiles, n_tiles, t0, rank, warp, lane);
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;          // the TMEM lane quarter this warp may read
     const int eg = (warp - 2) >> 2;  // which of the two warps on that quarter
     int i = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+    for (int t = t0; t < tiles; t += tstride, ++i) {
       const int buf = i % C::kAccBufs;
       const uint32_t aph = (uint32_t)(i / C::kAccBufs) & 1u;
       // Scales of this tile, loaded while the main loop still runs.
+      int mt, nt;
+      tile_coords(t, m_tiles, n_tiles, mt, nt);
       float sbt[(BN + 31) / 32];
-      load_tile_col_scales<BN>(sbt, ep, (t / m_tiles) * BN, N, lane);
+      load_tile_col_scales<BN>(sbt, ep, nt * BN, N, lane);
       float sat[C::kHalves];
 #pragma unroll
       for (int h = 0; h < C::kHalves; ++h) {
-        const int rr = (t % m_tiles) * BM + h * 128 + q * 32 + lane;
+        const int rr = mt * BM + h * 128 + q * 32 + lane;
         sat[h] = rr < M ? __ldg(ep.a_s + (int64_t)rr * ep.a_s_ld) : 0.f;
       }
       if (!mbar_wait(tfull + buf, aph, abort_flag, err)) break;
@@ -383,7 +622,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // (start, end) of the first tile's epilogue, written by lane 0 of the first epilogue warp.
       const bool etr = ep.trace != nullptr && i == 0 && warp == 2 && lane == 0;
       if (etr) ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + blockIdx.x * 2] = globaltimer_ns();
-      const int mt = t % m_tiles, nt = t / m_tiles;
       constexpr int kChunks = (BN + 31) / 32;
 #pragma unroll 1
       for (int h = 0; h < C::kHalves; ++h) {
@@ -460,7 +698,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<C::kTmemCols>(tmem);
   }
@@ -653,11 +891,11 @@ int make_tmap_x_blocks(CUtensorMap* out, const void* ptr, int64_t M, int64_t K, 
   return TO_OK;
 }
 
-template <Kind KD, int BM, int BN, int STAGES>
+template <Kind KD, int BM, int BN, int STAGES, bool KS2 = false>
 int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                     cudaStream_t st) {
   using C = GemmCfg<KD, BM, BN, STAGES>;
-  auto kern = k_gemm_sm100<KD, BM, BN, STAGES>;
+  auto kern = k_gemm_sm100<KD, BM, BN, STAGES, KS2>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -678,10 +916,30 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
     if (rc) return rc;
   }
   const int64_t tiles = ceil_div(M, BM) * ceil_div(N, BN);
-  const int grid = (int)std::min<int64_t>(tiles, sm_count());
-  k_gemm_sm100<KD, BM, BN, STAGES><<<grid, kGemmThreads, C::kSmem, st>>>(
-      ta, tb, tc32, tc16, (int)M, (int)N, (int)K, e2, device_error_ptr());
-  return check_launch("tcgen05 gemm");
+  if constexpr (KS2) {
+    // One tile per CTA pair: the caller guarantees 2 x tiles <= SMs.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * tiles), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc32, tc16, (int)M, (int)N, (int)K, e2,
+                                       device_error_ptr());
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 gemm (K-split pair) launch");
+    return check_launch("tcgen05 gemm (K-split pair)");
+  } else {
+    const int grid = (int)std::min<int64_t>(tiles, sm_count());
+    kern<<<grid, kGemmThreads, C::kSmem, st>>>(ta, tb, tc32, tc16, (int)M, (int)N, (int)K, e2,
+                                               device_error_ptr());
+    return check_launch("tcgen05 gemm");
+  }
 }
 
 // Tile shapes: large problems take 128 x 256 tiles; small-M layers (M <= 256, the decode /
@@ -709,10 +967,19 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
     case 256128: return launch_gemm_cfg<KD, 256, 128, 4>(a, b, M, N, K, ep, st);
     case 256080: return launch_gemm_cfg<KD, 256, 80, 5>(a, b, M, N, K, ep, st);
     case 256064: return launch_gemm_cfg<KD, 256, 64, 5>(a, b, M, N, K, ep, st);
+    case 256160: return launch_gemm_cfg<KD, 256, 160, 4, true>(a, b, M, N, K, ep, st);
     default: break;
   }
   const int64_t sms = sm_count();
   auto tiles = [&](int bm, int bn) { return ceil_div(M, bm) * ceil_div(N, bn); };
+  // 128 < M <= 256 with every 256 x 160 tile on a CTA pair in one wave: split K over the pair
+  // (half the A and B bytes per SM). TOB_GEMM_KSPLIT=0 disables it (measurements).
+  static const bool ks2_on = [] {
+    const char* v = getenv("TOB_GEMM_KSPLIT");
+    return v == nullptr || v[0] != '0';
+  }();
+  if (ks2_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && K >= 2 * (128 / KindTraits<KD>::kElemBytes))
+    return launch_gemm_cfg<KD, 256, 160, 4, true>(a, b, M, N, K, ep, st);
   if (M > 256 || tiles(128, 256) >= sms) return launch_gemm_cfg<KD, 128, 256, 4>(a, b, M, N, K, ep, st);
   if (M <= 128) {
     if (tiles(128, 128) <= sms && tiles(128, 64) > sms)

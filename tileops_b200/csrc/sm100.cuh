@@ -138,6 +138,42 @@ __device__ __forceinline__ void bulk_wait_read() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// Cluster-wide barrier with release/acquire ordering of shared memory (distributed shared
+// memory stores before it are visible to every CTA of the cluster after it). The warp is
+// reconverged first so that the aligned barrier counts it once, after all of its lanes' work.
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Split cluster barrier: arrive (release) now, wait (acquire) later; work in between overlaps.
+__device__ __forceinline__ void cluster_arrive_release() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  __syncwarp();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared::cluster address of `addr` (a shared::cta address) in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Bulk copy (no multicast) of `bytes` (multiple of 16) from this CTA's shared memory to a
+// peer CTA's shared memory, completing on the peer's mbarrier (both shared::cluster addresses).
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes,
+                                                  uint32_t peer_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "r"(smem_u32(src)), "r"(bytes), "r"(peer_bar)
+      : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory accesses before later async-proxy ones:
 // stores before a tensor-core or TMA-store read of them, and loads before a TMA load that
 // refills the same buffer once it has been released.
