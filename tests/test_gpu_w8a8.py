@@ -194,3 +194,22 @@ def test_fp8_ksplit_pair_vs_oracle(cuda, m, n, k):
     want = ofp8.block_matmul(qa.view(torch.uint8).cpu().numpy(), qb.view(torch.uint8).cpu().numpy(),
                              sa.cpu().numpy(), sb.reshape(1, 1).cpu().numpy(), (n, k), "bf16")
     np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 11008, 4096), (200, 1000, 640)])
+def test_int8_pair_accumulators_with_bf16_output(cuda, m, n, k):
+    """The 2-CTA (cta_group::2) tiles take 128 < M <= 256 layers with a 16-bit output: the raw
+    int32 accumulators they emit next to the bf16 output are bit-exact."""
+    from tileops_b200.quant_int8 import _run_w8a8
+
+    g = torch.Generator().manual_seed(3 * m + n + k)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand(m, 1, generator=g) * 0.045 + 0.005
+    b_s = torch.rand(n, 1, generator=g) * 0.009 + 0.001
+    acc = torch.empty(m, n, dtype=torch.int32, device=cuda)
+    y = _run_w8a8("to_w8a8_i8_gemm", "w8a8_block_int8_matmul", a.to(cuda), b.to(cuda), a_s.to(cuda),
+                  b_s.to(cuda), 1, k, m, n, k, torch.bfloat16, acc_out=acc)
+    assert np.array_equal(acc.cpu().numpy().astype(np.int64), oi8.accumulators(a.numpy(), b.numpy()))
+    want = oi8.block_matmul(a.numpy(), b.numpy(), a_s.numpy(), b_s.numpy(), (1, k), "bf16")
+    np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)

@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty + buf);
     }
-    if (lane == 0) bulk_wait_all();
+    if (lane == 0) bulk_wait_read<0>();  // stores have read their slabs
   }
 
   tc_fence_before();

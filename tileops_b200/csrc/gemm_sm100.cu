@@ -394,7 +394,7 @@ __device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_
   }
   tc_fence_before();
   __syncwarp();
-  if (ep.tma_store && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+  if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
   if (ptr) ptr[5] = globaltimer_ns();
   cluster_wait_acquire();
 }
@@ -693,7 +693,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (etr) ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + blockIdx.x * 2 + 1] = globaltimer_ns();
       if (lane == 0) mbar_arrive(tempty + buf);
     }
-    if (ep.tma_store && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+    if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
   }
 
   tc_fence_before();
@@ -701,6 +701,229 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<C::kTmemCols>(tmem);
+  }
+}
+
+// ------------------------------------------------------------------ 2-CTA tiles
+// k_gemm_pair: one 256 x BN output tile per CTA pair (a (2,1,1) cluster), M <= 256. The pair
+// runs tcgen05 with cta_group::2: each CTA streams its 128 rows of A and its BN/2 rows of B
+// into its own ring (TMA completing on the leader's barriers), the leader's single thread
+// issues M=256 x N=BN MMAs that read both CTAs' halves, and each CTA's TMEM receives the
+// full-K sums of its own 128 rows. Per SM that is half of A and half of B of the tile, as in the
+// K-split pair, with no partial sums to exchange.
+template <Kind KD, int BN, int STAGES>
+struct PairCfg {
+  static constexpr int kElem = KindTraits<KD>::kElemBytes;
+  static constexpr int kBK = 128 / kElem;         // K elements per stage (one 128-byte row)
+  static constexpr int kABytes = 128 * 128;       // this CTA's 128 rows of A
+  static constexpr int kBBytes = (BN / 2) * 128;  // this CTA's BN/2 rows of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = pow2_at_least(BN);
+  static constexpr int kStageOutBytes = 32 * 32 * 2;
+  static constexpr int kOutSlabs = ((BN + 31) / 32) * 4;  // one per (chunk, lane quarter)
+  static constexpr size_t kSmem = (size_t)STAGES * kStageBytes + 256;
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "2-CTA tiles: N a multiple of 32");
+  static_assert((size_t)kOutSlabs * kStageOutBytes <= (size_t)STAGES * kStageBytes, "slabs");
+  static_assert(kSmem <= 232448, "shared memory");
+};
+
+template <Kind KD, int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC16,
+                int M, int N, int K, Epi ep, int* err) {
+  using C = PairCfg<KD, BN, STAGES>;
+  using Tr = KindTraits<KD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sA = smem_raw;
+  uint8_t* sB = smem_raw + (size_t)STAGES * C::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + (size_t)STAGES * C::kStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* drain = tfull + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = (int)(blockIdx.x & 1);  // 0: the leader, which issues the MMAs
+  const int t = (int)(blockIdx.x >> 1);    // one tile per pair
+  const int n_tiles = (N + BN - 1) / BN;
+  const int mt = t / n_tiles, nt = t - mt * n_tiles;
+  const int kblocks = (K + C::kBK - 1) / C::kBK;
+  const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);   // the leader's producer arrives; both CTAs' bytes complete it
+      mbar_init(empty + s, 1);  // the leader's commit, multicast to both CTAs
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (ep.tma_store) {
+      prefetch_tmap(&tmC);
+      prefetch_tmap(&tmC16);
+    }
+    if (misaligned && err) atomicExch(err, (int)kErrSmemAlign);
+  }
+  // The leader's own copies complete on its own barriers, so it requests its first ring of
+  // stages before the cluster barrier (the peer must wait for the leader's barriers to exist).
+  int pre = 0;
+  uint64_t pol_a = 0, pol_b = 0;
+  const int k0 = k_start(t, kblocks);
+  if (threadIdx.x == 0 && !misaligned) {
+    pol_a = make_policy(ep.policy_a);
+    pol_b = make_policy(ep.policy_b);
+    if (rank == 0) {
+      pre = min(STAGES, kblocks);
+      const uint32_t lead_full = smem_u32(full);
+      for (int it = 0; it < pre; ++it) {
+        const int kb = (k0 + it) % kblocks;
+        mbar_arrive_expect_tx(full + it, 2 * C::kStageBytes);
+        tma_load_2d_pair(sA + (size_t)it * C::kABytes, &tmA, kb * C::kBK, mt * 256, lead_full + it * 8u,
+                         pol_a);
+        tma_load_2d_pair(sB + (size_t)it * C::kBBytes, &tmB, kb * C::kBK, nt * BN,
+                         lead_full + it * 8u, pol_b);
+      }
+    }
+  }
+  if (warp == 1) tmem_alloc_pair<C::kTmemCols>(tmem_holder);
+  tc_fence_before();
+  // Both CTAs' barriers exist before the peer's copies and the leader's commits signal them.
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (misaligned) {
+    // nothing to do; fall through to the teardown
+  } else if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
+      uint32_t s = (uint32_t)(pre % STAGES), ph = pre == STAGES ? 1u : 0u;
+      // the leader's expectations (the pre-requested ring is phase 0), for unwinding
+      uint32_t issued_mask = (1u << pre) - 1u, issued_phase = 0;
+      bool ok = true;
+      for (int it = pre; it < kblocks; ++it) {
+        const int kb = (k0 + it) % kblocks;
+        if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
+        if (rank == 0) {
+          mbar_arrive_expect_tx(full + s, 2 * C::kStageBytes);
+          issued_mask |= 1u << s;
+          issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
+        }
+        const uint32_t bar = lead_full + (uint32_t)s * 8u;
+        tma_load_2d_pair(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * 256 + rank * 128,
+                         bar, pol_a);
+        tma_load_2d_pair(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK,
+                         nt * BN + rank * (BN / 2), bar, pol_b);
+        if (++s == STAGES) { s = 0; ph ^= 1; }
+      }
+      if (!ok && rank == 0) {
+        // Unwinding: the leader's full barriers count both CTAs' bytes; let them land.
+        for (int i = 0; i < STAGES; ++i)
+          if (issued_mask & (1u << i)) {
+            const uint64_t tw = globaltimer_ns();
+            while (!mbar_try_wait(full + i, (issued_phase >> i) & 1u) &&
+                   globaltimer_ns() - tw < kWaitLimitNs) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, 256, BN);
+      uint32_t s = 0, ph = 0;
+      bool ok = true, any = false;
+      for (int it = 0; it < kblocks; ++it) {
+        if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
+        const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_pair<KD>(tmem, smem_desc_kmajor_sw128(a0 + 32 * k),
+                        smem_desc_kmajor_sw128(b0 + 32 * k), idesc, (it | k) != 0);
+        any = true;
+        umma_commit_pair_mc(empty + s, 0x3);
+        if (++s == STAGES) { s = 0; ph ^= 1; }
+      }
+      if (ok) {
+        umma_commit_pair_mc(tfull, 0x3);
+      } else if (any) {
+        // Unwinding: wait (bounded) until the MMAs already issued have finished.
+        umma_commit_pair(drain);
+        const uint64_t tw = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - tw < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;          // the TMEM lane quarter this warp may read
+    const int eg = (warp - 2) >> 2;  // which of the two warps on that quarter
+    float sbt[(BN + 31) / 32];
+    load_tile_col_scales<BN>(sbt, ep, nt * BN, N, lane);
+    const int row0 = mt * 256 + rank * 128 + q * 32;  // first row of this warp's 32-row slab
+    const int row = row0 + lane;
+    const bool row_ok = row < M;
+    const float sa = row_ok ? __ldg(ep.a_s + (int64_t)row * ep.a_s_ld) : 0.f;
+    const bool ok = mbar_wait(tfull, 0, abort_flag, err);
+    tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        if (((c0 / 32) & 1) != eg) continue;  // the two warps of a quarter alternate chunks
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+        tmem_ld16(taddr, r);
+        tmem_ld16(taddr + 16, r + 16);
+        tmem_ld_wait();
+        const int col0 = nt * BN + c0;
+        if (col0 >= N) continue;
+        const int valid = min(32, N - col0);
+        float v[32];
+        scale_chunk32<KD, BN>(r, v, sa, sbt, c0);
+        if (KD == Kind::I8 && ep.acc_out != nullptr && row_ok) {
+          int32_t* dst = ep.acc_out + (int64_t)row * N + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < valid) dst[j] = (int32_t)r[j];
+        }
+        if (ep.tma_store) {
+          // After tfull every MMA has read its operands: the ring holds the output slabs.
+          uint8_t* stg = smem_raw + (size_t)((c0 / 32) * 4 + q) * C::kStageOutBytes;
+          uint32_t pk[16];
+          pack_out16(v, pk, ep, col0, valid);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, col0, row0, stg);
+            bulk_commit();
+          }
+        } else if (row_ok) {
+          store_direct<KD>(v, ep, (int64_t)row * N + col0, col0, valid, N);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // both epilogues are done with TMEM; no signal to a peer is pending
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair<C::kTmemCols>(tmem);
   }
 }
 
@@ -942,6 +1165,47 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
   }
 }
 
+template <Kind KD, int BN, int STAGES>
+int launch_gemm_pair(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
+                     cudaStream_t st) {
+  using C = PairCfg<KD, BN, STAGES>;
+  auto kern = k_gemm_pair<KD, BN, STAGES>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "tcgen05 2-CTA gemm: shared memory attribute");
+  CUtensorMap ta, tb, tc32, tc16;
+  int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, 128);
+  if (!rc) rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, BN / 2);
+  if (rc) return rc;
+  Epi e2 = ep;
+  memset(&tc32, 0, sizeof(tc32));
+  memset(&tc16, 0, sizeof(tc16));
+  if (e2.tma_store) {
+    rc = make_tmap_out16(&tc32, e2.c, M, N, 32, e2.c_dtype);
+    if (rc) return rc;
+  }
+  const int64_t tiles = ceil_div(M, 256) * ceil_div(N, BN);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * tiles), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc32, tc16, (int)M, (int)N, (int)K, e2,
+                                     device_error_ptr());
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 2-CTA gemm launch");
+  return check_launch("tcgen05 2-CTA gemm");
+}
+
 // Tile shapes: large problems take 128 x 256 tiles; small-M layers (M <= 256, the decode /
 // small-batch regime, HBM-bound on B) take the narrowest N tile that still fits every tile
 // in one wave, so all SMs stream B at once.
@@ -978,6 +1242,15 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
     const char* v = getenv("TOB_GEMM_KSPLIT");
     return v == nullptr || v[0] != '0';
   }();
+  // Those with a 16-bit output (TMA-stored rows) run as 2-CTA (cta_group::2) tiles of
+  // 256 x 160: the same halved operand bytes per SM, without the partial-sum exchange.
+  // TOB_GEMM_PAIR=0 keeps them on the K-split pair (measurements).
+  static const bool pair_on = [] {
+    const char* v = getenv("TOB_GEMM_PAIR");
+    return v == nullptr || v[0] != '0';
+  }();
+  if (pair_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && ep.tma_store)
+    return launch_gemm_pair<KD, 160, 8>(a, b, M, N, K, ep, st);
   if (ks2_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && K >= 2 * (128 / KindTraits<KD>::kElemBytes))
     return launch_gemm_cfg<KD, 256, 160, 4, true>(a, b, M, N, K, ep, st);
   if (M > 256 || tiles(128, 256) >= sms) return launch_gemm_cfg<KD, 128, 256, 4>(a, b, M, N, K, ep, st);
