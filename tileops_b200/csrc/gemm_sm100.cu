@@ -752,6 +752,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int kblocks = (K + C::kBK - 1) / C::kBK;
   const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
 
+  // Tuning timeline (null in production): per stage the producer's issue time and (leader) the
+  // MMA thread's land time; per CTA entry, roles start, accumulators ready, epilogue end.
+  uint64_t* phases = ep.trace != nullptr ? ep.trace + (int64_t)gridDim.x * ep.trace_steps * 3 +
+                                               gridDim.x * 2 + (int64_t)blockIdx.x * 32
+                                         : nullptr;
+  if (phases && threadIdx.x == 0) phases[0] = globaltimer_ns();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full + s, 1);   // the leader's producer arrives; both CTAs' bytes complete it
@@ -769,33 +775,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     if (misaligned && err) atomicExch(err, (int)kErrSmemAlign);
   }
-  // The leader's own copies complete on its own barriers, so it requests its first ring of
-  // stages before the cluster barrier (the peer must wait for the leader's barriers to exist).
+  // First ring of stages, requested before the tensor-memory allocation: the leader's copies
+  // complete on its own barriers, so it starts at once; the peer's complete on the leader's, so
+  // it starts right after a cluster barrier that publishes them.
   int pre = 0;
   uint64_t pol_a = 0, pol_b = 0;
   const int k0 = k_start(t, kblocks);
-  if (threadIdx.x == 0 && !misaligned) {
+  auto request_first_ring = [&]() {
     pol_a = make_policy(ep.policy_a);
     pol_b = make_policy(ep.policy_b);
-    if (rank == 0) {
-      pre = min(STAGES, kblocks);
-      const uint32_t lead_full = smem_u32(full);
-      for (int it = 0; it < pre; ++it) {
-        const int kb = (k0 + it) % kblocks;
-        mbar_arrive_expect_tx(full + it, 2 * C::kStageBytes);
-        tma_load_2d_pair(sA + (size_t)it * C::kABytes, &tmA, kb * C::kBK, mt * 256, lead_full + it * 8u,
-                         pol_a);
-        tma_load_2d_pair(sB + (size_t)it * C::kBBytes, &tmB, kb * C::kBK, nt * BN,
-                         lead_full + it * 8u, pol_b);
-      }
+    pre = min(STAGES, kblocks);
+    const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
+    for (int it = 0; it < pre; ++it) {
+      const int kb = (k0 + it) % kblocks;
+      if (ep.trace != nullptr && it < ep.trace_steps)
+        ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
+      if (rank == 0) mbar_arrive_expect_tx(full + it, 2 * C::kStageBytes);
+      tma_load_2d_pair(sA + (size_t)it * C::kABytes, &tmA, kb * C::kBK, mt * 256 + rank * 128,
+                       lead_full + it * 8u, pol_a);
+      tma_load_2d_pair(sB + (size_t)it * C::kBBytes, &tmB, kb * C::kBK, nt * BN + rank * (BN / 2),
+                       lead_full + it * 8u, pol_b);
     }
-  }
+  };
+  // The cluster barrier that publishes both CTAs' barriers is split: every thread arrives at
+  // once, the leader's first ring and the tensor-memory allocation run while it completes.
+  if (phases && threadIdx.x == 0) phases[4] = globaltimer_ns();
+  cluster_arrive_relaxed();
+  if (threadIdx.x == 0 && !misaligned && rank == 0) request_first_ring();
+  if (phases && threadIdx.x == 32) phases[6] = globaltimer_ns();
   if (warp == 1) tmem_alloc_pair<C::kTmemCols>(tmem_holder);
+  if (phases && threadIdx.x == 32) phases[7] = globaltimer_ns();
+  cluster_wait_acquire();  // both CTAs' barriers exist: copies and commits may signal them
+  if (phases && threadIdx.x == 0) phases[5] = globaltimer_ns();
+  if (threadIdx.x == 0 && !misaligned && rank == 1) request_first_ring();
   tc_fence_before();
-  // Both CTAs' barriers exist before the peer's copies and the leader's commits signal them.
-  cluster_sync_all();
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  if (phases && threadIdx.x == 0) phases[1] = globaltimer_ns();
 
   if (misaligned) {
     // nothing to do; fall through to the teardown
@@ -810,6 +827,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int it = pre; it < kblocks; ++it) {
         const int kb = (k0 + it) % kblocks;
         if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
+        if (ep.trace != nullptr && it < ep.trace_steps)
+          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
         if (rank == 0) {
           mbar_arrive_expect_tx(full + s, 2 * C::kStageBytes);
           issued_mask |= 1u << s;
@@ -842,6 +861,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int it = 0; it < kblocks; ++it) {
         if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
         tc_fence_after();
+        if (ep.trace != nullptr && it < ep.trace_steps)
+          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 1] = globaltimer_ns();
         const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
         const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
 #pragma unroll
@@ -874,6 +895,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const float sa = row_ok ? __ldg(ep.a_s + (int64_t)row * ep.a_s_ld) : 0.f;
     const bool ok = mbar_wait(tfull, 0, abort_flag, err);
     tc_fence_after();
+    if (phases && warp == 2 && lane == 0) phases[2] = globaltimer_ns();
     if (ok) {
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -917,6 +939,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_before();
     __syncwarp();
     if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
+    if (phases && warp == 2 && lane == 0) phases[3] = globaltimer_ns();
   }
 
   tc_fence_before();

@@ -152,6 +152,12 @@ __device__ __forceinline__ void cluster_arrive_release() {
   __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
+// Arrive without release ordering: enough to publish mbarrier initialisation that a
+// fence.mbarrier_init.release.cluster already ordered.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait_acquire() {
   __syncwarp();
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
