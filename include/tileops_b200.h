@@ -62,6 +62,14 @@ TO_API int to_device_check(int device);
 /* Reads (and with clear != 0 resets) the device-side error word that kernels with bounded
  * waits set when a wait gives up: 0 = no error. Synchronises the current device. */
 TO_API int to_device_error_word(int* value, int clear);
+/* Self-test of the bounded waits (library extension, no reference counterpart). One warp waits
+ * on a shared-memory mbarrier through the same bounded wait the GEMM pipelines use, with a
+ * limit of limit_us microseconds (1 .. 1000000). arrive != 0: the barrier is arrived at first
+ * and the wait completes. arrive == 0: nothing arrives, the wait gives up after the limit,
+ * records 1 (wait timeout) in the device error word and the kernel returns; the context stays
+ * usable. out (device memory, 2 x u64) receives {completed ? 1 : 0, nanoseconds waited}.
+ * Asynchronous on stream. */
+TO_API int to_wait_limit_selftest(int limit_us, int arrive, unsigned long long* out, void* stream);
 /* Launch overlap for the streaming small-M AWQ kernel (programmatic dependent launch): with
  * enable = 1, a launch may start reading its weights, zeros and scales while the previous
  * kernel in the stream is still running; x is read and y written only after that kernel has

@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_last_error_string": (ctypes.c_char_p, []),
     "to_device_check": (_I, [_I]),
     "to_device_error_word": (_I, [ctypes.POINTER(_I), _I]),
+    "to_wait_limit_selftest": (_I, [_I, _I, _P, _P]),
     "to_set_launch_overlap": (_I, [_I]),
     "to_quant_per_tensor_i8": (_I, [_P, _I, _P, _P, _L, _P]),
     "to_dequant_per_tensor_i8": (_I, [_P, _P, _P, _I, _L, _P]),
@@ -155,6 +156,15 @@ def device_error_word(clear: bool = True) -> int:
     v = ctypes.c_int(0)
     check(load().to_device_error_word(ctypes.byref(v), 1 if clear else 0), "device_error_word")
     return v.value
+
+
+def wait_limit_selftest(limit_us: int, arrive: bool, out_ptr: int, stream: int = 0) -> None:
+    """Launches the bounded-wait self-test: one warp waits on an mbarrier for at most
+    `limit_us` microseconds; with `arrive` False nothing arrives and the wait gives up, setting
+    the device error word to 1. `out_ptr` is a device buffer of two u64 that receives
+    {completed, nanoseconds waited}."""
+    check(load().to_wait_limit_selftest(int(limit_us), 1 if arrive else 0, out_ptr, stream),
+          "wait_limit_selftest")
 
 
 def version() -> str:

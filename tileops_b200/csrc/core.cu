@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace tob {
 
@@ -62,6 +63,32 @@ int* device_error_ptr() {
 
 static std::atomic<int> g_launch_overlap{0};
 bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
+
+// One warp waits on an mbarrier of arrival count 1 through the same bounded wait the GEMM
+// pipelines use. With `arrive` set, lane 0 arrives first and the wait completes at once; without
+// it nothing arrives, so the wait runs to `limit_ns`, records the timeout in the device error
+// word and returns. `out[0]` receives 1 when the wait completed and 0 when it gave up, `out[1]`
+// the nanoseconds the wait took.
+__global__ void k_wait_limit_selftest(uint64_t limit_ns, int arrive, int* err,
+                                      unsigned long long* out) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && arrive) sm100::mbar_arrive(&bar);
+  const uint64_t t0 = sm100::globaltimer_ns();
+  const bool ok = sm100::mbar_wait(&bar, 0, &abort_flag, err, limit_ns);
+  const uint64_t t1 = sm100::globaltimer_ns();
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    out[0] = ok ? 1ull : 0ull;
+    out[1] = t1 - t0;
+  }
+}
 }  // namespace tob
 
 extern "C" {
@@ -84,6 +111,20 @@ int to_device_check(int device) {
 int to_set_launch_overlap(int enable) {
   if (enable < 0) return tob::g_launch_overlap.load();
   return tob::g_launch_overlap.exchange(enable ? 1 : 0);
+}
+
+int to_wait_limit_selftest(int limit_us, int arrive, unsigned long long* out, void* stream) {
+  if (limit_us < 1 || limit_us > 1000000)
+    return tob::fail(TO_EINVAL, "to_wait_limit_selftest: limit_us %d outside [1, 1000000]",
+                     limit_us);
+  if (!out) return tob::fail(TO_EINVAL, "to_wait_limit_selftest: null output pointer");
+  int* err = tob::device_error_ptr();
+  if (!err) return tob::fail(TO_ECUDA, "to_wait_limit_selftest: device error word unavailable");
+  tob::k_wait_limit_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      (uint64_t)limit_us * 1000ull, arrive ? 1 : 0, err, out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return tob::cuda_fail(e, "to_wait_limit_selftest: launch");
+  return TO_OK;
 }
 
 int to_device_error_word(int* value, int clear) {

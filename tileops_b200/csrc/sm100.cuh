@@ -61,10 +61,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase of parity `parity` to complete. Gives up when `*abort` becomes non-zero
-// (another role failed) or after kWaitLimitNs; in the latter case it records the timeout in
+// (another role failed) or after `limit_ns`; in the latter case it records the timeout in
 // the device error word and raises `*abort` so every role of the CTA unwinds.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* err) {
+                                          int* err, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -72,7 +72,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort = 1;
       if (err) atomicExch(err, (int)kErrWaitTimeout);
       return false;
