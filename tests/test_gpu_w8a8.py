@@ -213,3 +213,54 @@ def test_int8_pair_accumulators_with_bf16_output(cuda, m, n, k):
     assert np.array_equal(acc.cpu().numpy().astype(np.int64), oi8.accumulators(a.numpy(), b.numpy()))
     want = oi8.block_matmul(a.numpy(), b.numpy(), a_s.numpy(), b_s.numpy(), (1, k), "bf16")
     np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)
+
+
+def test_int8_pair_launch_overlap_chain(cuda):
+    """A chain of 2-CTA INT8 layers (each bf16 output quantised per token into the next
+    layer's input) gives bit-identical results with launch overlap on and off, eagerly and
+    replayed from a CUDA graph; the first layer also matches the oracle."""
+    g = torch.Generator().manual_seed(33)
+    m, dims = 200, [4096, 2048, 4096, 1024]
+    layers = []
+    for k, n in zip(dims[:-1], dims[1:]):
+        w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+        w_s = torch.rand(n, 1, generator=g) * 0.002 + 0.0005
+        layers.append((w.to(cuda), w_s.to(cuda)))
+    x = (torch.randn(m, dims[0], generator=g) * 2).to(torch.bfloat16).to(cuda)
+    torch.cuda.synchronize()
+
+    def chain(v):
+        outs = []
+        for w, w_s in layers:
+            q, q_s = tob.per_token_quant_int8(v)
+            v = tob.w8a8_block_int8_matmul(q, w, q_s, w_s, [1, w.shape[1]],
+                                           output_dtype=torch.bfloat16)
+            outs.append(v)
+        return outs
+
+    prev = tob.set_launch_overlap(False)
+    try:
+        ref = chain(x)
+        tob.set_launch_overlap(True)
+        for _ in range(3):
+            assert all(torch.equal(a, b) for a, b in zip(chain(x), ref))
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            chain(x)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = chain(x)
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            assert all(torch.equal(a, b) for a, b in zip(outs, ref))
+        del graph
+    finally:
+        tob.set_launch_overlap(prev)
+    q, q_s = tob.per_token_quant_int8(x)
+    w, w_s = layers[0]
+    want = oi8.block_matmul(q.cpu().numpy(), w.cpu().numpy(), q_s.cpu().numpy(),
+                            w_s.cpu().numpy(), (1, dims[0]), "bf16")
+    np.testing.assert_allclose(_f(ref[0]), want, rtol=1e-2, atol=1e-2)

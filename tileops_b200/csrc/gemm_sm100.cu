@@ -55,6 +55,9 @@ struct Epi {
 // warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue (two per TMEM lane quarter)
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+// The 2-CTA kernel adds an eleventh warp that issues the B copies.
+constexpr int kPairBWarp = 2 + kEpiWarps;
+constexpr int kPairThreads = kGemmThreads + 32;
 
 __host__ __device__ constexpr int pow2_at_least(int v) {
   int p = 32;
@@ -711,28 +714,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // issues M=256 x N=BN MMAs that read both CTAs' halves, and each CTA's TMEM receives the
 // full-K sums of its own 128 rows. Per SM that is half of A and half of B of the tile, as in the
 // K-split pair, with no partial sums to exchange.
-template <Kind KD, int BN, int STAGES>
+template <Kind KD, int BN, int STAGES, int KC>
 struct PairCfg {
   static constexpr int kElem = KindTraits<KD>::kElemBytes;
-  static constexpr int kBK = 128 / kElem;         // K elements per stage (one 128-byte row)
-  static constexpr int kABytes = 128 * 128;       // this CTA's 128 rows of A
-  static constexpr int kBBytes = (BN / 2) * 128;  // this CTA's BN/2 rows of B
+  static constexpr int kBK = KC * 128 / kElem;         // K elements per stage (KC 128-byte slices)
+  static constexpr int kAChunk = 128 * 128;            // one slice of this CTA's 128 rows of A
+  static constexpr int kBChunk = (BN / 2) * 128;       // one slice of this CTA's BN/2 rows of B
+  static constexpr int kABytes = KC * kAChunk;
+  static constexpr int kBBytes = KC * kBChunk;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = pow2_at_least(BN);
   static constexpr int kStageOutBytes = 32 * 32 * 2;
   static constexpr int kOutSlabs = ((BN + 31) / 32) * 4;  // one per (chunk, lane quarter)
   static constexpr size_t kSmem = (size_t)STAGES * kStageBytes + 256;
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "2-CTA tiles: N a multiple of 32");
+  static_assert(KC == 1 || KC == 2 || KC == 4, "1, 2 or 4 K slices per stage");
   static_assert((size_t)kOutSlabs * kStageOutBytes <= (size_t)STAGES * kStageBytes, "slabs");
   static_assert(kSmem <= 232448, "shared memory");
 };
 
-template <Kind KD, int BN, int STAGES>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <Kind KD, int BN, int STAGES, int KC>
+__global__ void __launch_bounds__(kPairThreads, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC16,
                 int M, int N, int K, Epi ep, int* err) {
-  using C = PairCfg<KD, BN, STAGES>;
+  using C = PairCfg<KD, BN, STAGES, KC>;
   using Tr = KindTraits<KD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sA = smem_raw;
@@ -778,36 +784,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // First ring of stages, requested before the tensor-memory allocation: the leader's copies
   // complete on its own barriers, so it starts at once; the peer's complete on the leader's, so
   // it starts right after a cluster barrier that publishes them.
+  //
+  // Two warps issue the copies: warp 0 those of A (and, on the leader, the expectation of both
+  // CTAs' bytes of a stage), warp kPairBWarp those of B. A warp's bulk tensor copies are
+  // processed one after another, so two issuing warps keep twice as many requests moving. Under
+  // programmatic dependent launch B (the weights) streams in while the previous kernel
+  // finishes; A is requested after it has completed.
+  const bool a_issuer = threadIdx.x == 0;
+  const bool b_issuer = threadIdx.x == kPairBWarp * 32;
   int pre = 0;
-  uint64_t pol_a = 0, pol_b = 0;
+  uint64_t pol = 0;
   const int k0 = k_start(t, kblocks);
+  // This thread's copy of stage slot s for K block kb: A (a_issuer) or B. With KC = 2 the
+  // operand maps are 3-D views {128 bytes, rows, K slices} and one copy brings KC slices.
+  auto load_stage = [&](int s, int kb, uint32_t bar) {
+    if (a_issuer) {
+      if (KC == 1)
+        tma_load_2d_pair(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * 256 + rank * 128,
+                         bar, pol);
+      else
+        tma_load_3d_pair(sA + (size_t)s * C::kABytes, &tmA, 0, mt * 256 + rank * 128, kb * KC,
+                         bar, pol);
+    } else {
+      if (KC == 1)
+        tma_load_2d_pair(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK,
+                         nt * BN + rank * (BN / 2), bar, pol);
+      else
+        tma_load_3d_pair(sB + (size_t)s * C::kBBytes, &tmB, 0, nt * BN + rank * (BN / 2),
+                         kb * KC, bar, pol);
+    }
+  };
   auto request_first_ring = [&]() {
-    pol_a = make_policy(ep.policy_a);
-    pol_b = make_policy(ep.policy_b);
+    pol = make_policy(a_issuer ? ep.policy_a : ep.policy_b);
     pre = min(STAGES, kblocks);
     const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
+    if (a_issuer) grid_dependency_wait();  // A may be the previous kernel's output
     for (int it = 0; it < pre; ++it) {
       const int kb = (k0 + it) % kblocks;
-      if (ep.trace != nullptr && it < ep.trace_steps)
-        ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
-      if (rank == 0) mbar_arrive_expect_tx(full + it, 2 * C::kStageBytes);
-      tma_load_2d_pair(sA + (size_t)it * C::kABytes, &tmA, kb * C::kBK, mt * 256 + rank * 128,
-                       lead_full + it * 8u, pol_a);
-      tma_load_2d_pair(sB + (size_t)it * C::kBBytes, &tmB, kb * C::kBK, nt * BN + rank * (BN / 2),
-                       lead_full + it * 8u, pol_b);
+      if (a_issuer) {
+        if (ep.trace != nullptr && it < ep.trace_steps)
+          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
+        if (rank == 0) mbar_arrive_expect_tx(full + it, 2 * C::kStageBytes);
+        load_stage(it, kb, lead_full + it * 8u);
+      } else {
+        load_stage(it, kb, lead_full + it * 8u);
+      }
     }
   };
   // The cluster barrier that publishes both CTAs' barriers is split: every thread arrives at
   // once, the leader's first ring and the tensor-memory allocation run while it completes.
   if (phases && threadIdx.x == 0) phases[4] = globaltimer_ns();
   cluster_arrive_relaxed();
-  if (threadIdx.x == 0 && !misaligned && rank == 0) request_first_ring();
+  if ((a_issuer || b_issuer) && !misaligned && rank == 0) request_first_ring();
   if (phases && threadIdx.x == 32) phases[6] = globaltimer_ns();
   if (warp == 1) tmem_alloc_pair<C::kTmemCols>(tmem_holder);
   if (phases && threadIdx.x == 32) phases[7] = globaltimer_ns();
   cluster_wait_acquire();  // both CTAs' barriers exist: copies and commits may signal them
   if (phases && threadIdx.x == 0) phases[5] = globaltimer_ns();
-  if (threadIdx.x == 0 && !misaligned && rank == 1) request_first_ring();
+  if ((a_issuer || b_issuer) && !misaligned && rank == 1) request_first_ring();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -816,9 +850,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (misaligned) {
     // nothing to do; fall through to the teardown
-  } else if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer (both CTAs)
-    if (lane == 0) {
+  } else if (warp == 0 || warp == kPairBWarp) {
+    // ------------------------------------------------------------ TMA producers (both CTAs)
+    if (a_issuer || b_issuer) {
       const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
       uint32_t s = (uint32_t)(pre % STAGES), ph = pre == STAGES ? 1u : 0u;
       // the leader's expectations (the pre-requested ring is phase 0), for unwinding
@@ -827,29 +861,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int it = pre; it < kblocks; ++it) {
         const int kb = (k0 + it) % kblocks;
         if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
-        if (ep.trace != nullptr && it < ep.trace_steps)
-          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
-        if (rank == 0) {
-          mbar_arrive_expect_tx(full + s, 2 * C::kStageBytes);
-          issued_mask |= 1u << s;
-          issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
-        }
         const uint32_t bar = lead_full + (uint32_t)s * 8u;
-        tma_load_2d_pair(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * 256 + rank * 128,
-                         bar, pol_a);
-        tma_load_2d_pair(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK,
-                         nt * BN + rank * (BN / 2), bar, pol_b);
+        if (a_issuer) {
+          if (ep.trace != nullptr && it < ep.trace_steps)
+            ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
+          if (rank == 0) {
+            mbar_arrive_expect_tx(full + s, 2 * C::kStageBytes);
+            issued_mask |= 1u << s;
+            issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
+          }
+          load_stage((int)s, kb, bar);
+        } else {
+          load_stage((int)s, kb, bar);
+        }
         if (++s == STAGES) { s = 0; ph ^= 1; }
       }
-      if (!ok && rank == 0) {
-        // Unwinding: the leader's full barriers count both CTAs' bytes; let them land.
+      if (a_issuer) grid_dependents_launch();
+      if (!ok && rank == 0 && a_issuer) {
+        // Unwinding: the leader's full barriers count both CTAs' bytes; let them land. One
+        // deadline for all stages: a stage whose B copy was never issued does not complete.
+        const uint64_t tw = globaltimer_ns();
         for (int i = 0; i < STAGES; ++i)
-          if (issued_mask & (1u << i)) {
-            const uint64_t tw = globaltimer_ns();
+          if (issued_mask & (1u << i))
             while (!mbar_try_wait(full + i, (issued_phase >> i) & 1u) &&
                    globaltimer_ns() - tw < kWaitLimitNs) {
             }
-          }
+      } else if (!ok && b_issuer) {
+        // Unwinding: a B copy of a stage whose expectation the A issuer did not post cannot
+        // be observed on the barrier; a copy lands within microseconds, so give it 50 us.
+        const uint64_t tw = globaltimer_ns();
+        while (globaltimer_ns() - tw < 50000ull) {
+        }
       }
     }
   } else if (warp == 1) {
@@ -866,9 +908,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
         const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_pair<KD>(tmem, smem_desc_kmajor_sw128(a0 + 32 * k),
-                        smem_desc_kmajor_sw128(b0 + 32 * k), idesc, (it | k) != 0);
+        for (int k = 0; k < 4 * KC; ++k)
+          umma_pair<KD>(tmem, smem_desc_kmajor_sw128(a0 + (k / 4) * C::kAChunk + 32 * (k % 4)),
+                        smem_desc_kmajor_sw128(b0 + (k / 4) * C::kBChunk + 32 * (k % 4)), idesc,
+                        (it | k) != 0);
         any = true;
         umma_commit_pair_mc(empty + s, 0x3);
         if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -892,6 +935,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row0 = mt * 256 + rank * 128 + q * 32;  // first row of this warp's 32-row slab
     const int row = row0 + lane;
     const bool row_ok = row < M;
+    grid_dependency_wait();  // A's scales and the output: after the previous kernel
     const float sa = row_ok ? __ldg(ep.a_s + (int64_t)row * ep.a_s_ld) : 0.f;
     const bool ok = mbar_wait(tfull, 0, abort_flag, err);
     tc_fence_after();
@@ -967,29 +1011,32 @@ EncodeFn get_encode() {
   return fn;
 }
 
-// 2-D K-major operand [rows, cols] (cols contiguous, elem bytes each) tiled as
-// box_rows x 128 bytes with the 128-byte swizzle. Cached per (pointer, shape, box).
+// K-major operand [rows, cols] (cols contiguous, elem bytes each) tiled as box_rows x 128
+// bytes with the 128-byte swizzle; with slices > 1 a 3-D view {128 bytes, rows, 128-byte K
+// slices} whose box lands as `slices` consecutive [box_rows][128 B] tiles. Cached per
+// (pointer, shape, box).
 int make_tmap_kmajor(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
-                     int box_rows) {
+                     int box_rows, int slices) {
   struct Key {
     const void* p;
     int64_t rows, cols;
-    int elem, box;
+    int elem, box, slices;
     bool operator==(const Key& o) const {
-      return p == o.p && rows == o.rows && cols == o.cols && elem == o.elem && box == o.box;
+      return p == o.p && rows == o.rows && cols == o.cols && elem == o.elem && box == o.box &&
+             slices == o.slices;
     }
   };
   struct Hash {
     size_t operator()(const Key& k) const {
       return std::hash<const void*>()(k.p) ^ (size_t)(k.rows * 1315423911u) ^
-             (size_t)(k.cols * 2654435761u) ^ (size_t)(k.box * 97 + k.elem);
+             (size_t)(k.cols * 2654435761u) ^ (size_t)(k.box * 97 + k.elem + k.slices * 7919);
     }
   };
   static std::mutex mu;
   static std::unordered_map<Key, CUtensorMap, Hash> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const Key key{(const char*)ptr + ((int64_t)dev << 56), rows, cols, elem, box_rows};
+  const Key key{(const char*)ptr + ((int64_t)dev << 56), rows, cols, elem, box_rows, slices};
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
@@ -1000,14 +1047,29 @@ int make_tmap_kmajor(CUtensorMap* out, const void* ptr, int64_t rows, int64_t co
   }
   EncodeFn encode = get_encode();
   if (!encode) return fail(TO_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(cols * elem)};
-  cuuint32_t box[2] = {(cuuint32_t)(128 / elem), (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(out, elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
-                      2, const_cast<void*>(ptr), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (slices > 1 && (cols * elem) % 128 != 0)
+    return fail(TO_EINVAL, "K-slice view needs a row length that is a multiple of 128 bytes");
+  const CUtensorMapDataType dt =
+      elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUresult r;
+  if (slices <= 1) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * elem)};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / elem), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    r = encode(out, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[3] = {(cuuint64_t)(128 / elem), (cuuint64_t)rows,
+                          (cuuint64_t)(cols * elem / 128)};
+    cuuint64_t strides[2] = {(cuuint64_t)(cols * elem), 128};
+    cuuint32_t box[3] = {(cuuint32_t)(128 / elem), (cuuint32_t)box_rows, (cuuint32_t)slices};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = encode(out, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS)
     return fail(TO_ECUDA, "cuTensorMapEncodeTiled failed (%d) for [%lld, %lld] x %d B", (int)r,
                 (long long)rows, (long long)cols, elem);
@@ -1188,11 +1250,11 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
   }
 }
 
-template <Kind KD, int BN, int STAGES>
+template <Kind KD, int BN, int STAGES, int KC>
 int launch_gemm_pair(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                      cudaStream_t st) {
-  using C = PairCfg<KD, BN, STAGES>;
-  auto kern = k_gemm_pair<KD, BN, STAGES>;
+  using C = PairCfg<KD, BN, STAGES, KC>;
+  auto kern = k_gemm_pair<KD, BN, STAGES, KC>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -1200,8 +1262,8 @@ int launch_gemm_pair(const void* a, const void* b, int64_t M, int64_t N, int64_t
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "tcgen05 2-CTA gemm: shared memory attribute");
   CUtensorMap ta, tb, tc32, tc16;
-  int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, 128);
-  if (!rc) rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, BN / 2);
+  int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, 128, KC);
+  if (!rc) rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, BN / 2, KC);
   if (rc) return rc;
   Epi e2 = ep;
   memset(&tc32, 0, sizeof(tc32));
@@ -1213,16 +1275,21 @@ int launch_gemm_pair(const void* a, const void* b, int64_t M, int64_t N, int64_t
   const int64_t tiles = ceil_div(M, 256) * ceil_div(N, BN);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * tiles), 1, 1);
-  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = C::kSmem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (launch_overlap()) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc32, tc16, (int)M, (int)N, (int)K, e2,
                                      device_error_ptr());
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 2-CTA gemm launch");
@@ -1272,8 +1339,17 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
     const char* v = getenv("TOB_GEMM_PAIR");
     return v == nullptr || v[0] != '0';
   }();
-  if (pair_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && ep.tma_store)
-    return launch_gemm_pair<KD, 160, 8>(a, b, M, N, K, ep, st);
+  if (pair_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && ep.tma_store) {
+    // K slices per copy (measurement override TOB_PAIR_SLICES = 1, 2 or 4)
+    static const int slices = [] {
+      const char* v = getenv("TOB_PAIR_SLICES");
+      return v == nullptr ? 2 : atoi(v);
+    }();
+    if ((K * KindTraits<KD>::kElemBytes) % 128 != 0 || slices == 1)
+      return launch_gemm_pair<KD, 160, 8, 1>(a, b, M, N, K, ep, st);
+    if (slices == 4) return launch_gemm_pair<KD, 160, 2, 4>(a, b, M, N, K, ep, st);
+    return launch_gemm_pair<KD, 160, 4, 2>(a, b, M, N, K, ep, st);
+  }
   if (ks2_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && K >= 2 * (128 / KindTraits<KD>::kElemBytes))
     return launch_gemm_cfg<KD, 256, 160, 4, true>(a, b, M, N, K, ep, st);
   if (M > 256 || tiles(128, 256) >= sms) return launch_gemm_cfg<KD, 128, 256, 4>(a, b, M, N, K, ep, st);

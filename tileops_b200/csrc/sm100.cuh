@@ -257,9 +257,11 @@ enum class Kind : int { I8 = 0, E4M3 = 1, F16 = 2, BF16 = 3 };
 // ------------------------------------------------------------------ host-side tensor maps
 // (defined in gemm_sm100.cu)
 // K-major operand [rows, cols] of `elem`-byte elements as box_rows x 128-byte boxes with the
-// 128-byte swizzle; cached per (pointer, shape, box).
+// 128-byte swizzle; cached per (pointer, shape, box). slices > 1: a 3-D view {128 bytes, rows,
+// cols * elem / 128} whose boxes bring `slices` consecutive 128-byte K slices of box_rows rows
+// (cols * elem must be a multiple of 128).
 int make_tmap_kmajor(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
-                     int box_rows);
+                     int box_rows, int slices = 1);
 // 16-bit output [rows, cols] for staged epilogue stores: 32-row boxes of box_cols columns.
 int make_tmap_out16(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int box_cols,
                     int dtype);
@@ -382,6 +384,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(leader_bar), "l"(policy)
+      : "memory");
+}
+
+// 3-D form of tma_load_2d_pair (coordinates innermost first).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m, int x, int y,
+                                                 int z, uint32_t leader_bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(leader_bar), "l"(policy)
       : "memory");
 }
 
