@@ -152,6 +152,8 @@ def test_gemm_deterministic(cuda):
     (16, 1024, 2048, 32),     # group size 32: several group rows per stage
     (24, 512, 512, 512),      # four token tiles, G == K
     (32, 1024, 4096, 128),    # the largest M it takes
+    (32, 14336, 256, 128),    # 32 tokens of a long K chunk do not fit: two 16-token launches
+    (20, 14336, 512, 128),    # the same with a 4-token second launch
     (5, 256, 96, 256),        # 12 words: a partial column tile, G == K
     # prefetching SIMT stream (M <= 2, and shapes the TMA kernel does not take)
     (1, 4096, 28672, 128),    # 32-word column tiles

@@ -5,7 +5,7 @@
 // design keeps every SM's share of them in flight and spends as few instructions as possible
 // per weight once it lands:
 //   * TMA feed. One producer thread per CTA streams the CTA's K-chunk of packed weights as
-//     8 KB tensor copies (cp.async.bulk.tensor, no multicast; 64-256 rows of the column tile)
+//     8-16 KB tensor copies (cp.async.bulk.tensor, no multicast; 128-256 rows of the column tile)
 //     through a ring of shared-memory stages with mbarrier completion and bounded waits. The
 //     chunk's scales, zeros and x arrive once, one copy each (x through a 3-D view of 64-element
 //     blocks that lands in the 128-byte-swizzled layout), so each stage costs one TMA
@@ -49,13 +49,21 @@ namespace {
 
 constexpr int kSmConsumers = 4;
 constexpr int kSmThreads = 32 * (1 + kSmConsumers);
-constexpr int kSmStageBytes = 8192;  // one weight box per stage: (2048 / CW) rows x CW words
+constexpr int kSmMaxStageBytes = 16384;  // one weight box per stage, at most 256 rows
 constexpr int kSmMaxStages = 12;
-constexpr size_t kSmSmemLimit = 110 * 1024;  // two CTAs per SM
+constexpr size_t kSmSmemLimit = 112 * 1024;  // two CTAs per SM (228 KB, 1 KB reserved per CTA)
+constexpr int kSmCtasPerSm = 2;
+
+// Bytes of one stage (one TMA box of CW-word rows): as large as the 256-row box limit allows,
+// since every copy costs a roughly fixed time on top of its bytes.
+template <int CW>
+__host__ __device__ constexpr int sm_stage_bytes() {
+  return 256 * 4 * CW < kSmMaxStageBytes ? 256 * 4 * CW : kSmMaxStageBytes;
+}
 
 // Shared-memory plan of one CTA (offsets from a 1024-byte-aligned base):
 //   x      : kchunk/64 tiles of [NT*8 tokens x 128 B] (128-byte swizzle), one 3-D TMA box
-//   ring   : `stages` weight boxes of 8 KB
+//   ring   : `stages` weight boxes of sm_stage_bytes<CW>() (8 or 16 KB)
 //   scales : [szrows x 8CW] 16-bit, zeros : [szrows x CW] words -- the chunk's groups, one box each
 //   tot    : fragment-order partial sums [16*WPQ*NT][32] fp32
 //   barriers
@@ -107,15 +115,17 @@ __device__ __forceinline__ void consumer_bar() {
 // Grid: (column tiles of CW = 8*WPQ packed words, K-chunks); the K-chunks of a column tile
 // form one cluster. NT = 8-token tiles of M (1, 2 or 4 for M <= 8, 16, 32).
 template <typename T, int NT, int WPQ>
-__global__ void __launch_bounds__(kSmThreads) k_awq_small_m(
+__global__ void __launch_bounds__(kSmThreads, kSmCtasPerSm) k_awq_small_m(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
     T* __restrict__ y, int M, int K, int N, int G, int kchunk, int ksplit, SmPlan plan,
     int* err) {
   using H2 = typename Half2Of<T>::type;
   constexpr int CW = 8 * WPQ;
-  constexpr int kRows = kSmStageBytes / (4 * CW);  // K rows per stage: 64, 128 or 256
+  constexpr int kStageBytes = sm_stage_bytes<CW>();
+  constexpr int kRows = kStageBytes / (4 * CW);      // K rows per stage
   constexpr int kSteps = kRows / 16 / kSmConsumers;  // 16-row MMA steps per warp per stage
+  static_assert(kSteps >= 1 && kRows <= 256, "stage shape");
   constexpr int kXTile = 1024 * NT;                  // one 64-row block of x
   constexpr int kCols = CW * 8;
   const int stages = plan.stages;
@@ -162,8 +172,8 @@ __global__ void __launch_bounds__(kSmThreads) k_awq_small_m(
       const uint64_t pol_w = policy_evict_first();  // streamed once
       const uint64_t pol_x = policy_evict_last();   // re-read by every column tile
       auto issue_w = [&](int st, int slot) {
-        mbar_arrive_expect_tx(full + slot, kSmStageBytes);
-        tma_load_2d(ring + slot * kSmStageBytes, &tm_w, col0, kb + st * kRows, full + slot, pol_w);
+        mbar_arrive_expect_tx(full + slot, kStageBytes);
+        tma_load_2d(ring + slot * kStageBytes, &tm_w, col0, kb + st * kRows, full + slot, pol_w);
       };
       const int pre = min(nst, stages);
       for (int st = 0; st < pre; ++st) issue_w(st, st);
@@ -205,7 +215,7 @@ __global__ void __launch_bounds__(kSmThreads) k_awq_small_m(
     for (int st = 0; ok && st < nst; ++st) {
       const int slot = st % stages;
       if (!mbar_wait(full + slot, (st / stages) & 1, abort_flag, err)) break;
-      const uint32_t* wt = reinterpret_cast<const uint32_t*>(ring + slot * kSmStageBytes);
+      const uint32_t* wt = reinterpret_cast<const uint32_t*>(ring + slot * kStageBytes);
 #pragma unroll
       for (int u = 0; u < kSteps; ++u) {
         const int step = cw * kSteps + u;           // 16-row step within the stage
@@ -339,7 +349,7 @@ __global__ void __launch_bounds__(kSmThreads) k_awq_small_m(
 template <int NT, int WPQ>
 bool plan_small_m(int64_t K, int64_t G, int kchunk, SmPlan* p) {
   constexpr int CW = 8 * WPQ;
-  constexpr int kRows = kSmStageBytes / (4 * CW);
+  constexpr int kRows = sm_stage_bytes<CW>() / (4 * CW);
   p->x_bytes = (kchunk / 64) * 1024 * NT;
   p->szrows = G == K ? 1 : (int)(kchunk / G);
   p->s_bytes = round128(p->szrows * 8 * CW * 2);
@@ -351,7 +361,7 @@ bool plan_small_m(int64_t K, int64_t G, int kchunk, SmPlan* p) {
     if (want >= 1) p->stages = std::min(p->stages, want);
   }
   for (;;) {
-    p->ring_bytes = p->stages * kSmStageBytes;
+    p->ring_bytes = p->stages * sm_stage_bytes<CW>();
     if (p->total() <= kSmSmemLimit) return p->szrows <= 256 && kchunk / 64 <= 256;
     if (p->stages <= 2) return false;
     --p->stages;
@@ -362,7 +372,7 @@ template <typename T, int NT, int WPQ>
 int launch_small_m(const void* x, const int32_t* qw, const void* s, const int32_t* qz, void* y,
                    int64_t M, int64_t K, int64_t N, int64_t G, int ksplit, cudaStream_t st) {
   constexpr int CW = 8 * WPQ;
-  constexpr int kRows = kSmStageBytes / (4 * CW);
+  constexpr int kRows = sm_stage_bytes<CW>() / (4 * CW);
   const int64_t words = N / 8;
   const int tiles = (int)ceil_div(words, CW);
   // K-chunks are whole stages and whole groups; the x, scale and zero slices must fit too.
@@ -463,8 +473,18 @@ int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dt
   if (M <= 16)
     return f16 ? sm100::dispatch_small_m<__half, 2>(x, qw, s, qz, y, M, K, N, G, st)
                : sm100::dispatch_small_m<__nv_bfloat16, 2>(x, qw, s, qz, y, M, K, N, G, st);
-  return f16 ? sm100::dispatch_small_m<__half, 4>(x, qw, s, qz, y, M, K, N, G, st)
-             : sm100::dispatch_small_m<__nv_bfloat16, 4>(x, qw, s, qz, y, M, K, N, G, st);
+  int rc = f16 ? sm100::dispatch_small_m<__half, 4>(x, qw, s, qz, y, M, K, N, G, st)
+               : sm100::dispatch_small_m<__nv_bfloat16, 4>(x, qw, s, qz, y, M, K, N, G, st);
+  if (rc != TO_EUNSUPPORTED) return rc;
+  // 32 tokens of x for a long K chunk do not fit next to the weight ring: run the tokens as
+  // two launches of at most 16 (nothing was launched above).
+  const char* x2 = static_cast<const char*>(x) + (size_t)16 * K * 2;
+  char* y2 = static_cast<char*>(y) + (size_t)16 * N * 2;
+  rc = f16 ? sm100::dispatch_small_m<__half, 2>(x, qw, s, qz, y, 16, K, N, G, st)
+           : sm100::dispatch_small_m<__nv_bfloat16, 2>(x, qw, s, qz, y, 16, K, N, G, st);
+  if (rc != TO_OK) return rc;
+  return f16 ? sm100::dispatch_small_m<__half, 2>(x2, qw, s, qz, y2, M - 16, K, N, G, st)
+             : sm100::dispatch_small_m<__nv_bfloat16, 2>(x2, qw, s, qz, y2, M - 16, K, N, G, st);
 }
 
 }  // namespace tob
