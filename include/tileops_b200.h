@@ -62,6 +62,14 @@ TO_API int to_device_check(int device);
 /* Reads (and with clear != 0 resets) the device-side error word that kernels with bounded
  * waits set when a wait gives up: 0 = no error. Synchronises the current device. */
 TO_API int to_device_error_word(int* value, int clear);
+/* Device buffers shared between the processes of one node (plumbing for the gathering GEMM,
+ * no reference counterpart): to_ipc_alloc allocates `bytes` on the current device and writes
+ * its 64-byte CUDA IPC handle; to_ipc_open maps a peer's handle into this process (peer access
+ * enabled on demand); to_ipc_close unmaps it; to_ipc_free releases an own buffer. */
+TO_API int to_ipc_alloc(size_t bytes, void** ptr, void* handle);
+TO_API int to_ipc_open(const void* handle, void** ptr);
+TO_API int to_ipc_close(void* ptr);
+TO_API int to_ipc_free(void* ptr);
 /* Self-test of the bounded waits (library extension, no reference counterpart). One warp waits
  * on a shared-memory mbarrier through the same bounded wait the GEMM pipelines use, with a
  * limit of limit_us microseconds (1 .. 1000000). arrive != 0: the barrier is arrived at first
@@ -163,6 +171,20 @@ TO_API size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_
 TO_API int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
                 const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
                 int64_t group_size, void* workspace, size_t workspace_bytes, void* stream);
+/* Library extension for N-sharded layers (no reference counterpart; it fuses to_awq_gemm on a
+ * rank's column slice with the all-gather that follows it). The group's `world` ranks each
+ * hold N = N_full / world output columns of qweight/scales/qzeros; this rank computes its
+ * [M, N] slice on the tensor-core kernel and stores it straight into the [M, N * world]
+ * output of every rank, y_ranks[r] (host array of device pointers valid on this device: its
+ * own buffer and the peers' buffers mapped with to_ipc_open), at columns
+ * [rank * N, (rank + 1) * N). The stores have completed when the kernel has; the caller
+ * orders the peers' reads after every rank's kernel (one collective barrier) and must not
+ * reuse a buffer a peer may still read. TO_EUNSUPPORTED (nothing launched) for shapes outside
+ * the tensor-core kernel: run to_awq_gemm and an all-gather instead. */
+TO_API int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales,
+                              int s_dtype, const int32_t* qzeros, void* const* y_ranks,
+                              int world, int rank, int64_t M, int64_t K, int64_t N,
+                              int64_t group_size, void* stream);
 
 /* ---- W8A8 block-scaled GEMMs --------------------------------------------------------------
  * C[m,n] = sum_kb  (sum_{k in kb} A[m,k]*B[n,k]) * a_s[m,kb] * b_s[n/block_n, kb]

@@ -1,0 +1,96 @@
+"""The gathering AWQ GEMM of N-sharded layers on two GPUs of one node: each rank's tensor-core
+kernel stores its column slice into every rank's [M, N] output over NVLink (CUDA IPC mappings),
+one NCCL barrier follows. Checked against the unsharded layer on the same GPU and against the
+oracle on sampled columns. Needs two GPUs (skipped on a one-GPU box)."""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+import traceback
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=60), device_id=dev)
+        import tileops_b200 as tob
+        from oracle import awq as oawq
+        from tileops_b200 import sharded
+
+        k, n, gs = 1024, 2048, 128
+        g = torch.Generator().manual_seed(11)  # every rank builds the same full layer
+        w = torch.randint(0, 16, (k, n), generator=g)
+        z = torch.randint(0, 16, (k // gs, n), generator=g)
+        s = (torch.rand(k // gs, n, generator=g) * 0.018 + 0.002).bfloat16()
+        qw = torch.from_numpy(oawq.pack(w.numpy())).to(dev)
+        qz = torch.from_numpy(oawq.pack(z.numpy())).to(dev)
+        s = s.to(dev)
+        layer = sharded.ShardedAWQLinear(qw, s, qz)
+        report = {}
+        for m in (256, 40):
+            x = torch.randn(m, k, generator=g).bfloat16().to(dev)
+            full = tob.awq_gemm(x, qw, s, qz, 1)
+            y1 = layer.gathered(x).clone()
+            y2 = layer.gathered(x)  # the layer's other buffer
+            torch.cuda.synchronize()
+            cols = torch.arange(0, n, 37)
+            want = oawq.gemm(x.float().cpu().numpy(), qw.cpu().numpy(), s.float().cpu().numpy(),
+                             qz.cpu().numpy(), "bf16")[:, cols.numpy()]
+            report[m] = (
+                float((y1.float() - full.float()).abs().max()),
+                bool(torch.equal(y1, y2)),
+                float(np.abs(y1[:, cols.to(dev)].float().cpu().numpy() - want).max()),
+                float(np.abs(want).max()),
+            )
+        layer.close()
+        q.put((rank, "ok", report))
+    except Exception:  # noqa: BLE001
+        q.put((rank, "error", traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_awq_gathered_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, status, payload in results:
+        assert status == "ok", f"rank {rank}:\n{payload}"
+        for m, (vs_full, stable, vs_oracle, scale) in payload.items():
+            assert vs_full <= 1e-2 * max(1.0, scale), (rank, m, vs_full)
+            assert stable, (rank, m)
+            assert vs_oracle <= 1e-2 + 1e-2 * scale, (rank, m, vs_oracle)

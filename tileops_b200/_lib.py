@@ -65,6 +65,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_awq_dequant": (_I, [_P, _P, _I, _P, _P, _L, _L, _L, _P]),
     "to_awq_gemm_workspace_size": (_S, [_L, _L, _L, _L]),
     "to_awq_gemm": (_I, [_P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _P, _S, _P]),
+    "to_awq_gemm_gather": (_I, [_P, _P, _P, _I, _P, ctypes.POINTER(_P), _I, _I, _L, _L, _L, _L,
+                                _P]),
+    "to_ipc_alloc": (_I, [_S, ctypes.POINTER(_P), _P]),
+    "to_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "to_ipc_close": (_I, [_P]),
+    "to_ipc_free": (_I, [_P]),
     "to_w8a8_i8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _L, _P]),
     "to_w8a8_fp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _L, _L, _L, _L, _L, _P]),
 }
@@ -165,6 +171,35 @@ def wait_limit_selftest(limit_us: int, arrive: bool, out_ptr: int, stream: int =
     {completed, nanoseconds waited}."""
     check(load().to_wait_limit_selftest(int(limit_us), 1 if arrive else 0, out_ptr, stream),
           "wait_limit_selftest")
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Allocates `nbytes` on the current device; returns (device pointer, CUDA IPC handle)."""
+    p = _P(0)
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    check(load().to_ipc_alloc(int(nbytes), ctypes.byref(p), h), "ipc_alloc")
+    return int(p.value), h.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    """Maps a peer process's buffer (its IPC handle) into this process; returns the pointer."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"ipc_open: a handle has {IPC_HANDLE_BYTES} bytes (got {len(handle)})")
+    p = _P(0)
+    h = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    check(load().to_ipc_open(h, ctypes.byref(p)), "ipc_open")
+    return int(p.value)
+
+
+def ipc_close(ptr_value: int) -> None:
+    check(load().to_ipc_close(ptr_value), "ipc_close")
+
+
+def ipc_free(ptr_value: int) -> None:
+    check(load().to_ipc_free(ptr_value), "ipc_free")
 
 
 def version() -> str:

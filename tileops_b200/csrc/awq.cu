@@ -626,6 +626,9 @@ int check_awq_shapes(const char* op, int64_t K, int64_t N, int64_t G) {
 int awq_gemm_tc_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                        const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
                        cudaStream_t st);
+int awq_gemm_tc_gather_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                              const int32_t* qz, void* const* y_ranks, int world, int rank,
+                              int64_t M, int64_t K, int64_t N, int64_t G, cudaStream_t st);
 int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                        const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
                        cudaStream_t st);
@@ -734,6 +737,28 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
   }
   return awq_gemv_dispatch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size,
                            (cudaStream_t)stream);
+}
+
+int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
+                       const int32_t* qzeros, void* const* y_ranks, int world, int rank,
+                       int64_t M, int64_t K, int64_t N, int64_t group_size, void* stream) {
+  int rc = check_awq_shapes("awq_gemm_gather", K, N, group_size);
+  if (rc) return rc;
+  if (M <= 0) return fail(TO_EINVAL, "awq_gemm_gather: invalid M=%lld", (long long)M);
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(TO_EINVAL, "awq_gemm_gather: rank %d of %d (1 to 8 ranks)", rank, world);
+  if (!y_ranks) return fail(TO_EINVAL, "awq_gemm_gather: null output table");
+  for (int r = 0; r < world; ++r)
+    if (!y_ranks[r]) return fail(TO_EINVAL, "awq_gemm_gather: null output of rank %d", r);
+  if (!aligned16(scales) || !aligned16(x))
+    return fail(TO_EINVAL, "awq_gemm_gather: x and scales must be 16-byte aligned");
+  rc = awq_gemm_tc_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M,
+                                 K, N, group_size, (cudaStream_t)stream);
+  if (rc == TO_EUNSUPPORTED)
+    return fail(TO_EUNSUPPORTED,
+                "awq_gemm_gather: shapes outside the tensor-core kernel (N %% 32, K %% 8, group "
+                "size, alignment); run the local GEMM and an all-gather instead");
+  return rc;
 }
 
 }  // extern "C"

@@ -50,6 +50,14 @@ static_assert(kAwqSmem <= 232448, "shared memory");
 // of a 64-column strip are contiguous along K, strips are 8 KB apart.
 constexpr uint32_t kAwqBLbo = 8192, kAwqBSbo = 1024;
 
+// Output tensor maps: one per destination. A plain call has one (this GPU's y); the gathering
+// form of an N-sharded layer has one per rank of the group (the peers' [M, N_full] outputs,
+// mapped into this process), each tile being stored to all of them at column offset ycol0.
+constexpr int kAwqMaxRanks = 8;
+struct AwqOutMaps {
+  CUtensorMap m[kAwqMaxRanks];
+};
+
 __device__ __forceinline__ int awq_k_start(int t, int kblocks) {
   return (int)(((unsigned)t * 5u) % (unsigned)kblocks);
 }
@@ -58,8 +66,8 @@ template <typename T>
 __global__ void __launch_bounds__(kAwqThreads, 1)
     k_awq_gemm_sm100(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
-                     const __grid_constant__ CUtensorMap tmY, int M, int N, int K, int G,
-                     int group_rows, int* err) {
+                     const __grid_constant__ AwqOutMaps ym, int ny, int ycol0, int M, int N,
+                     int K, int G, int group_rows, int* err) {
   using H = Half2Of<T>;
   using H2 = typename H::type;
   constexpr Kind KD = std::is_same<T, __half>::value ? Kind::F16 : Kind::BF16;
@@ -110,7 +118,7 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
     prefetch_tmap(&tmW);
     prefetch_tmap(&tmS);
     prefetch_tmap(&tmZ);
-    prefetch_tmap(&tmY);
+    for (int r = 0; r < ny; ++r) prefetch_tmap(&ym.m[r]);
   }
   if (warp == 0) tmem_alloc<512>(tmem_holder);
   tc_fence_before();
@@ -321,7 +329,11 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmY, nt * kAwqBN + c0, row0, stg);
+          // Destinations in a rotated order, so the ranks' stores spread over the links.
+          for (int j = 0; j < ny; ++j) {
+            const int r = (j + t) % ny;
+            tma_store_2d(&ym.m[r], ycol0 + nt * kAwqBN + c0, row0, stg);
+          }
           bulk_commit();
         }
       }
@@ -329,7 +341,16 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty + buf);
     }
-    if (lane == 0) bulk_wait_read<0>();  // stores have read their slabs
+    if (lane == 0) {
+      if (ny > 1) {
+        // Peers' outputs: the stores have completed and are ordered before whatever this
+        // GPU signals to the peers after the kernel.
+        bulk_wait_all();
+        __threadfence_system();
+      } else {
+        bulk_wait_read<0>();  // stores have read their slabs
+      }
+    }
   }
 
   tc_fence_before();
@@ -341,8 +362,9 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
 }
 
 template <typename T>
-int launch_awq_gemm(const void* x, const int32_t* qw, const void* s, const int32_t* qz, void* y,
-                    int64_t M, int64_t K, int64_t N, int64_t G, int dtype, cudaStream_t st) {
+int launch_awq_gemm(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
+                    void* const* ys, int ny, int64_t n_full, int64_t ycol0, int64_t M, int64_t K,
+                    int64_t N, int64_t G, int dtype, cudaStream_t st) {
   auto kern = k_awq_gemm_sm100<T>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -350,18 +372,21 @@ int launch_awq_gemm(const void* x, const int32_t* qw, const void* s, const int32
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAwqSmem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "awq tcgen05 gemm: shared memory attribute");
+  if (ny < 1 || ny > kAwqMaxRanks) return fail(TO_EINVAL, "awq tcgen05 gemm: %d outputs", ny);
   const int group_rows = G >= kAwqBK ? 1 : (int)(kAwqBK / G);
-  CUtensorMap tx, tw, ts, tz, ty;
+  CUtensorMap tx, tw, ts, tz;
+  AwqOutMaps ym;
+  memset(&ym, 0, sizeof(ym));
   int rc = make_tmap_kmajor(&tx, x, M, K, 2, kAwqBM);
   if (!rc) rc = make_tmap_plain(&tw, qw, K, N / 8, 4, kAwqBN / 8, kAwqBK);
   if (!rc) rc = make_tmap_plain(&ts, s, K / G, N, 2, kAwqBN, group_rows);
   if (!rc) rc = make_tmap_plain(&tz, qz, K / G, N / 8, 4, kAwqBN / 8, group_rows);
-  if (!rc) rc = make_tmap_out16(&ty, y, M, N, 32, dtype);
+  for (int r = 0; !rc && r < ny; ++r) rc = make_tmap_out16(&ym.m[r], ys[r], M, n_full, 32, dtype);
   if (rc) return rc;
   const int64_t tiles = ceil_div(M, kAwqBM) * ceil_div(N, kAwqBN);
   const int grid = (int)std::min<int64_t>(tiles, sm_count());
-  kern<<<grid, kAwqThreads, kAwqSmem, st>>>(tx, tw, ts, tz, ty, (int)M, (int)N, (int)K, (int)G,
-                                            group_rows, device_error_ptr());
+  kern<<<grid, kAwqThreads, kAwqSmem, st>>>(tx, tw, ts, tz, ym, ny, (int)ycol0, (int)M, (int)N,
+                                            (int)K, (int)G, group_rows, device_error_ptr());
   return check_launch("awq tcgen05 gemm");
 }
 
@@ -379,9 +404,33 @@ int awq_gemm_tc_launch(const void* x, const int32_t* qw, const void* s, int s_dt
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return TO_EUNSUPPORTED;
   if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz) || !aligned16(y))
     return TO_EUNSUPPORTED;
+  void* ys[1] = {y};
   if (s_dtype == TO_F16)
-    return sm100::launch_awq_gemm<__half>(x, qw, s, qz, y, M, K, N, G, s_dtype, st);
-  return sm100::launch_awq_gemm<__nv_bfloat16>(x, qw, s, qz, y, M, K, N, G, s_dtype, st);
+    return sm100::launch_awq_gemm<__half>(x, qw, s, qz, ys, 1, N, 0, M, K, N, G, s_dtype, st);
+  return sm100::launch_awq_gemm<__nv_bfloat16>(x, qw, s, qz, ys, 1, N, 0, M, K, N, G, s_dtype,
+                                               st);
+}
+
+// The gathering form for a layer whose N columns are split over `world` ranks: this rank's
+// [M, N] slice is stored into the [M, N * world] output of every rank (y_ranks[r], mapped into
+// this process) at columns [rank * N, (rank + 1) * N). TO_EUNSUPPORTED when the shapes do not
+// meet the kernel's TMA constraints (nothing launched).
+int awq_gemm_tc_gather_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                              const int32_t* qz, void* const* y_ranks, int world, int rank,
+                              int64_t M, int64_t K, int64_t N, int64_t G, cudaStream_t st) {
+  if (s_dtype != TO_F16 && s_dtype != TO_BF16) return TO_EUNSUPPORTED;
+  if (N % 32 != 0 || K % 8 != 0) return TO_EUNSUPPORTED;
+  if (!(G % 64 == 0 || G == 32 || G == K)) return TO_EUNSUPPORTED;
+  if (M > INT32_MAX || N * world > INT32_MAX || K > INT32_MAX) return TO_EUNSUPPORTED;
+  if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz)) return TO_EUNSUPPORTED;
+  for (int r = 0; r < world; ++r)
+    if (!aligned16(y_ranks[r])) return TO_EUNSUPPORTED;
+  const int64_t n_full = N * world, col0 = N * rank;
+  if (s_dtype == TO_F16)
+    return sm100::launch_awq_gemm<__half>(x, qw, s, qz, y_ranks, world, n_full, col0, M, K, N,
+                                          G, s_dtype, st);
+  return sm100::launch_awq_gemm<__nv_bfloat16>(x, qw, s, qz, y_ranks, world, n_full, col0, M, K,
+                                               N, G, s_dtype, st);
 }
 
 }  // namespace tob

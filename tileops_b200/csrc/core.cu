@@ -127,6 +127,47 @@ int to_wait_limit_selftest(int limit_us, int arrive, unsigned long long* out, vo
   return TO_OK;
 }
 
+int to_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return tob::fail(TO_EINVAL, "to_ipc_alloc: invalid argument");
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return tob::cuda_fail(e, "to_ipc_alloc: cudaMalloc");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return tob::cuda_fail(e, "to_ipc_alloc: cudaIpcGetMemHandle");
+  }
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return TO_OK;
+}
+
+int to_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return tob::fail(TO_EINVAL, "to_ipc_open: invalid argument");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return tob::cuda_fail(e, "to_ipc_open: cudaIpcOpenMemHandle");
+  return TO_OK;
+}
+
+int to_ipc_close(void* ptr) {
+  if (!ptr) return TO_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return tob::cuda_fail(e, "to_ipc_close: cudaIpcCloseMemHandle");
+  return TO_OK;
+}
+
+int to_ipc_free(void* ptr) {
+  if (!ptr) return TO_OK;
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return tob::cuda_fail(e, "to_ipc_free: cudaFree");
+  return TO_OK;
+}
+
 int to_device_error_word(int* value, int clear) {
   if (!value) return tob::fail(TO_EINVAL, "to_device_error_word: null output pointer");
   cudaError_t e = cudaDeviceSynchronize();

@@ -10,6 +10,12 @@ lays them out as [M, N].
 
 The compute step is a constructor argument so the bookkeeping runs unchanged on CPU ranks of a
 gloo group in tests; the default is the sm_100a kernel of this package.
+
+AWQ layers on CUDA can also run the gather inside the GEMM (`ShardedAWQLinear.gathered`): every
+rank maps every peer's output buffer (`PeerBuffers`, CUDA IPC over NVLink), the tensor-core
+kernel stores each output tile of its slice into all of them as the tile completes, and one
+collective barrier orders the peers' reads after every rank's stores. The exchange overlaps the
+GEMM and needs no reshuffle: each buffer is the [M, N] output.
 """
 
 from __future__ import annotations
@@ -76,6 +82,81 @@ def gather_columns(local: torch.Tensor, group=None, layout: str = "mn") -> torch
     return out.permute(1, 0, 2).reshape(m, world * npr)
 
 
+class _DeviceArray:
+    """Exposes a raw device allocation to torch.as_tensor (no copy, no ownership)."""
+
+    def __init__(self, ptr_value: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr,
+                                         "data": (ptr_value, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerBuffers:
+    """`count` output buffers of [m, n] 16-bit elements on every rank of `group`, each mapped
+    into every rank's process: ptrs[b][r] is rank r's buffer b as seen from this process and
+    tensors[b] this rank's own buffer b. Collective: every rank constructs it with the same
+    shape. close() is collective too."""
+
+    def __init__(self, m: int, n: int, dtype: torch.dtype, group=None, count: int = 2):
+        from . import _lib
+
+        if dtype not in (torch.float16, torch.bfloat16):
+            raise TypeError(f"PeerBuffers: 16-bit outputs only (got {dtype})")
+        self.group = group
+        self.rank, self.world = _world(group)
+        self.shape = (m, n)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        nbytes = m * n * 2
+        own, handles = [], []
+        for _ in range(count):
+            p, h = _lib.ipc_alloc(nbytes)
+            own.append(p)
+            handles.append(h)
+        table: list = [None] * self.world
+        dist.all_gather_object(table, (handles, (m, n, str(dtype))), group=group)
+        for r, (_, meta) in enumerate(table):
+            if tuple(meta) != (m, n, str(dtype)):
+                raise ValueError(f"PeerBuffers: rank {r} has {meta}, rank {self.rank} has "
+                                 f"{(m, n, str(dtype))}")
+        self._opened: list[int] = []
+        self.ptrs: list[list[int]] = []
+        for b in range(count):
+            row = []
+            for r in range(self.world):
+                if r == self.rank:
+                    row.append(own[b])
+                else:
+                    q = _lib.ipc_open(table[r][0][b])
+                    self._opened.append(q)
+                    row.append(q)
+            self.ptrs.append(row)
+        self._own = own
+        self.tensors = [torch.as_tensor(_DeviceArray(p, (m, n), "<i2"), device=dev).view(dtype)
+                        for p in own]
+        self._next = 0
+
+    def next_index(self) -> int:
+        """Buffers are used in turn; a buffer is reused every `count` calls."""
+        b = self._next
+        self._next = (self._next + 1) % len(self._own)
+        return b
+
+    def close(self) -> None:
+        from . import _lib
+
+        if not self._own:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no peer writes into our buffers any more
+        self.tensors = []
+        for q in self._opened:
+            _lib.ipc_close(q)
+        dist.barrier(group=self.group)  # every peer has unmapped ours
+        for p in self._own:
+            _lib.ipc_free(p)
+        self._opened, self._own, self.ptrs = [], [], []
+
+
 class ShardedAWQLinear:
     """y = x @ dequant(W) with W's columns split across the group (tileops/quant_awq.py:112)."""
 
@@ -91,6 +172,26 @@ class ShardedAWQLinear:
 
             compute = lambda x, qw, s, qz: awq_gemm(x, qw, s, qz, 1)  # noqa: E731
         self.compute = compute
+        self._peer_buffers: dict[int, PeerBuffers] = {}
+        self._flag: Optional[torch.Tensor] = None
+
+    @classmethod
+    def from_shard(cls, qweight, scales, qzeros, group=None,
+                   compute: Optional[Callable] = None) -> "ShardedAWQLinear":
+        """A layer from this rank's column slice, already cut (N = world x the slice's)."""
+        self = cls.__new__(cls)
+        self.group = group
+        self.rank, self.world = _world(group)
+        self.n = qweight.shape[1] * 8 * self.world
+        self.qweight, self.scales, self.qzeros = qweight, scales, qzeros
+        if compute is None:
+            from .quant_awq import awq_gemm
+
+            compute = lambda x, qw, s, qz: awq_gemm(x, qw, s, qz, 1)  # noqa: E731
+        self.compute = compute
+        self._peer_buffers = {}
+        self._flag = None
+        return self
 
     def local(self, x: torch.Tensor) -> torch.Tensor:
         return self.compute(x, self.qweight, self.scales, self.qzeros)
@@ -98,6 +199,51 @@ class ShardedAWQLinear:
     def __call__(self, x: torch.Tensor, gather: bool = True, layout: str = "mn") -> torch.Tensor:
         y = self.local(x)
         return gather_columns(y, self.group, layout) if gather else y
+
+    def gathered(self, x: torch.Tensor) -> torch.Tensor:
+        """The whole [M, N] output with the all-gather done inside the GEMM (CUDA ranks of an
+        NCCL group). The result is one of two buffers per M that the layer reuses in turn: it
+        stays valid until the layer's second-next call with the same M. Shapes the fused kernel
+        does not take run the local GEMM and an all-gather instead."""
+        import ctypes
+
+        from . import _lib
+        from .quant_awq import _as_words
+
+        if self.world == 1:
+            return self.local(x)
+        _lib.ensure_device(x, "awq_gemm_gather")
+        m = x.shape[0]
+        dtype = self.scales.dtype
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=x.device)
+        bufs = self._peer_buffers.get(m)
+        if bufs is None:
+            bufs = PeerBuffers(m, self.n, dtype, self.group)
+            self._peer_buffers[m] = bufs
+        b = bufs.next_index()
+        xx = x.to(dtype).contiguous()
+        qw, qz = _as_words(self.qweight), _as_words(self.qzeros)
+        k = xx.shape[1]
+        n_local = self.n // self.world
+        table = (ctypes.c_void_p * self.world)(*bufs.ptrs[b])
+        lib = _lib.load()
+        rc = lib.to_awq_gemm_gather(xx.data_ptr(), qw.data_ptr(), self.scales.data_ptr(),
+                                    _lib.DTYPE_CODES[dtype], qz.data_ptr(), table, self.world,
+                                    self.rank, m, k, n_local, k // self.qzeros.shape[0],
+                                    _lib.stream_ptr())
+        if rc == _lib.TO_EUNSUPPORTED:
+            return gather_columns(self.local(x), self.group)
+        _lib.check(rc, "awq_gemm_gather")
+        # Every rank's kernel (and so its stores into the peers' buffers) precedes the reads.
+        dist.all_reduce(self._flag, group=self.group)
+        return bufs.tensors[b]
+
+    def close(self) -> None:
+        """Releases the peer-mapped output buffers (collective)."""
+        for bufs in self._peer_buffers.values():
+            bufs.close()
+        self._peer_buffers = {}
 
 
 class ShardedW8A8Linear:
