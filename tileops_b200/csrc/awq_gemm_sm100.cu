@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
             pk[j / 2] = bits_of(o);
           }
         }
-        if (lane == 0) bulk_wait_read<0>();
+        if (lane < ny) bulk_wait_read<0>();  // the slab's previous stores have read it
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -328,12 +328,10 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
               make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          // Destinations in a rotated order, so the ranks' stores spread over the links.
-          for (int j = 0; j < ny; ++j) {
-            const int r = (j + t) % ny;
-            tma_store_2d(&ym.m[r], ycol0 + nt * kAwqBN + c0, row0, stg);
-          }
+        if (lane < ny) {
+          // One destination per lane: copies issued by different threads proceed in
+          // parallel. Rotated by tile, so the ranks' stores spread over the links.
+          tma_store_2d(&ym.m[(lane + t) % ny], ycol0 + nt * kAwqBN + c0, row0, stg);
           bulk_commit();
         }
       }
@@ -341,7 +339,7 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty + buf);
     }
-    if (lane == 0) {
+    if (lane < ny) {
       if (ny > 1) {
         // Peers' outputs: the stores have completed and are ordered before whatever this
         // GPU signals to the peers after the kernel.
