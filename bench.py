@@ -558,6 +558,10 @@ class Decode:
     def total_units(self, world):
         return self.weight_bytes / 1e9  # GB of weights streamed per step, whole job
 
+    def extra(self, ms_step):
+        # one step advances the M sequences of the batch by one token each
+        return {"tokens_per_s": self.m / (ms_step * 1e-3)}
+
     def roofline_units(self):
         return "hbm", self.weight_bytes / self.world
 
@@ -718,6 +722,8 @@ def main() -> int:
             "gpu_launches": args.steps * wl.launches_per_step,
             "clocks": clocks,
         }
+        if hasattr(wl, "extra"):
+            line.update(wl.extra(ms_step))
         print(json.dumps(line), flush=True)
     if hasattr(wl, "close"):
         wl.close()  # collective: releases buffers mapped into the peers
