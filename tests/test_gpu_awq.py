@@ -144,7 +144,7 @@ def test_gemm_deterministic(cuda):
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("m,k,n,g", [
-    # TMA-fed register-MMA kernel (3 <= M <= 32, N % 32 == 0, K % 64 == 0)
+    # TMA-fed register-MMA kernel (3 <= M <= 64, N % 32 == 0, K % 64 == 0)
     (3, 4096, 28672, 128),    # 32-word column tiles, K split 4
     (4, 14336, 4096, 128),    # long K: the stage ring wraps, K split 8
     (8, 4096, 4096, 64),      # one full 8-token tile
@@ -154,6 +154,10 @@ def test_gemm_deterministic(cuda):
     (32, 1024, 4096, 128),    # the largest M it takes
     (32, 14336, 256, 128),    # 32 tokens of a long K chunk do not fit: two 16-token launches
     (20, 14336, 512, 128),    # the same with a 4-token second launch
+    (64, 4096, 4096, 128),    # 33..64 tokens: eight token tiles (few tcgen05 tiles here)
+    (48, 2048, 1024, 64),
+    (40, 14336, 512, 128),    # x of a long K chunk does not fit: 32 + 8 tokens
+    (33, 200, 256, 200),      # K % 64 != 0: the tcgen05 kernel takes it instead
     (5, 256, 96, 256),        # 12 words: a partial column tile, G == K
     # prefetching SIMT stream (M <= 2, and shapes the TMA kernel does not take)
     (1, 4096, 28672, 128),    # 32-word column tiles

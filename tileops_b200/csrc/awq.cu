@@ -340,6 +340,22 @@ bool small_m_enabled() {
   }();
   return on;
 }
+// Largest M routed to the register-MMA kernel (measurement override TOB_AWQ_SMALL_M_MAX).
+int64_t small_m_max() {
+  static const int64_t v = [] {
+    const char* e = getenv("TOB_AWQ_SMALL_M_MAX");
+    const int64_t w = e ? atoll(e) : 0;
+    return (w >= 2 && w <= 64) ? w : 64;
+  }();
+  return v;
+}
+
+// 33 <= M <= 64: the tcgen05 kernel wins once its 128 x 256 tiles cover a third of the SMs
+// (one M tile: N >= ~12.6K columns); below that the register-MMA kernel, which splits K over
+// a cluster, keeps more SMs streaming.
+bool tc_for_mid_m(int64_t M, int64_t N) {
+  return M >= kTensorCoreMinM && ceil_div(M, 128) * ceil_div(N, 256) * 3 >= sm_count();
+}
 
 template <typename T>
 int launch_gemv_any_m(const void* x, const int32_t* qw, const void* s, const int32_t* qz, void* y,
@@ -723,17 +739,22 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
   if (M <= 0) return fail(TO_EINVAL, "awq_gemm: invalid M=%lld", (long long)M);
   if (!aligned16(scales) || !aligned16(x))
     return fail(TO_EINVAL, "awq_gemm: x and scales must be 16-byte aligned");
-  // Prefill-sized M runs on the tcgen05 GEMM; 3 <= M <= 32 on the TMA-fed register-MMA
-  // kernel; M <= 2 and the shapes neither takes (ragged N, unaligned rows) on the streaming
-  // SIMT kernels.
-  if (M >= kTensorCoreMinM) {
+  // Prefill-sized M runs on the tcgen05 GEMM; 3 <= M <= 64 on the TMA-fed register-MMA
+  // kernel (33..64 only when the tcgen05 tiles would leave most SMs idle); M <= 2 and the
+  // shapes neither takes (ragged N, unaligned rows) on the streaming SIMT kernels.
+  if (M > small_m_max() || tc_for_mid_m(M, N)) {
     const int rc = awq_gemm_tc_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N,
                                       group_size, (cudaStream_t)stream);
     if (rc != TO_EUNSUPPORTED) return rc;
   } else if (M > kStreamMaxM && small_m_enabled()) {
-    const int rc = awq_small_m_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N,
-                                      group_size, (cudaStream_t)stream);
+    int rc = awq_small_m_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size,
+                                (cudaStream_t)stream);
     if (rc != TO_EUNSUPPORTED) return rc;
+    if (M >= kTensorCoreMinM) {  // shapes the register-MMA kernel does not take
+      rc = awq_gemm_tc_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size,
+                              (cudaStream_t)stream);
+      if (rc != TO_EUNSUPPORTED) return rc;
+    }
   }
   return awq_gemv_dispatch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size,
                            (cudaStream_t)stream);

@@ -460,7 +460,7 @@ int dispatch_small_m(const void* x, const int32_t* qw, const void* s, const int3
 int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                        const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
                        cudaStream_t st) {
-  if (M < 1 || M > 32) return TO_EUNSUPPORTED;
+  if (M < 1 || M > 64) return TO_EUNSUPPORTED;
   if (s_dtype != TO_F16 && s_dtype != TO_BF16) return TO_EUNSUPPORTED;
   if (N % 32 != 0 || K % 64 != 0) return TO_EUNSUPPORTED;  // TMA strides, whole x blocks
   if (!(G == K || G % 64 == 0 || G == 32)) return TO_EUNSUPPORTED;
@@ -473,18 +473,22 @@ int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dt
   if (M <= 16)
     return f16 ? sm100::dispatch_small_m<__half, 2>(x, qw, s, qz, y, M, K, N, G, st)
                : sm100::dispatch_small_m<__nv_bfloat16, 2>(x, qw, s, qz, y, M, K, N, G, st);
-  int rc = f16 ? sm100::dispatch_small_m<__half, 4>(x, qw, s, qz, y, M, K, N, G, st)
-               : sm100::dispatch_small_m<__nv_bfloat16, 4>(x, qw, s, qz, y, M, K, N, G, st);
+  int rc = M <= 32
+               ? (f16 ? sm100::dispatch_small_m<__half, 4>(x, qw, s, qz, y, M, K, N, G, st)
+                      : sm100::dispatch_small_m<__nv_bfloat16, 4>(x, qw, s, qz, y, M, K, N, G,
+                                                                  st))
+               : (f16 ? sm100::dispatch_small_m<__half, 8>(x, qw, s, qz, y, M, K, N, G, st)
+                      : sm100::dispatch_small_m<__nv_bfloat16, 8>(x, qw, s, qz, y, M, K, N, G,
+                                                                  st));
   if (rc != TO_EUNSUPPORTED) return rc;
-  // 32 tokens of x for a long K chunk do not fit next to the weight ring: run the tokens as
-  // two launches of at most 16 (nothing was launched above).
-  const char* x2 = static_cast<const char*>(x) + (size_t)16 * K * 2;
-  char* y2 = static_cast<char*>(y) + (size_t)16 * N * 2;
-  rc = f16 ? sm100::dispatch_small_m<__half, 2>(x, qw, s, qz, y, 16, K, N, G, st)
-           : sm100::dispatch_small_m<__nv_bfloat16, 2>(x, qw, s, qz, y, 16, K, N, G, st);
+  // The tokens of x for a long K chunk do not fit next to the weight ring: run them as two
+  // launches of half the tile (nothing was launched above).
+  const int64_t half = M <= 32 ? 16 : 32;
+  const char* x2 = static_cast<const char*>(x) + (size_t)half * K * 2;
+  char* y2 = static_cast<char*>(y) + (size_t)half * N * 2;
+  rc = awq_small_m_launch(x, qw, s, s_dtype, qz, y, half, K, N, G, st);
   if (rc != TO_OK) return rc;
-  return f16 ? sm100::dispatch_small_m<__half, 2>(x2, qw, s, qz, y2, M - 16, K, N, G, st)
-             : sm100::dispatch_small_m<__nv_bfloat16, 2>(x2, qw, s, qz, y2, M - 16, K, N, G, st);
+  return awq_small_m_launch(x2, qw, s, s_dtype, qz, y2, M - half, K, N, G, st);
 }
 
 }  // namespace tob
