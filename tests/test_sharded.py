@@ -139,3 +139,31 @@ def test_shard_bounds_validation():
     w = torch.zeros(64, 16, dtype=torch.int8)
     with pytest.raises(ValueError):
         shard_w8a8(w, torch.ones(3, 1), 24, 1, 2)  # 32-row shards do not align with 24-row blocks
+
+
+def test_from_shard_single_rank_gathered_is_local():
+    """Without a process group a layer is its own shard and `gathered` is the local call."""
+    from tileops_b200.sharded import ShardedAWQLinear
+
+    calls = []
+
+    def compute(x, qw, s, qz):
+        calls.append((x.shape, qw.shape, s.shape, qz.shape))
+        return torch.full((x.shape[0], s.shape[1]), 2.0)
+
+    qw = torch.zeros(64, 4, dtype=torch.int32)
+    s = torch.ones(1, 32, dtype=torch.float16)
+    qz = torch.zeros(1, 4, dtype=torch.int32)
+    layer = ShardedAWQLinear.from_shard(qw, s, qz, compute=compute)
+    assert (layer.rank, layer.world, layer.n) == (0, 1, 32)
+    y = layer.gathered(torch.zeros(3, 64))
+    assert y.shape == (3, 32) and bool((y == 2.0).all())
+    assert calls == [((3, 64), (64, 4), (1, 32), (1, 4))]
+    layer.close()  # nothing was mapped
+
+
+def test_ipc_handle_length_checked_before_the_library():
+    import tileops_b200._lib as lib
+
+    with pytest.raises(ValueError):
+        lib.ipc_open(b"\x00" * 10)
