@@ -264,3 +264,40 @@ def test_int8_pair_launch_overlap_chain(cuda):
     want = oi8.block_matmul(q.cpu().numpy(), w.cpu().numpy(), q_s.cpu().numpy(),
                             w_s.cpu().numpy(), (1, dims[0]), "bf16")
     np.testing.assert_allclose(_f(ref[0]), want, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+@pytest.mark.parametrize("m,n,k,bn", [(300, 384, 1024, 128),   # ragged M, 8 K blocks
+                                      (256, 512, 448, 128),    # last K block half full
+                                      (128, 640, 768, 256),    # column blocks span two tiles
+                                      (200, 264, 512, 264)])   # one column block (bn = N)
+def test_int8_block_scaled_tensor_core_vs_oracle(cuda, out, m, n, k, bn):
+    """block_k = 128 with per-(row, K block) and per-(column block, K block) scales on the
+    tcgen05 block-scaled tiles (two TMEM buffers folded into fp32 sums per K block)."""
+    g = torch.Generator().manual_seed(m * 7 + n + k + bn)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    kt = -(-k // 128)
+    a_s = torch.rand(m, kt, generator=g) * 0.05 + 0.001
+    b_s = torch.rand(-(-n // bn), kt, generator=g) * 0.05 + 0.001
+    y = tob.w8a8_block_int8_matmul(a.to(cuda), b.to(cuda), a_s.to(cuda), b_s.to(cuda), [bn, 128],
+                                   output_dtype=_DT[out])
+    want = oi8.block_matmul(a.numpy(), b.numpy(), a_s.numpy(), b_s.numpy(), (bn, 128), out)
+    tol = 1e-4 if out == "f32" else 1e-2
+    np.testing.assert_allclose(_f(y), want, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("m,n,k,bn", [(256, 384, 1024, 128), (130, 256, 640, 256)])
+def test_fp8_block_scaled_tensor_core_vs_oracle(cuda, m, n, k, bn):
+    """The e4m3 block-scaled path (DeepSeek-style 128 x 128 blocks) on the tcgen05 tiles."""
+    g = torch.Generator().manual_seed(m + 5 * n + k)
+    qa = (torch.randn(m, k, generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn)
+    qb = (torch.randn(n, k, generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn)
+    kt = -(-k // 128)
+    a_s = torch.rand(m, kt, generator=g) * 0.01 + 0.0005
+    b_s = torch.rand(-(-n // bn), kt, generator=g) * 0.01 + 0.0005
+    y = tob.w8a8_block_fp8_matmul(qa.to(cuda), qb.to(cuda), a_s.to(cuda), b_s.to(cuda), [bn, 128],
+                                  output_dtype=torch.bfloat16)
+    want = ofp8.block_matmul(qa.view(torch.uint8).numpy(), qb.view(torch.uint8).numpy(),
+                             a_s.numpy(), b_s.numpy(), (bn, 128), "bf16")
+    np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)

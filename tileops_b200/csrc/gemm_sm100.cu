@@ -707,6 +707,217 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ block-scaled tiles
+// k_gemm_bs: W8A8 with per-(row, K block) activation scales and per-(column block, K block)
+// weight scales, block_k = one 128-byte K slice:
+//   C[m, n] = sum_kb (A_kb B_kb^T)[m, n] * a_s[m, kb] * b_s[n / bn, kb]
+// (tileops/quant_int8.py:180, tileops/quant_fp8.py:188; DeepSeek-style 128 x 128 blocks).
+// One 128 x 128 output tile per CTA. The products of each K block land in one of two TMEM
+// buffers (the MMA warp alternates); the eight epilogue warps fold each finished buffer into
+// fp32 running sums held in registers (64 columns of one row per thread), scaled by that
+// block's two scales, and release it, so the tensor core fills one buffer while the other is
+// read. The sums then leave like the per-channel kernel's outputs.
+template <Kind KD, int STAGES>
+struct BsCfg {
+  static constexpr int kElem = KindTraits<KD>::kElemBytes;
+  static constexpr int kBK = 128 / kElem;  // K elements per stage = one scale block
+  static constexpr int kABytes = 128 * 128;
+  static constexpr int kBBytes = 128 * 128;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStageOutBytes = 32 * 32 * 2;
+  static constexpr size_t kOutBytes = kEpiWarps * kStageOutBytes;
+  static constexpr size_t kSmem = (size_t)STAGES * kStageBytes + kOutBytes + 256;
+  static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier area");
+  static_assert(kSmem <= 232448, "shared memory");
+};
+
+template <Kind KD, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_gemm_bs(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmC, int M, int N, int K, Epi ep, int* err) {
+  using C = BsCfg<KD, STAGES>;
+  using Tr = KindTraits<KD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sA = smem_raw;
+  uint8_t* sB = smem_raw + (size_t)STAGES * C::kABytes;
+  uint8_t* sOut = sB + (size_t)STAGES * C::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::kOutBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* pfull = empty + STAGES;  // [2] a K block's products are in TMEM buffer b
+  uint64_t* pempty = pfull + 2;      // [2] the epilogue warps have folded buffer b
+  uint64_t* drain = pempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + 127) / 128;
+  const int mt = (int)(blockIdx.x % (unsigned)m_tiles), nt = (int)(blockIdx.x / (unsigned)m_tiles);
+  const int kblocks = (K + C::kBK - 1) / C::kBK;
+  const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(pfull + b, 1);
+      mbar_init(pempty + b, kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (ep.tma_store) prefetch_tmap(&tmC);
+    if (misaligned && err) atomicExch(err, (int)kErrSmemAlign);
+  }
+  if (warp == 1) tmem_alloc<256>(tmem_holder);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (misaligned) {
+    // nothing to do; fall through to the teardown
+  } else if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = make_policy(ep.policy_a), pol_b = make_policy(ep.policy_b);
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        if (kb >= STAGES && !mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
+        mbar_arrive_expect_tx(full + s, C::kStageBytes);
+        tma_load_2d(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * 128, full + s, pol_a);
+        tma_load_2d(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK, nt * 128, full + s, pol_b);
+        issued_mask |= 1u << s;
+        issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
+      }
+      if (!ok) {
+        // Unwinding: let every copy this thread started land before the CTA exits.
+        const uint64_t tw = globaltimer_ns();
+        for (int i = 0; i < STAGES; ++i)
+          if (issued_mask & (1u << i))
+            while (!mbar_try_wait(full + i, (issued_phase >> i) & 1u) &&
+                   globaltimer_ns() - tw < kWaitLimitNs) {
+            }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, 128, 128);
+      bool ok = true, any = false;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        const int b = kb & 1;
+        const uint32_t bph = (uint32_t)(kb >> 1) & 1u;
+        if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
+        if (kb >= 2 && !mbar_wait(pempty + b, bph ^ 1, abort_flag, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
+        const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma<KD>(tmem + (uint32_t)(b * 128), smem_desc_kmajor_sw128(a0 + 32 * k),
+                   smem_desc_kmajor_sw128(b0 + 32 * k), idesc, k != 0);
+        any = true;
+        umma_commit(empty + s);
+        umma_commit(pfull + b);
+      }
+      if (!ok && any) {
+        // Unwinding: wait (bounded) until the MMAs already issued have finished with TMEM.
+        umma_commit(drain);
+        const uint64_t tw = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - tw < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ fold + epilogue
+    const int q = warp & 3;          // the TMEM lane quarter this warp may read
+    const int eg = (warp - 2) >> 2;  // columns [64 eg, 64 eg + 64) of the tile
+    const int row0 = mt * 128 + q * 32;
+    const int row = row0 + lane;
+    const bool row_ok = row < M;
+    const float* arow = ep.a_s + (int64_t)min(row, M - 1) * ep.a_s_ld;
+    const float* bcol = ep.b_s + (ep.bn >= N ? 0 : (int64_t)(nt * 128) / ep.bn) * ep.b_s_ld;
+    float run[64];
+#pragma unroll
+    for (int j = 0; j < 64; ++j) run[j] = 0.f;
+    bool ok = true;
+    float sa_next = __ldg(arow), sb_next = __ldg(bcol);
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int b = kb & 1;
+      const uint32_t bph = (uint32_t)(kb >> 1) & 1u;
+      const float sa = sa_next, sb = sb_next;
+      if (kb + 1 < kblocks) {
+        sa_next = __ldg(arow + kb + 1);
+        sb_next = __ldg(bcol + kb + 1);
+      }
+      if (!mbar_wait(pfull + b, bph, abort_flag, err)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r[32];
+        const uint32_t taddr =
+            tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + eg * 64 + h * 32);
+        tmem_ld16(taddr, r);
+        tmem_ld16(taddr + 16, r + 16);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float pj = (KD == Kind::I8) ? (float)(int32_t)r[j] : __uint_as_float(r[j]);
+          run[h * 32 + j] = fmaf(pj * sa, sb, run[h * 32 + j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pempty + b);
+    }
+    if (ok) {
+      uint8_t* stg = sOut + (size_t)(warp - 2) * C::kStageOutBytes;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col0 = nt * 128 + eg * 64 + h * 32;
+        if (col0 >= N) continue;
+        const int valid = min(32, N - col0);
+        const float* v = run + h * 32;
+        if (ep.tma_store) {
+          if (lane == 0) bulk_wait_read<0>();  // the previous store has read the slab
+          __syncwarp();
+          uint32_t pk[16];
+          pack_out16(v, pk, ep, col0, valid);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, col0, row0, stg);
+            bulk_commit();
+          }
+        } else if (row_ok) {
+          store_direct<KD>(v, ep, (int64_t)row * N + col0, col0, valid, N);
+        }
+      }
+    }
+    if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<256>(tmem);
+  }
+}
+
 // ------------------------------------------------------------------ 2-CTA tiles
 // k_gemm_pair: one 256 x BN output tile per CTA pair (a (2,1,1) cluster), M <= 256. The pair
 // runs tcgen05 with cta_group::2: each CTA streams its 128 rows of A and its BN/2 rows of B
@@ -1364,6 +1575,34 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
   return launch_gemm_cfg<KD, 256, 128, 4>(a, b, M, N, K, ep, st);
 }
 
+template <Kind KD>
+int launch_gemm_bs(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
+                   cudaStream_t st) {
+  constexpr int kStages = 6;
+  using C = BsCfg<KD, kStages>;
+  auto kern = k_gemm_bs<KD, kStages>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+  });
+  if (attr_err != cudaSuccess)
+    return cuda_fail(attr_err, "tcgen05 block-scaled gemm: shared memory attribute");
+  CUtensorMap ta, tb, tc32;
+  int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, 128);
+  if (!rc) rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, 128);
+  if (rc) return rc;
+  memset(&tc32, 0, sizeof(tc32));
+  if (ep.tma_store) {
+    rc = make_tmap_out16(&tc32, ep.c, M, N, 32, ep.c_dtype);
+    if (rc) return rc;
+  }
+  const int64_t tiles = ceil_div(M, 128) * ceil_div(N, 128);
+  kern<<<(unsigned)tiles, kGemmThreads, C::kSmem, st>>>(ta, tb, tc32, (int)M, (int)N, (int)K, ep,
+                                                       device_error_ptr());
+  return check_launch("tcgen05 block-scaled gemm");
+}
+
 }  // namespace sm100
 
 // Routes a W8A8 call to the tcgen05 kernel when its scales are per-row x per-column-block
@@ -1372,7 +1611,33 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
 int w8a8_tc_launch(bool fp8, const void* a, const void* b, const float* a_s, const float* b_s,
                    void* c, int c_dtype, const void* bias, int32_t* acc_out, int64_t M, int64_t N,
                    int64_t K, int64_t bn, int64_t bk, cudaStream_t st) {
-  if (bk < K) return TO_EUNSUPPORTED;
+  if (bk < K) {
+    // Per-K-block scales: the block-scaled tiles take block_k = 128 with column blocks that
+    // 128-column tiles do not straddle.
+    if (bk != 128 || !(bn % 128 == 0 || bn >= N) || acc_out != nullptr) return TO_EUNSUPPORTED;
+    if (K % 16 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return TO_EUNSUPPORTED;
+    if (!aligned16(a) || !aligned16(b)) return TO_EUNSUPPORTED;
+    if (M * N < 128 * 128 || ceil_div(M, 128) * ceil_div(N, 128) > INT32_MAX)
+      return TO_EUNSUPPORTED;
+    if (getenv("TOB_GEMM_BS_GENERIC") != nullptr) return TO_EUNSUPPORTED;  // measurement
+    const int64_t kt = ceil_div(K, bk);
+    sm100::Epi ep;
+    memset(&ep, 0, sizeof(ep));
+    ep.a_s = a_s;
+    ep.a_s_ld = kt;  // a_s [M, kt]
+    ep.b_s = b_s;
+    ep.b_s_ld = kt;  // b_s [ceil(N / bn), kt]
+    ep.bn = bn >= N ? N : bn;
+    ep.c = c;
+    ep.c_dtype = c_dtype;
+    ep.bias = bias;
+    ep.acc_out = nullptr;
+    ep.policy_a = 0;
+    ep.policy_b = 0;
+    ep.tma_store = (c_dtype == TO_BF16 || c_dtype == TO_F16) && (N % 8 == 0) && aligned16(c);
+    if (fp8) return sm100::launch_gemm_bs<sm100::Kind::E4M3>(a, b, M, N, K, ep, st);
+    return sm100::launch_gemm_bs<sm100::Kind::I8>(a, b, M, N, K, ep, st);
+  }
   if (K % 16 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return TO_EUNSUPPORTED;
   if (!aligned16(a) || !aligned16(b)) return TO_EUNSUPPORTED;
   if (M * N < 128 * 128) return TO_EUNSUPPORTED;  // tiny problems: the generic kernel is cheaper
