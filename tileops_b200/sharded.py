@@ -112,24 +112,31 @@ class PeerBuffers:
             p, h = _lib.ipc_alloc(nbytes)
             own.append(p)
             handles.append(h)
-        table: list = [None] * self.world
-        dist.all_gather_object(table, (handles, (m, n, str(dtype))), group=group)
-        for r, (_, meta) in enumerate(table):
-            if tuple(meta) != (m, n, str(dtype)):
-                raise ValueError(f"PeerBuffers: rank {r} has {meta}, rank {self.rank} has "
-                                 f"{(m, n, str(dtype))}")
         self._opened: list[int] = []
         self.ptrs: list[list[int]] = []
-        for b in range(count):
-            row = []
-            for r in range(self.world):
-                if r == self.rank:
-                    row.append(own[b])
-                else:
-                    q = _lib.ipc_open(table[r][0][b])
-                    self._opened.append(q)
-                    row.append(q)
-            self.ptrs.append(row)
+        try:
+            table: list = [None] * self.world
+            dist.all_gather_object(table, (handles, (m, n, str(dtype))), group=group)
+            for r, (_, meta) in enumerate(table):
+                if tuple(meta) != (m, n, str(dtype)):
+                    raise ValueError(f"PeerBuffers: rank {r} has {meta}, rank {self.rank} has "
+                                     f"{(m, n, str(dtype))}")
+            for b in range(count):
+                row = []
+                for r in range(self.world):
+                    if r == self.rank:
+                        row.append(own[b])
+                    else:
+                        q = _lib.ipc_open(table[r][0][b])
+                        self._opened.append(q)
+                        row.append(q)
+                self.ptrs.append(row)
+        except Exception:
+            for q in self._opened:
+                _lib.ipc_close(q)
+            for p in own:
+                _lib.ipc_free(p)
+            raise
         self._own = own
         self.tensors = [torch.as_tensor(_DeviceArray(p, (m, n), "<i2"), device=dev).view(dtype)
                         for p in own]
