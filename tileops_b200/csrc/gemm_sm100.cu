@@ -731,6 +731,36 @@ struct BsCfg {
   static_assert(kSmem <= 232448, "shared memory");
 };
 
+// Two fp32 lanes per instruction (sm_100 packed f32x2 arithmetic): each lane rounds exactly
+// like the scalar mul.rn / fma.rn.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 template <Kind KD, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm_bs(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -861,19 +891,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!mbar_wait(pfull + b, bph, abort_flag, err)) { ok = false; break; }
       tc_fence_after();
+      uint32_t r[64];
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + eg * 64);
+      tmem_ld16(taddr, r);
+      tmem_ld16(taddr + 16, r + 16);
+      tmem_ld16(taddr + 32, r + 32);
+      tmem_ld16(taddr + 48, r + 48);
+      tmem_ld_wait();
+      // run += (P * a_s) * b_s with each rounding of the scalar form, two columns per
+      // instruction. An int8 block sum |P| <= 128 * 128 * 128 < 2^22 becomes a float exactly as
+      // (bits(2^23 + 2^22) + P) - (2^23 + 2^22), which keeps the conversion off the slow pipe.
+      const float2 sa2 = make_float2(sa, sa), sb2 = make_float2(sb, sb);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t r[32];
-        const uint32_t taddr =
-            tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 128 + eg * 64 + h * 32);
-        tmem_ld16(taddr, r);
-        tmem_ld16(taddr + 16, r + 16);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float pj = (KD == Kind::I8) ? (float)(int32_t)r[j] : __uint_as_float(r[j]);
-          run[h * 32 + j] = fmaf(pj * sa, sb, run[h * 32 + j]);
+      for (int j = 0; j < 64; j += 2) {
+        float2 pj;
+        if constexpr (KD == Kind::I8) {
+          pj = sub2_rn(make_float2(__int_as_float(0x4B400000 + (int32_t)r[j]),
+                                   __int_as_float(0x4B400000 + (int32_t)r[j + 1])),
+                       make_float2(12582912.0f, 12582912.0f));
+        } else {
+          pj = make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
         }
+        const float2 acc = fma2_rn(mul2_rn(pj, sa2), sb2, make_float2(run[j], run[j + 1]));
+        run[j] = acc.x;
+        run[j + 1] = acc.y;
       }
       tc_fence_before();
       __syncwarp();
