@@ -717,12 +717,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // fp32 running sums held in registers (64 columns of one row per thread), scaled by that
 // block's two scales, and release it, so the tensor core fills one buffer while the other is
 // read. The sums then leave like the per-channel kernel's outputs.
-template <Kind KD, int STAGES>
+template <Kind KD, int STAGES, int KC>
 struct BsCfg {
   static constexpr int kElem = KindTraits<KD>::kElemBytes;
-  static constexpr int kBK = 128 / kElem;  // K elements per stage = one scale block
-  static constexpr int kABytes = 128 * 128;
-  static constexpr int kBBytes = 128 * 128;
+  static constexpr int kBK = 128 / kElem;  // K elements per scale block (one 128-byte slice)
+  static constexpr int kChunk = 128 * 128;  // one slice of 128 rows
+  static constexpr int kABytes = KC * kChunk;  // a stage holds KC K blocks
+  static constexpr int kBBytes = KC * kChunk;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStageOutBytes = 32 * 32 * 2;
   static constexpr size_t kOutBytes = kEpiWarps * kStageOutBytes;
@@ -761,11 +762,11 @@ __device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
   return d;
 }
 
-template <Kind KD, int STAGES>
+template <Kind KD, int STAGES, int KC>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm_bs(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmC, int M, int N, int K, Epi ep, int* err) {
-  using C = BsCfg<KD, STAGES>;
+  using C = BsCfg<KD, STAGES, KC>;
   using Tr = KindTraits<KD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sA = smem_raw;
@@ -783,6 +784,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int m_tiles = (M + 127) / 128;
   const int mt = (int)(blockIdx.x % (unsigned)m_tiles), nt = (int)(blockIdx.x / (unsigned)m_tiles);
   const int kblocks = (K + C::kBK - 1) / C::kBK;
+  const int nstages = (kblocks + KC - 1) / KC;  // stages of KC K blocks (the last may be partial)
   const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
 
   if (threadIdx.x == 0) {
@@ -816,13 +818,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint64_t pol_a = make_policy(ep.policy_a), pol_b = make_policy(ep.policy_b);
       uint32_t issued_mask = 0, issued_phase = 0;
       bool ok = true;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        if (kb >= STAGES && !mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
+      for (int st = 0; st < nstages; ++st) {
+        const int s = st % STAGES;
+        const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
+        if (st >= STAGES && !mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
         mbar_arrive_expect_tx(full + s, C::kStageBytes);
-        tma_load_2d(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * 128, full + s, pol_a);
-        tma_load_2d(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK, nt * 128, full + s, pol_b);
+        if (KC == 1) {
+          tma_load_2d(sA + (size_t)s * C::kABytes, &tmA, st * C::kBK, mt * 128, full + s, pol_a);
+          tma_load_2d(sB + (size_t)s * C::kBBytes, &tmB, st * C::kBK, nt * 128, full + s, pol_b);
+        } else {  // 3-D views {128 B, rows, K slices}: KC slices per copy
+          tma_load_3d(sA + (size_t)s * C::kABytes, &tmA, 0, mt * 128, st * KC, full + s, pol_a);
+          tma_load_3d(sB + (size_t)s * C::kBBytes, &tmB, 0, nt * 128, st * KC, full + s, pol_b);
+        }
         issued_mask |= 1u << s;
         issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
       }
@@ -841,23 +848,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, 128, 128);
       bool ok = true, any = false;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        const int b = kb & 1;
-        const uint32_t bph = (uint32_t)(kb >> 1) & 1u;
+      for (int st = 0; ok && st < nstages; ++st) {
+        const int s = st % STAGES;
+        const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
         if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
-        if (kb >= 2 && !mbar_wait(pempty + b, bph ^ 1, abort_flag, err)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
-        const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
+        for (int sub = 0; sub < KC; ++sub) {
+          const int kb = st * KC + sub;
+          if (kb >= kblocks) break;
+          const int b = kb & 1;
+          const uint32_t bph = (uint32_t)(kb >> 1) & 1u;
+          if (kb >= 2 && !mbar_wait(pempty + b, bph ^ 1, abort_flag, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes + (size_t)sub * C::kChunk);
+          const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes + (size_t)sub * C::kChunk);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma<KD>(tmem + (uint32_t)(b * 128), smem_desc_kmajor_sw128(a0 + 32 * k),
-                   smem_desc_kmajor_sw128(b0 + 32 * k), idesc, k != 0);
-        any = true;
-        umma_commit(empty + s);
-        umma_commit(pfull + b);
+          for (int k = 0; k < 4; ++k)
+            umma<KD>(tmem + (uint32_t)(b * 128), smem_desc_kmajor_sw128(a0 + 32 * k),
+                     smem_desc_kmajor_sw128(b0 + 32 * k), idesc, k != 0);
+          any = true;
+          umma_commit(pfull + b);
+        }
+        if (ok) umma_commit(empty + s);
       }
       if (!ok && any) {
         // Unwinding: wait (bounded) until the MMAs already issued have finished with TMEM.
@@ -1616,12 +1627,11 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
   return launch_gemm_cfg<KD, 256, 128, 4>(a, b, M, N, K, ep, st);
 }
 
-template <Kind KD>
+template <Kind KD, int kStages, int KC>
 int launch_gemm_bs(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                    cudaStream_t st) {
-  constexpr int kStages = 6;
-  using C = BsCfg<KD, kStages>;
-  auto kern = k_gemm_bs<KD, kStages>;
+  using C = BsCfg<KD, kStages, KC>;
+  auto kern = k_gemm_bs<KD, kStages, KC>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -1630,8 +1640,8 @@ int launch_gemm_bs(const void* a, const void* b, int64_t M, int64_t N, int64_t K
   if (attr_err != cudaSuccess)
     return cuda_fail(attr_err, "tcgen05 block-scaled gemm: shared memory attribute");
   CUtensorMap ta, tb, tc32;
-  int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, 128);
-  if (!rc) rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, 128);
+  int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, 128, KC);
+  if (!rc) rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, 128, KC);
   if (rc) return rc;
   memset(&tc32, 0, sizeof(tc32));
   if (ep.tma_store) {
@@ -1676,8 +1686,13 @@ int w8a8_tc_launch(bool fp8, const void* a, const void* b, const float* a_s, con
     ep.policy_a = 0;
     ep.policy_b = 0;
     ep.tma_store = (c_dtype == TO_BF16 || c_dtype == TO_F16) && (N % 8 == 0) && aligned16(c);
-    if (fp8) return sm100::launch_gemm_bs<sm100::Kind::E4M3>(a, b, M, N, K, ep, st);
-    return sm100::launch_gemm_bs<sm100::Kind::I8>(a, b, M, N, K, ep, st);
+    // Two K blocks per copy when K is whole 128-byte slices (each copy costs a roughly fixed
+    // time on top of its bytes), else one.
+    if (K % 128 == 0)
+      return fp8 ? sm100::launch_gemm_bs<sm100::Kind::E4M3, 3, 2>(a, b, M, N, K, ep, st)
+                 : sm100::launch_gemm_bs<sm100::Kind::I8, 3, 2>(a, b, M, N, K, ep, st);
+    return fp8 ? sm100::launch_gemm_bs<sm100::Kind::E4M3, 6, 1>(a, b, M, N, K, ep, st)
+               : sm100::launch_gemm_bs<sm100::Kind::I8, 6, 1>(a, b, M, N, K, ep, st);
   }
   if (K % 16 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return TO_EUNSUPPORTED;
   if (!aligned16(a) || !aligned16(b)) return TO_EUNSUPPORTED;
