@@ -8,10 +8,12 @@ One step = one pass of the hot path over one batch of synthetic, seeded input. W
                bf16 out (w8a8_block_int8_matmul, block [1, 4096]). Ranks run independent
                replicas (weak scaling). HBM-bound: roofline in GB/s.
   awq_prefill  AWQ W4A16 layer M=2048 K=8192 N=28672 bf16, group 128, output columns sharded
-               over the ranks with an NCCL all-gather of the bf16 output (strong scaling).
+               over the ranks, the all-gather of the bf16 output inside the GEMM epilogue
+               (TOB_BENCH_GATHER=nccl: an NCCL all-gather after it) (strong scaling).
                Tensor-bound: roofline in TFLOP/s.
   fp8          FP8 layer M=N=K=8192 from bf16: per-token dynamic quantisation of A, tensor-wide
                quantisation of B, per-token x per-tensor e4m3 GEMM to bf16 (replicas).
+  fp8_block    FP8 block-scaled GEMM M=4096 N=K=7168, [128, 128] scale blocks, bf16 out (replicas).
   awq_gemv     AWQ W4A16 decode GEMV x[1, 4096] fp16 @ int4 [4096, 4096], group 128 (replicas).
   decode       32 layers x {qkv 4096->6144, o 4096->4096, gate_up 4096->28672, down 14336->4096}
                AWQ int4 group 128, fp16, M tokens (--decode-m, default 16); N-sharded with an
@@ -417,6 +419,87 @@ class Fp8Layer:
                                                    "dequant GEMM (reference algorithm)")
 
 
+class Fp8BlockGemm:
+    name = "fp8_block"
+    unit = "TFLOP/s"
+    dtype = "e4m3"
+    bound = "tensor"
+    scaling = "weak"
+    profile = "w8a8_block_scaled_m4096_n7168_k7168.md"
+    M, N, K = 4096, 7168, 7168
+    data = ("synthetic (seeded e4m3 codes of N(0, 50^2) values; per-(token, 128-column block) and "
+            "per-(128 x 128 block) fp32 scales U(0.001, 0.051))")
+    launches_per_step = 1
+
+    def __init__(self, dev, rank, world):
+        import tileops_b200 as tob
+
+        self.tob = tob
+        M, N, K = self.M, self.N, self.K
+        kt = K // 128
+        g = torch.Generator().manual_seed(1234 + 6 + rank)
+        qa_cpu = (torch.randn(M, K, generator=g) * 50).to(torch.float8_e4m3fn)
+        sa_cpu = torch.rand(M, kt, generator=g) * 0.05 + 0.001
+        # 3 x 51 MB of weights > 126 MB L2: every step streams its B from HBM
+        self.qbs = [(torch.randn(N, K, generator=g) * 50).to(torch.float8_e4m3fn).to(dev)
+                    for _ in range(3)]
+        self.sb = (torch.rand(N // 128, kt, generator=g) * 0.05 + 0.001).to(dev)
+        self.qa, self.sa = qa_cpu.to(dev), sa_cpu.to(dev)
+        self.qa_host, self.sa_host = qa_cpu.view(torch.uint8).pin_memory(), sa_cpu.pin_memory()
+        self.out_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.dev = dev
+        self.flops = 2 * M * N * K
+
+    def step(self, i):
+        self.tob.w8a8_block_fp8_matmul(self.qa, self.qbs[i % 3], self.sa, self.sb, [128, 128],
+                                       output_dtype=torch.bfloat16)
+
+    kernel_step = step
+
+    def e2e_step(self, i):
+        qa = self.qa_host.to(self.dev, non_blocking=True).view(torch.float8_e4m3fn)
+        sa = self.sa_host.to(self.dev, non_blocking=True)
+        c = self.tob.w8a8_block_fp8_matmul(qa, self.qbs[i % 3], sa, self.sb, [128, 128],
+                                           output_dtype=torch.bfloat16)
+        self.out_host.copy_(c, non_blocking=True)
+
+    def h2d_d2h(self):
+        return self.qa_host.numel() + 4 * self.sa_host.numel(), 2 * self.out_host.numel()
+
+    def total_units(self, world):
+        return world * self.flops / 1e12
+
+    def roofline_units(self):
+        return "tensor", self.flops
+
+    def config(self, world):
+        return {"workload": "fp8_e4m3 block-scaled GEMM M=4096 N=K=7168, [128, 128] scale "
+                            "blocks (DeepSeek-style) -> bf16",
+                "M": self.M, "N": self.N, "K": self.K, "block": [128, 128],
+                "parallelism": f"replicas x{world}",
+                "l2": "rotating weights: 3 x 51 MB buffers > 126 MB L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        import numpy as np
+
+        from oracle import fp8 as ofp8
+
+        torch.set_num_threads(threads)
+        m = 64  # 64 of the 4096 rows per pass
+        K, N = cls.K, cls.N
+        kt = K // 128
+        g = torch.Generator().manual_seed(1234 + 6)
+        qa = (torch.randn(m, K, generator=g) * 50).to(torch.float8_e4m3fn).view(torch.uint8)
+        qb = (torch.randn(N, K, generator=g) * 50).to(torch.float8_e4m3fn).view(torch.uint8)
+        sa = (torch.rand(m, kt, generator=g) * 0.05 + 0.001).numpy()
+        sb = (torch.rand(N // 128, kt, generator=g) * 0.05 + 0.001).numpy()
+        a, b = np.ascontiguousarray(qa.numpy()), np.ascontiguousarray(qb.numpy())
+        run = lambda: ofp8.block_matmul_reference_cpu(a, b, sa, sb, (128, 128), "bf16")  # noqa: E731
+        return run, 2 * m * N * K / 1e12, ("M=64 of 4096 rows per pass (full N, K); numpy CPU "
+                                           "fp32 block dequant + fp32 GEMM (reference algorithm)")
+
+
 class AwqGemv:
     name = "awq_gemv"
     unit = "GB/s"
@@ -589,7 +672,7 @@ class Decode:
                                  "torch CPU reference algorithm")
 
 
-WORKLOADS = {c.name: c for c in (Int8Layer, AwqPrefill, Fp8Layer, AwqGemv, Decode)}
+WORKLOADS = {c.name: c for c in (Int8Layer, AwqPrefill, Fp8Layer, Fp8BlockGemm, AwqGemv, Decode)}
 
 
 def time_cpu(workload_cls, reps: int):
@@ -702,7 +785,7 @@ def main() -> int:
             unit = "TFLOP/s"
             peak = float(peaks["bf16_tflops"])
             peak_note = peak_kind + " bf16 burst"
-            if wl.name == "fp8":  # dense e4m3 runs at twice the bf16 rate
+            if wl.name in ("fp8", "fp8_block"):  # dense e4m3 runs at twice the bf16 rate
                 peak, peak_note = 2 * peak, peak_kind + " bf16 burst x2 (e4m3)"
         cpu_v, cpu_t, cores, sample = time_cpu(wl_cls, 3)
         h2d, d2h = wl.h2d_d2h()
