@@ -301,3 +301,22 @@ def test_fp8_block_scaled_tensor_core_vs_oracle(cuda, m, n, k, bn):
     want = ofp8.block_matmul(qa.view(torch.uint8).numpy(), qb.view(torch.uint8).numpy(),
                              a_s.numpy(), b_s.numpy(), (bn, 128), "bf16")
     np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)
+
+
+def test_fp8_apply_linear_block_128_with_bias(cuda):
+    """apply_w8a8_block_fp8_linear with [128, 128] blocks and a bf16 bias: group quantisation of
+    the input, the block-scaled tensor-core GEMM, the bias added after rounding (fused)."""
+    g = torch.Generator().manual_seed(77)
+    m, n, k = 256, 512, 1024
+    x = torch.randn(m, k, generator=g).bfloat16()
+    w = (torch.randn(n, k, generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn)
+    w_s = torch.rand(n // 128, k // 128, generator=g) * 0.01 + 0.0005
+    bias = torch.randn(n, generator=g).bfloat16()
+    y = tob.apply_w8a8_block_fp8_linear(x.to(cuda), w.to(cuda), [128, 128], w_s.to(cuda),
+                                        bias=bias.to(cuda))
+    assert y.dtype == torch.bfloat16 and y.shape == (m, n)
+    q, s = tob.per_token_group_quant_fp8(x.to(cuda), 128)
+    mm = ofp8.block_matmul(q.view(torch.uint8).cpu().numpy(), w.view(torch.uint8).numpy(),
+                           s.cpu().numpy(), w_s.numpy(), (128, 128), "bf16")
+    want = (torch.from_numpy(mm).bfloat16() + bias).float().numpy()
+    np.testing.assert_allclose(_f(y), want, rtol=1e-2, atol=1e-2)
