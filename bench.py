@@ -16,8 +16,9 @@ One step = one pass of the hot path over one batch of synthetic, seeded input. W
   fp8_block    FP8 block-scaled GEMM M=4096 N=K=7168, [128, 128] scale blocks, bf16 out (replicas).
   awq_gemv     AWQ W4A16 decode GEMV x[1, 4096] fp16 @ int4 [4096, 4096], group 128 (replicas).
   decode       32 layers x {qkv 4096->6144, o 4096->4096, gate_up 4096->28672, down 14336->4096}
-               AWQ int4 group 128, fp16, M tokens (--decode-m, default 16); N-sharded with an
-               all-gather after every linear. HBM GB/s over the weight bytes.
+               AWQ int4 group 128, fp16, M tokens (--decode-m, default 16), silu_and_mul of the
+               gate_up halves into down; N-sharded with an all-gather after every linear.
+               HBM GB/s over the weight bytes.
 
 Reported on one JSON line (rank 0):
   value      device throughput of K steps replayed from a CUDA graph, inputs resident in HBM,
@@ -589,7 +590,7 @@ class Decode:
     SHAPES = [(4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096)]  # (K, N) per linear
     G = 128
     data = "synthetic (seeded random packed int4 weights, scales U(0.002,0.02), x N(0,1))"
-    launches_per_step = 128
+    launches_per_step = 160  # 128 linears + 32 silu_and_mul
 
     def __init__(self, dev, rank, world, m=16):
         import tileops_b200 as tob
@@ -623,7 +624,8 @@ class Decode:
             h = gather(self.tob.awq_gemm(x, *qkv, 1))
             a = gather(self.tob.awq_gemm(h[:, :4096].contiguous(), *o, 1))
             u = gather(self.tob.awq_gemm(a, *gu, 1))
-            x = gather(self.tob.awq_gemm(u[:, :14336].contiguous(), *down, 1))
+            act = self.tob.silu_and_mul(u[:, :14336], u[:, 14336:])  # gate, up read in place
+            x = gather(self.tob.awq_gemm(act, *down, 1))
         return x
 
     def step(self, i):
@@ -650,7 +652,8 @@ class Decode:
 
     def config(self, world):
         return {"workload": f"awq decode step, 32 layers x 4 linears (8B-class), M={self.m} fp16, "
-                            "group 128, N-sharded + all-gather per linear",
+                            "group 128, silu_and_mul between gate_up and down, N-sharded + "
+                            "all-gather per linear",
                 "M": self.m, "layers": self.LAYERS, "parallelism": f"tp{world} (N-sharded)",
                 "l2": "3.6 GB of weights per step > L2",
                 "launch_overlap": "programmatic dependent launch between consecutive layers"}

@@ -202,6 +202,19 @@ TO_API int to_w8a8_fp8_gemm(const void* a, const void* b, const float* a_s, cons
                      void* c, int c_dtype, const void* bias, int64_t M, int64_t N, int64_t K,
                      int64_t block_n, int64_t block_k, void* stream);
 
+/* ---- gated activations (tileops/fused.py) -----------------------------------------------
+ * C = act(A) * B element-wise over [rows, cols] views with unit column stride and row strides
+ * lda, ldb, ldc (elements; a flat tensor of n elements is rows = 1, cols = n). dtype F32, F16
+ * or BF16 for all three. Arithmetic in fp32; act(A) is rounded to dtype, then the product. */
+/* replaces tileops/fused.py:97 silu_and_mul (kernel tileops/backend/cuda/fused.py:17):
+ * act(x) = x * sigmoid(x). */
+TO_API int to_silu_and_mul(const void* a, const void* b, void* c, int dtype, int64_t rows,
+                           int64_t cols, int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+/* replaces tileops/fused.py:107 gelu_and_mul (kernel tileops/backend/cuda/fused.py:32):
+ * act(x) = 0.5 x (1 + tanh(0.7978845608028654 (x + 0.044715 x^3))). */
+TO_API int to_gelu_and_mul(const void* a, const void* b, void* c, int dtype, int64_t rows,
+                           int64_t cols, int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

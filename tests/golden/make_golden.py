@@ -4,7 +4,8 @@ on seeded CPU inputs.
 
     python tests/golden/make_golden.py
 
-Writes awq.npz, int8.npz, fp8.npz, sym.npz. Each case stores its inputs and the reference's
+Writes awq.npz, int8.npz, fp8.npz, sym.npz, fused.npz (or only the files named on the command
+line: awq, int8, fp8, sym, fused). Each case stores its inputs and the reference's
 outputs; float tensors are stored as float32 values (bf16/fp16 values are exact in fp32)
 with the source dtype under "<case>/<field>.dtype", FP8 tensors as uint8 codes. The
 symmetric-INT8 ops have no CPU path in the reference (its TileLang kernels need a GPU
@@ -404,9 +405,41 @@ def make_sym() -> None:
     c.save("sym.npz")
 
 
+# ------------------------------------------------------------------ gated activations
+def make_fused() -> None:
+    """silu_and_mul / gelu_and_mul (tileops/fused.py:97-114) have no CPU path in the reference
+    (TileLang kernels), so their goldens are the comparators of the reference's own
+    tests/fused.py: ``F.silu(a) * b`` and ``F.gelu(a, approximate="tanh") * b`` on torch CPU,
+    here also in fp16 and bf16."""
+    import torch.nn.functional as F
+
+    c = Cases()
+    for i, (dt, tag) in enumerate(((torch.float32, "f32"), (torch.float16, "f16"),
+                                   (torch.bfloat16, "bf16"))):
+        seed(120 + i)
+        a = torch.randn(32, 128).to(dt)  # the reference test's shape
+        b = torch.randn(32, 128).to(dt)
+        c.put(f"silu_{tag}", "a", a)
+        c.put(f"silu_{tag}", "b", b)
+        c.put(f"silu_{tag}", "c", F.silu(a) * b)
+        c.put(f"gelu_{tag}", "a", a)
+        c.put(f"gelu_{tag}", "b", b)
+        c.put(f"gelu_{tag}", "c", F.gelu(a, approximate="tanh") * b)
+        # wide range and an odd width: saturated sigmoid, tanh and exp(-x) overflow
+        a = (torch.randn(7, 33) * 30).to(dt)
+        b = torch.randn(7, 33).to(dt)
+        c.put(f"silu_wide_{tag}", "a", a)
+        c.put(f"silu_wide_{tag}", "b", b)
+        c.put(f"silu_wide_{tag}", "c", F.silu(a) * b)
+        c.put(f"gelu_wide_{tag}", "a", a)
+        c.put(f"gelu_wide_{tag}", "b", b)
+        c.put(f"gelu_wide_{tag}", "c", F.gelu(a, approximate="tanh") * b)
+    c.save("fused.npz")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(1)
-    make_awq()
-    make_int8()
-    make_fp8()
-    make_sym()
+    makers = {"awq": make_awq, "int8": make_int8, "fp8": make_fp8, "sym": make_sym,
+              "fused": make_fused}
+    for name in sys.argv[1:] or list(makers):
+        makers[name]()

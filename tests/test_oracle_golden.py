@@ -7,7 +7,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from oracle import awq, fp8, int8, numerics, sym
+from oracle import awq, fp8, fused, int8, numerics, sym
 
 
 def _np(case, field):
@@ -202,3 +202,24 @@ def test_sym_dequant(golden):
 def test_sym_quant_per_channel(golden, name):
     c = golden("sym.npz")[name]
     assert np.array_equal(sym.quantize(_np(c, "x"), _np(c, "s"), int(c["dim"])), _np(c, "q"))
+
+
+# ------------------------------------------------------------------ gated activations
+_FUSED = [f"{op}{w}_{dt}" for op in ("silu", "gelu") for w in ("", "_wide")
+          for dt in ("f32", "f16", "bf16")]
+
+
+@pytest.mark.parametrize("name", _FUSED)
+def test_fused_act_and_mul_vs_golden(golden, name):
+    """The oracle against torch CPU ``act(a) * b``, the comparator of the reference's tests:
+    fp32 within rounding of the exp/tanh implementations; 16-bit outputs within two ulps (torch
+    may round the 16-bit activation one ulp apart from the correctly rounded fp32 value)."""
+    c = golden("fused.npz")[name]
+    dt = c.dtype_name("a")
+    got = fused.act_and_mul(_np(c, "a"), _np(c, "b"), name.split("_")[0], dt)
+    want = _np(c, "c")
+    if dt == "f32":
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+    else:
+        ulp = 2.0 ** (-10 if dt == "f16" else -7)
+        np.testing.assert_allclose(got, want, rtol=2 * ulp, atol=1e-6)

@@ -44,6 +44,7 @@ from .quant_int8 import (
     w8a8_int8_accumulators,
 )
 from ._lib import set_launch_overlap, version
+from .fused import gelu_and_mul, silu_and_mul
 
 __all__ = [
     "set_launch_overlap",
@@ -76,4 +77,6 @@ __all__ = [
     "pack_awq_int4",
     "unpack_awq_int4",
     "version",
+    "silu_and_mul",
+    "gelu_and_mul",
 ]
