@@ -14,6 +14,7 @@ One step = one pass of the hot path over one batch of synthetic, seeded input. W
   fp8          FP8 layer M=N=K=8192 from bf16: per-token dynamic quantisation of A, tensor-wide
                quantisation of B, per-token x per-tensor e4m3 GEMM to bf16 (replicas).
   fp8_block    FP8 block-scaled GEMM M=4096 N=K=7168, [128, 128] scale blocks, bf16 out (replicas).
+  dense_bf16   dense bf16 GEMM M=2048 K=8192 N=28672 (the prefill layer, unquantized; replicas).
   awq_gemv     AWQ W4A16 decode GEMV x[1, 4096] fp16 @ int4 [4096, 4096], group 128 (replicas).
   decode       32 layers x {qkv 4096->6144, o 4096->4096, gate_up 4096->28672, down 14336->4096}
                AWQ int4 group 128, fp16, M tokens (--decode-m, default 16), silu_and_mul of the
@@ -420,6 +421,69 @@ class Fp8Layer:
                                                    "dequant GEMM (reference algorithm)")
 
 
+class DenseBf16:
+    name = "dense_bf16"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    bound = "tensor"
+    scaling = "weak"
+    profile = "dense_bf16_m2048_k8192_n28672.md"
+    M, K, N = 2048, 8192, 28672
+    data = "synthetic (seeded bf16 N(0,1) weights, activations N(0, 1/K))"
+    launches_per_step = 1
+
+    def __init__(self, dev, rank, world):
+        import tileops_b200 as tob
+
+        self.tob = tob
+        M, K, N = self.M, self.K, self.N
+        g = torch.Generator().manual_seed(1234 + 7 + rank)
+        a_cpu = (torch.randn(M, K, generator=g) / K ** 0.5).bfloat16()
+        # 2 x 470 MB of weights > 126 MB L2
+        self.bs = [torch.randn(K, N, generator=g).bfloat16().to(dev) for _ in range(2)]
+        self.a = a_cpu.to(dev)
+        self.a_host = a_cpu.pin_memory()
+        self.out_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        self.dev = dev
+        self.flops = 2 * M * N * K
+
+    def step(self, i):
+        self.tob.gemm(self.a, self.bs[i % 2])
+
+    kernel_step = step
+
+    def e2e_step(self, i):
+        a = self.a_host.to(self.dev, non_blocking=True)
+        self.out_host.copy_(self.tob.gemm(a, self.bs[i % 2]), non_blocking=True)
+
+    def h2d_d2h(self):
+        return 2 * self.a_host.numel(), 2 * self.out_host.numel()
+
+    def total_units(self, world):
+        return world * self.flops / 1e12
+
+    def roofline_units(self):
+        return "tensor", self.flops
+
+    def config(self, world):
+        return {"workload": "dense bf16 GEMM M=2048 K=8192 N=28672 (the AWQ prefill layer with "
+                            "dense weights): the comparator of the quantized layers",
+                "M": self.M, "N": self.N, "K": self.K, "parallelism": f"replicas x{world}",
+                "l2": "rotating weights: 2 x 470 MB buffers > 126 MB L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        torch.set_num_threads(threads)
+        M, K = cls.M, cls.K
+        n = 7168  # a quarter of the 28672 columns per pass
+        g = torch.Generator().manual_seed(1234 + 7)
+        a = (torch.randn(M, K, generator=g) / K ** 0.5).bfloat16()
+        b = torch.randn(K, n, generator=g).bfloat16()
+        run = lambda: a @ b  # noqa: E731
+        return run, 2 * M * n * K / 1e12, ("N=7168 of 28672 columns per pass (full M, K); torch "
+                                           "CPU bf16 matmul")
+
+
 class Fp8BlockGemm:
     name = "fp8_block"
     unit = "TFLOP/s"
@@ -675,7 +739,8 @@ class Decode:
                                  "torch CPU reference algorithm")
 
 
-WORKLOADS = {c.name: c for c in (Int8Layer, AwqPrefill, Fp8Layer, Fp8BlockGemm, AwqGemv, Decode)}
+WORKLOADS = {c.name: c for c in (Int8Layer, AwqPrefill, Fp8Layer, Fp8BlockGemm, DenseBf16,
+                                  AwqGemv, Decode)}
 
 
 def time_cpu(workload_cls, reps: int):

@@ -44,6 +44,7 @@ from .quant_int8 import (
     w8a8_int8_accumulators,
 )
 from ._lib import set_launch_overlap, version
+from .blas import gemm, mm
 from .fused import gelu_and_mul, silu_and_mul
 
 __all__ = [
@@ -79,4 +80,6 @@ __all__ = [
     "version",
     "silu_and_mul",
     "gelu_and_mul",
+    "gemm",
+    "mm",
 ]

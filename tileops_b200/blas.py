@@ -1,0 +1,61 @@
+"""Dense 16-bit GEMM, as in the reference's ``tileops.gemm`` / ``tileops.mm``
+(tileops/blas/gemm.py:31-78, out handling tileops/runtime/__init__.py:579-595): ``C = A @ B``
+with A (M, K) and B (K, N) row-major, fp32 accumulation, C in the inputs' dtype.
+
+This is the dense comparator of the quantized layers: the same tcgen05 tiles as the W8A8 GEMMs
+(kind::f16, A K-major, B read MN-major as 64-column strips, no scales). float16 and bfloat16
+run on those tiles when K % 8 == 0 and N % 64 == 0 with 16-byte aligned operands; other
+shapes (and float32) go to the plain library GEMM of torch (cuBLAS) on the same device.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Matrix multiply ``C = A @ B`` (2-D tensors, row-major) -- tileops/blas/gemm.py:31."""
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("gemm expects 2-D A and B")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"gemm: incompatible shapes {tuple(a.shape)} @ {tuple(b.shape)}")
+    if a.dtype != b.dtype:
+        raise TypeError("gemm: A and B dtypes must match")
+    _lib.ensure_device(a, "gemm")
+    _lib.same_device("gemm", a, b)
+    aa = a.contiguous()
+    bb = b.contiguous()
+    if out is None:
+        out = torch.empty(m, n, dtype=a.dtype, device=a.device)
+    else:
+        if out.shape != (m, n):
+            raise ValueError(f"gemm: out.shape={tuple(out.shape)} != ({m}, {n})")
+        if out.dtype != a.dtype or out.device != a.device:
+            raise TypeError("gemm: out dtype/device must match A")
+    cc = out.contiguous()
+    rc = _lib.TO_EUNSUPPORTED
+    if a.dtype in (torch.float16, torch.bfloat16):
+        rc = _lib.load().to_gemm(aa.data_ptr(), bb.data_ptr(), cc.data_ptr(),
+                                 _lib.DTYPE_CODES[a.dtype], m, n, k, _lib.stream_ptr())
+    if rc == _lib.TO_EUNSUPPORTED:
+        torch.mm(aa, bb, out=cc)  # shapes outside the tcgen05 tiles: the library GEMM
+    else:
+        _lib.check(rc, "gemm")
+    if cc.data_ptr() != out.data_ptr():
+        out.copy_(cc)
+    return out
+
+
+def mm(input: torch.Tensor, mat2: torch.Tensor, *,
+       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``torch.mm`` -- 2-D matrix multiply ``input @ mat2`` (tileops/blas/gemm.py:71)."""
+    return gemm(input, mat2, out=out)
+
+
+__all__ = ["gemm", "mm"]

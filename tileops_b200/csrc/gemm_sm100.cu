@@ -126,7 +126,7 @@ __device__ __forceinline__ void load_tile_col_scales(float (&sb)[(BN + 31) / 32]
   for (int i = 0; i < (BN + 31) / 32; ++i) {
     const int col = min(n0 + 32 * i + lane, N - 1);
     const int64_t idx = ep.bn >= N ? 0 : (ep.bn == 1 ? (int64_t)col : (int64_t)col / ep.bn);
-    sb[i] = __ldg(ep.b_s + idx * ep.b_s_ld);
+    sb[i] = ep.b_s != nullptr ? __ldg(ep.b_s + idx * ep.b_s_ld) : 1.f;  // null: unscaled
   }
 }
 
@@ -407,12 +407,17 @@ __device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_
 // 128-row half: it sends its partial sums of the other half into the peer's (by then idle)
 // operand ring through distributed shared memory and adds the peer's partial sums to its own.
 // int32 sums stay exact; fp32 sums are added in a fixed order. One tile per CTA pair.
-template <Kind KD, int BM, int BN, int STAGES, bool KS2>
+// BMN: B is [K, N] row-major (MN-major for the MMA), as in a dense C = A @ B, copied as
+// 64-column strips of BK rows (a 3-D tensor-map view {64 columns, K rows, N / 64 strips}) into
+// the 128-byte-swizzled MN-major layout; otherwise B is [N, K] (K-major).
+template <Kind KD, int BM, int BN, int STAGES, bool KS2, bool BMN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC16,
                  int M, int N, int K, Epi ep, int* err) {
   static_assert(!KS2 || BM == 256, "the K-split pair finalises one 128-row half per CTA");
+  static_assert(!BMN || (!KS2 && BN % 64 == 0 && KindTraits<KD>::kElemBytes == 2),
+                "MN-major B: 16-bit operands in whole 64-column strips");
   using C = GemmCfg<KD, BM, BN, STAGES>;
   using Tr = KindTraits<KD>;
   // The swizzled operand tiles need 1024-byte alignment; the dynamic shared memory window
@@ -488,7 +493,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
         mbar_arrive_expect_tx(full + it, C::kStageBytes);
         tma_load_2d(sA + (size_t)it * C::kABytes, &tmA, kb * C::kBK, mt * BM, full + it, pol_a);
-        tma_load_2d(sB + (size_t)it * C::kBBytes, &tmB, kb * C::kBK, nt * BN, full + it, pol_b);
+        if constexpr (BMN)
+          tma_load_3d(sB + (size_t)it * C::kBBytes, &tmB, 0, kb * C::kBK, nt * (BN / 64),
+                      full + it, pol_b);
+        else
+          tma_load_2d(sB + (size_t)it * C::kBBytes, &tmB, kb * C::kBK, nt * BN, full + it, pol_b);
       }
     }
   }
@@ -524,7 +533,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 0] = globaltimer_ns();
           mbar_arrive_expect_tx(full + s, C::kStageBytes);
           tma_load_2d(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * BM, full + s, pol_a);
-          tma_load_2d(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK, nt * BN, full + s, pol_b);
+          if constexpr (BMN)
+            tma_load_3d(sB + (size_t)s * C::kBBytes, &tmB, 0, kb * C::kBK, nt * (BN / 64),
+                        full + s, pol_b);
+          else
+            tma_load_2d(sB + (size_t)s * C::kBBytes, &tmB, kb * C::kBK, nt * BN, full + s, pol_b);
           issued_mask |= 1u << s;
           issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
           if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -549,7 +562,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, 128, BN);
+      constexpr uint32_t idesc =
+          BMN ? make_idesc_major(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, 128, BN, 0, 1)
+              : make_idesc(Tr::kDFmt, Tr::kAFmt, Tr::kBFmt, 128, BN);
       uint32_t s = 0, ph = 0;
       int i = 0, step = 0;
       bool ok = true, any = false;
@@ -568,7 +583,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t bdesc = smem_desc_kmajor_sw128(b0 + 32 * k);
+            // MN-major: 64-column strips BK rows deep (8 KB apart); K step k = 16 rows = 2 KB
+            const uint64_t bdesc = BMN ? smem_desc_mnmajor_sw128(b0 + 2048 * k, 8192, 1024)
+                                       : smem_desc_kmajor_sw128(b0 + 32 * k);
 #pragma unroll
             for (int h = 0; h < C::kHalves; ++h) {
               const uint64_t adesc = smem_desc_kmajor_sw128(a0 + 16384 * h + 32 * k);
@@ -617,7 +634,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
       for (int h = 0; h < C::kHalves; ++h) {
         const int rr = mt * BM + h * 128 + q * 32 + lane;
-        sat[h] = rr < M ? __ldg(ep.a_s + (int64_t)rr * ep.a_s_ld) : 0.f;
+        sat[h] = rr >= M ? 0.f : ep.a_s != nullptr ? __ldg(ep.a_s + (int64_t)rr * ep.a_s_ld) : 1.f;
       }
       if (!mbar_wait(tfull + buf, aph, abort_flag, err)) break;
       tc_fence_after();
@@ -1462,11 +1479,32 @@ int make_tmap_x_blocks(CUtensorMap* out, const void* ptr, int64_t M, int64_t K, 
   return TO_OK;
 }
 
-template <Kind KD, int BM, int BN, int STAGES, bool KS2 = false>
+// B [K, N] of 16-bit elements, N a multiple of 64, as a 3-D view {64 columns, K rows, N / 64
+// strips}: one box brings box_rows rows of `strips` consecutive 64-column strips, landing as
+// strips of box_rows x 128 bytes (128-byte swizzle) -- the MN-major operand layout.
+int make_tmap_mn_strips(CUtensorMap* out, const void* ptr, int64_t K, int64_t N, int box_rows,
+                        int strips) {
+  EncodeFn encode = get_encode();
+  if (!encode) return fail(TO_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  if (N % 64 != 0) return fail(TO_EINVAL, "MN-major strips need N a multiple of 64");
+  cuuint64_t dims[3] = {64, (cuuint64_t)K, (cuuint64_t)(N / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)(N * 2), 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)strips};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(ptr), dims, strides,
+                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TO_ECUDA, "cuTensorMapEncodeTiled (MN-major strips) failed (%d) for [%lld, %lld]",
+                (int)r, (long long)K, (long long)N);
+  return TO_OK;
+}
+
+template <Kind KD, int BM, int BN, int STAGES, bool KS2 = false, bool BMN = false>
 int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                     cudaStream_t st) {
   using C = GemmCfg<KD, BM, BN, STAGES>;
-  auto kern = k_gemm_sm100<KD, BM, BN, STAGES, KS2>;
+  auto kern = k_gemm_sm100<KD, BM, BN, STAGES, KS2, BMN>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -1476,7 +1514,8 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
   CUtensorMap ta, tb, tc32, tc16;
   int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, BM);
   if (rc) return rc;
-  rc = make_tmap_kmajor(&tb, b, N, K, C::kElem, BN);
+  rc = BMN ? make_tmap_mn_strips(&tb, b, K, N, C::kBK, BN / 64)
+           : make_tmap_kmajor(&tb, b, N, K, C::kElem, BN);
   if (rc) return rc;
   Epi e2 = ep;
   memset(&tc32, 0, sizeof(tc32));
@@ -1728,3 +1767,48 @@ int w8a8_tc_launch(bool fp8, const void* a, const void* b, const float* a_s, con
 }
 
 }  // namespace tob
+
+extern "C" {
+
+int to_gemm(const void* a, const void* b, void* c, int dtype, int64_t M, int64_t N, int64_t K,
+            void* stream) {
+  using namespace tob;
+  if (M < 0 || N < 0 || K < 0)
+    return fail(TO_EINVAL, "gemm: invalid shape M=%lld N=%lld K=%lld", (long long)M,
+                (long long)N, (long long)K);
+  if (dtype != TO_F16 && dtype != TO_BF16)
+    return fail(TO_EUNSUPPORTED, "gemm: dtype %s (float16 and bfloat16 are supported)",
+                dtype_name(dtype));
+  if (M == 0 || N == 0) return TO_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (K == 0) {
+    const cudaError_t e = cudaMemsetAsync(c, 0, (size_t)(M * N * 2), st);
+    return e == cudaSuccess ? TO_OK : cuda_fail(e, "gemm: zero fill");
+  }
+  // TMA constraints of the tcgen05 tiles: 16-byte rows of A, whole 64-column strips of B.
+  if (K % 8 != 0 || N % 64 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX ||
+      !aligned16(a) || !aligned16(b) || !aligned16(c))
+    return fail(TO_EUNSUPPORTED,
+                "gemm: shape or alignment outside the tensor-core tiles (K %% 8 == 0, N %% 64 "
+                "== 0, 16-byte aligned operands needed)");
+  sm100::Epi ep;
+  memset(&ep, 0, sizeof(ep));
+  ep.a_s = nullptr;  // unscaled: the epilogue multiplies by 1
+  ep.b_s = nullptr;
+  ep.bn = N;
+  ep.c = c;
+  ep.c_dtype = dtype;
+  ep.tma_store = 1;
+  // 256-row tiles (3 stages of 64 KB, one accumulator buffer) halve the copies per MMA; they
+  // pay once they fill the SMs, 128-row tiles (4 stages, two accumulator buffers) below that.
+  using sm100::Kind;
+  if (ceil_div(M, 256) * ceil_div(N, 256) >= sm_count())
+    return dtype == TO_F16
+               ? sm100::launch_gemm_cfg<Kind::F16, 256, 256, 3, false, true>(a, b, M, N, K, ep, st)
+               : sm100::launch_gemm_cfg<Kind::BF16, 256, 256, 3, false, true>(a, b, M, N, K, ep, st);
+  return dtype == TO_F16
+             ? sm100::launch_gemm_cfg<Kind::F16, 128, 256, 4, false, true>(a, b, M, N, K, ep, st)
+             : sm100::launch_gemm_cfg<Kind::BF16, 128, 256, 4, false, true>(a, b, M, N, K, ep, st);
+}
+
+}  // extern "C"
