@@ -485,7 +485,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       pol_b = make_policy(ep.policy_b);
       int mt, nt;
       tile_coords(t0, m_tiles, n_tiles, mt, nt);
-      const int k0 = k_start(t0, kb_n);
+      // The dense form's B (larger than L2) is shared by the M tiles of a band: they walk K in
+      // step, so each B block is read from DRAM once.
+      const int k0 = BMN ? 0 : k_start(t0, kb_n);
       pre = min(STAGES, kb_n);
       for (int it = 0; it < pre; ++it) {
         const int kb = kb_lo + (k0 + it) % kb_n;
@@ -525,7 +527,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int t = t0; ok && t < tiles; t += tstride) {
         int mt, nt;
         tile_coords(t, m_tiles, n_tiles, mt, nt);
-        const int k0 = k_start(t, kb_n);
+        const int k0 = BMN ? 0 : k_start(t, kb_n);
         for (int it = (t == t0 ? pre : 0); it < kb_n; ++it, ++step) {
           const int kb = kb_lo + (k0 + it) % kb_n;
           if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
