@@ -150,3 +150,35 @@ def test_dropin_module_names():
     for name in ("block_dequant_fp8", "w8a8_triton_block_scaled_mm", "awq_dequantize_triton",
                  "apply_w8a8_block_fp8_linear", "dequantize_per_channel"):
         assert hasattr(tileops, name)
+
+
+def test_fused_and_gemm_validation_before_compute():
+    """The checks of tileops/fused.py:34-64 and tileops/blas/gemm.py:41-50, raised before any
+    device work (so they hold on CPU tensors too)."""
+    with pytest.raises(ValueError, match="shape mismatch"):
+        tob.silu_and_mul(torch.zeros(2, 3), torch.zeros(2, 4))
+    with pytest.raises(TypeError, match="dtype mismatch"):
+        tob.gelu_and_mul(torch.zeros(2, 3), torch.zeros(2, 3, dtype=torch.float16))
+    with pytest.raises(ValueError, match="out.shape"):
+        tob.silu_and_mul(torch.zeros(2, 3), torch.zeros(2, 3), out=torch.zeros(3, 2))
+    with pytest.raises(TypeError, match="out.dtype"):
+        tob.silu_and_mul(torch.zeros(2, 3), torch.zeros(2, 3),
+                         out=torch.zeros(2, 3, dtype=torch.float16))
+    with pytest.raises(TypeError, match="CUDA"):
+        tob.silu_and_mul(torch.zeros(2, 3), torch.zeros(2, 3))
+    with pytest.raises(ValueError, match="2-D"):
+        tob.gemm(torch.zeros(3), torch.zeros(3, 4))
+    with pytest.raises(ValueError, match="incompatible"):
+        tob.mm(torch.zeros(2, 3), torch.zeros(4, 5))
+    with pytest.raises(TypeError, match="dtypes must match"):
+        tob.gemm(torch.zeros(2, 3), torch.zeros(3, 4, dtype=torch.float16))
+    with pytest.raises(TypeError, match="CUDA"):
+        tob.gemm(torch.zeros(2, 3), torch.zeros(3, 4))
+
+
+def test_dropin_fused_and_blas_names():
+    import tileops
+    import tileops.fused as tf
+
+    assert tileops.silu_and_mul is tob.silu_and_mul and tf.gelu_and_mul is tob.gelu_and_mul
+    assert tileops.gemm is tob.gemm and tileops.mm is tob.mm
