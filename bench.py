@@ -16,6 +16,7 @@ One step = one pass of the hot path over one batch of synthetic, seeded input. W
   fp8_block    FP8 block-scaled GEMM M=4096 N=K=7168, [128, 128] scale blocks, bf16 out (replicas).
   dense_bf16   dense bf16 GEMM M=2048 K=8192 N=28672 (the prefill layer, unquantized; replicas).
   awq_gemv     AWQ W4A16 decode GEMV x[1, 4096] fp16 @ int4 [4096, 4096], group 128 (replicas).
+  dense_gemv   dense fp16 GEMV y = A[4096, 4096] @ x (the decode GEMV, unquantized; replicas).
   decode       32 layers x {qkv 4096->6144, o 4096->4096, gate_up 4096->28672, down 14336->4096}
                AWQ int4 group 128, fp16, M tokens (--decode-m, default 16), silu_and_mul of the
                gate_up halves into down; N-sharded with an all-gather after every linear.
@@ -643,6 +644,67 @@ class AwqGemv:
                                  "matmul (reference algorithm)")
 
 
+class DenseGemv:
+    name = "dense_gemv"
+    unit = "GB/s"
+    dtype = "f16"
+    bound = "hbm"
+    scaling = "weak"
+    profile = "dense_gemv_m4096_k4096.md"
+    M, K = 4096, 4096
+    SETS = 8  # 8 x 33.6 MB > L2
+    data = "synthetic (seeded fp16 A N(0,1), x N(0, 1/K))"
+    launches_per_step = 1
+
+    def __init__(self, dev, rank, world):
+        import tileops_b200 as tob
+
+        self.tob = tob
+        M, K = self.M, self.K
+        g = torch.Generator().manual_seed(1234 + 8 + rank)
+        self.sets = [torch.randn(M, K, generator=g).half().to(dev) for _ in range(self.SETS)]
+        x_cpu = (torch.randn(K, generator=g) / K ** 0.5).half()
+        self.x = x_cpu.to(dev)
+        self.x_host = x_cpu.pin_memory()
+        self.out_host = torch.empty(M, dtype=torch.float16).pin_memory()
+        self.dev = dev
+        self.kernel_bytes = 2 * M * K + 2 * K + 2 * M
+
+    def step(self, i):
+        self.tob.gemv(self.sets[i % self.SETS], self.x)
+
+    kernel_step = step
+
+    def e2e_step(self, i):
+        x = self.x_host.to(self.dev, non_blocking=True)
+        self.out_host.copy_(self.tob.gemv(self.sets[i % self.SETS], x), non_blocking=True)
+
+    def h2d_d2h(self):
+        return 2 * self.K, 2 * self.M
+
+    def total_units(self, world):
+        return world * self.kernel_bytes / 1e9  # GB per step, whole job
+
+    def roofline_units(self):
+        return "hbm", self.kernel_bytes
+
+    def config(self, world):
+        return {"workload": "dense fp16 GEMV y[4096] = A[4096,4096] @ x (the AWQ GEMV layer with "
+                            "dense weights): the comparator of the int4 GEMV",
+                "M": self.M, "K": self.K, "parallelism": f"replicas x{world}",
+                "l2": "8 rotating weight sets x 33.6 MB > L2"}
+
+    @classmethod
+    def cpu_reference(cls, threads):
+        torch.set_num_threads(threads)
+        M, K = cls.M, cls.K
+        g = torch.Generator().manual_seed(1234 + 8)
+        a = torch.randn(M, K, generator=g).half()
+        x = (torch.randn(K, generator=g) / K ** 0.5).half()
+        run = lambda: a @ x  # noqa: E731
+        return run, (2 * M * K + 2 * K + 2 * M) / 1e9, "the full GEMV per pass; torch CPU fp16 mv"
+
+
 class Decode:
     name = "decode"
     unit = "GB/s"
@@ -740,7 +802,7 @@ class Decode:
 
 
 WORKLOADS = {c.name: c for c in (Int8Layer, AwqPrefill, Fp8Layer, Fp8BlockGemm, DenseBf16,
-                                  AwqGemv, Decode)}
+                                  AwqGemv, DenseGemv, Decode)}
 
 
 def time_cpu(workload_cls, reps: int):

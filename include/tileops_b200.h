@@ -202,13 +202,19 @@ TO_API int to_w8a8_fp8_gemm(const void* a, const void* b, const float* a_s, cons
                      void* c, int c_dtype, const void* bias, int64_t M, int64_t N, int64_t K,
                      int64_t block_n, int64_t block_k, void* stream);
 
-/* ---- dense GEMM (tileops/blas/gemm.py) -----------------------------------------------------
+/* ---- dense GEMM and GEMV (tileops/blas/gemm.py, tileops/blas/gemv.py) ---------------------
  * replaces tileops/blas/gemm.py:31 gemm (and its mm alias, :71): C [M,N] = A [M,K] @ B [K,N],
  * all row-major, dtype F16 or BF16 for A, B and C, fp32 accumulation, C rounded once. Runs on
  * the tcgen05 tiles when K % 8 == 0, N % 64 == 0 and the pointers are 16-byte aligned; other
  * shapes return TO_EUNSUPPORTED with nothing launched. */
 TO_API int to_gemm(const void* a, const void* b, void* c, int dtype, int64_t M, int64_t N,
                    int64_t K, void* stream);
+/* replaces tileops/blas/gemv.py:22 gemv (and its mv alias, :60): y [M] = A [M,K] @ x [K], A
+ * row-major, dtype F32, F16 or BF16 for A, x and y, fp32 accumulation, y rounded once. Any M, K
+ * (K = 0 writes zeros); 16-byte loads when K * sizeof(dtype) % 16 == 0 and A, x are 16-byte
+ * aligned. */
+TO_API int to_gemv(const void* a, const void* x, void* y, int dtype, int64_t M, int64_t K,
+                   void* stream);
 
 /* ---- gated activations (tileops/fused.py) -----------------------------------------------
  * C = act(A) * B element-wise over [rows, cols] views with unit column stride and row strides

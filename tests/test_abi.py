@@ -65,6 +65,14 @@ def test_workspace_queries_need_no_device(lib):
     assert lib.to_awq_gemm_workspace_size(1, 4096, 4096, 128) >= 0
 
 
+def test_gemv_shape_checks_need_no_device(lib):
+    assert lib.to_gemv(None, None, None, _lib.DTYPE_CODES[torch.float16], -1, 4, None) == \
+        _lib.TO_EINVAL
+    assert lib.to_gemv(None, None, None, _lib.DTYPE_CODES[torch.float16], 0, 4, None) == _lib.TO_OK
+    assert lib.to_gemv(None, None, None, _lib.DTYPE_CODES[torch.float16], 3, 4, None) == \
+        _lib.TO_EINVAL  # null pointers
+
+
 def test_status_mapping():
     with pytest.raises(ValueError):
         _lib.check(_lib.TO_EINVAL, "x")
@@ -153,8 +161,9 @@ def test_dropin_module_names():
 
 
 def test_fused_and_gemm_validation_before_compute():
-    """The checks of tileops/fused.py:34-64 and tileops/blas/gemm.py:41-50, raised before any
-    device work (so they hold on CPU tensors too)."""
+    """The checks of tileops/fused.py:34-64, tileops/blas/gemm.py:41-50 and
+    tileops/blas/gemv.py:32-43, raised before any device work (so they hold on CPU tensors
+    too)."""
     with pytest.raises(ValueError, match="shape mismatch"):
         tob.silu_and_mul(torch.zeros(2, 3), torch.zeros(2, 4))
     with pytest.raises(TypeError, match="dtype mismatch"):
@@ -174,6 +183,17 @@ def test_fused_and_gemm_validation_before_compute():
         tob.gemm(torch.zeros(2, 3), torch.zeros(3, 4, dtype=torch.float16))
     with pytest.raises(TypeError, match="CUDA"):
         tob.gemm(torch.zeros(2, 3), torch.zeros(3, 4))
+    # tileops/blas/gemv.py:32-43
+    with pytest.raises(ValueError, match="A 2-D and x 1-D"):
+        tob.gemv(torch.zeros(2, 3), torch.zeros(2, 3))
+    with pytest.raises(ValueError, match="len"):
+        tob.mv(torch.zeros(2, 3), torch.zeros(4))
+    with pytest.raises(TypeError, match="dtypes must match"):
+        tob.gemv(torch.zeros(2, 3), torch.zeros(3, dtype=torch.float16))
+    with pytest.raises(ValueError, match="Unsupported dtype"):
+        tob.gemv(torch.zeros(2, 3, dtype=torch.int8), torch.zeros(3, dtype=torch.int8))
+    with pytest.raises(TypeError, match="CUDA"):
+        tob.gemv(torch.zeros(2, 3), torch.zeros(3))
 
 
 def test_dropin_fused_and_blas_names():
@@ -182,3 +202,4 @@ def test_dropin_fused_and_blas_names():
 
     assert tileops.silu_and_mul is tob.silu_and_mul and tf.gelu_and_mul is tob.gelu_and_mul
     assert tileops.gemm is tob.gemm and tileops.mm is tob.mm
+    assert tileops.gemv is tob.gemv and tileops.mv is tob.mv

@@ -1,6 +1,7 @@
-"""GPU parity of the dense 16-bit GEMM (tileops.gemm / mm): the tcgen05 tiles with B read
-MN-major against an fp32 torch product of the same inputs (rtol = atol = 1e-2 on outputs of unit
-scale), ragged shapes, out= and the library fallback for other shapes."""
+"""GPU parity of the dense GEMM and GEMV (tileops.gemm / mm, tileops.gemv / mv): the tcgen05
+tiles with B read MN-major and the streaming GEMV against an fp32 (fp64 for GEMV) torch product of
+the same inputs (rtol = atol = 1e-2 on 16-bit outputs of unit scale, 1e-4 on fp32 GEMV), ragged
+shapes, out= and the library fallback for other GEMM shapes."""
 
 from __future__ import annotations
 
@@ -56,3 +57,83 @@ def test_gemm_other_shapes_and_errors(cuda):
         tob.gemm(torch.zeros(2, 3, device=cuda), torch.zeros(3, 5, device=cuda).half())
     with pytest.raises(ValueError):
         tob.gemm(torch.zeros(3, device=cuda), torch.zeros(3, 5, device=cuda))
+
+
+# ---------------------------------------------------------------- GEMV (tileops.gemv / mv)
+
+def _gemv_inputs(m, k, dt, seed):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).to(dt)
+    x = (torch.randn(k, generator=g) / max(k, 1) ** 0.5).to(dt)
+    return a, x
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,k", [(9, 4), (1, 1), (28672, 512),     # one warp per row
+                                 (7, 65536), (300, 8192),    # rows split over 8 / 2 warps
+                                 (1000, 33), (513, 1001),    # K not a multiple of the vector
+                                 (4096, 4096), (1500, 3000),  # bulk-copy stream, one chunk
+                                 (1200, 20000)])             # bulk-copy stream, ragged chunks
+def test_gemv_vs_fp32(cuda, dt, m, k):
+    a, x = _gemv_inputs(m, k, dt, m * 31 + k)
+    y = tob.gemv(a.to(cuda), x.to(cuda))
+    assert y.dtype == dt and y.shape == (m,)
+    want = (a.double() @ x.double()).numpy()
+    tol = 1e-4 if dt == torch.float32 else 1e-2
+    np.testing.assert_allclose(y.double().cpu().numpy(), want, rtol=tol, atol=tol)
+
+
+def test_gemv_reference_cases(cuda):
+    # the cases of the reference's dense tests (tests/blas.py:50-75, 158-163), rtol = atol = 1e-3
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(9, 4, generator=g).to(cuda)
+    x = torch.randn(4, generator=g).to(cuda)
+    torch.testing.assert_close(tob.gemv(a, x), a @ x, rtol=1e-3, atol=1e-3)
+    a2 = torch.randn(4, 3, generator=g).to(cuda)
+    x2 = torch.randn(3, generator=g).to(cuda)
+    torch.testing.assert_close(tob.mv(a2, x2), tob.gemv(a2, x2), rtol=1e-3, atol=1e-3)
+    a3 = torch.randn(5, 2, generator=g).to(cuda)
+    x3 = torch.randn(2, generator=g).to(cuda)
+    out = torch.empty(5, device=cuda)
+    assert tob.gemv(a3, x3, out=out) is out
+    torch.testing.assert_close(out, a3 @ x3, rtol=1e-3, atol=1e-3)
+    with pytest.raises(ValueError):
+        tob.gemv(torch.randn(3, 4, device=cuda), torch.randn(3, device=cuda))
+
+
+def test_gemv_layouts_deterministic_and_empty(cuda):
+    a, x = _gemv_inputs(2048, 4096, torch.bfloat16, 5)
+    a, x = a.to(cuda), x.to(cuda)
+    y1 = tob.gemv(a, x)
+    assert torch.equal(y1, tob.gemv(a, x))
+    # strided out, misaligned x (scalar-load path), transposed A (made contiguous)
+    o = torch.zeros(4096, dtype=torch.bfloat16, device=cuda)[::2]
+    assert tob.gemv(a, x, out=o) is o and torch.equal(o, y1)
+    xb = torch.empty(4097, dtype=torch.bfloat16, device=cuda)
+    xb[1:] = x
+    y2 = tob.gemv(a, xb[1:])
+    np.testing.assert_allclose(y2.float().cpu().numpy(), y1.float().cpu().numpy(), rtol=1e-2,
+                               atol=1e-2)
+    at = a.t().contiguous().t()
+    assert torch.equal(tob.gemv(at, x), y1)
+    # K = 0 gives zeros, M = 0 an empty result
+    z = tob.gemv(torch.empty(6, 0, dtype=torch.float16, device=cuda),
+                 torch.empty(0, dtype=torch.float16, device=cuda))
+    assert torch.equal(z, torch.zeros(6, dtype=torch.float16, device=cuda))
+    assert tob.gemv(torch.empty(0, 8, device=cuda), torch.ones(8, device=cuda)).shape == (0,)
+
+
+def test_gemv_errors(cuda):
+    with pytest.raises(ValueError):
+        tob.gemv(torch.zeros(2, 3, device=cuda), torch.zeros(2, 3, device=cuda))
+    with pytest.raises(TypeError):
+        tob.gemv(torch.zeros(2, 3, device=cuda), torch.zeros(3, device=cuda).half())
+    with pytest.raises(ValueError):
+        tob.gemv(torch.zeros(2, 3, dtype=torch.int32, device=cuda),
+                 torch.zeros(3, dtype=torch.int32, device=cuda))
+    with pytest.raises(ValueError):
+        tob.gemv(torch.zeros(2, 3, device=cuda), torch.zeros(3, device=cuda),
+                 out=torch.zeros(3, device=cuda))
+    with pytest.raises(TypeError):
+        tob.gemv(torch.zeros(2, 3, device=cuda), torch.zeros(3, device=cuda),
+                 out=torch.zeros(2, dtype=torch.float16, device=cuda))

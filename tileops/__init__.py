@@ -1,9 +1,9 @@
 """Drop-in name for code written against the reference: ``from tileops import awq_gemm`` and
 ``import tileops.quant_awq`` resolve to the sm_100a implementation in :mod:`tileops_b200`.
 Only the quantized-linear modules, the gated activations of ``tileops.fused``
-(``silu_and_mul``, ``gelu_and_mul``) and the dense ``gemm`` / ``mm`` comparator are provided;
-the rest of the reference package (other elementwise ops, norms, attention, other BLAS, Metal
-backends) is not part of this library."""
+(``silu_and_mul``, ``gelu_and_mul``) and the dense ``gemm`` / ``mm`` / ``gemv`` / ``mv``
+comparators are provided; the rest of the reference package (other elementwise ops, norms,
+attention, other BLAS, Metal backends) is not part of this library."""
 
 import sys as _sys
 

@@ -44,7 +44,7 @@ from .quant_int8 import (
     w8a8_int8_accumulators,
 )
 from ._lib import set_launch_overlap, version
-from .blas import gemm, mm
+from .blas import gemm, gemv, mm, mv
 from .fused import gelu_and_mul, silu_and_mul
 
 __all__ = [
@@ -82,4 +82,6 @@ __all__ = [
     "gelu_and_mul",
     "gemm",
     "mm",
+    "gemv",
+    "mv",
 ]

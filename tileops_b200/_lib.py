@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_w8a8_i8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _L, _P]),
     "to_w8a8_fp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _L, _L, _L, _L, _L, _P]),
     "to_gemm": (_I, [_P, _P, _P, _I, _L, _L, _L, _P]),
+    "to_gemv": (_I, [_P, _P, _P, _I, _L, _L, _P]),
     "to_silu_and_mul": (_I, [_P, _P, _P, _I, _L, _L, _L, _L, _L, _P]),
     "to_gelu_and_mul": (_I, [_P, _P, _P, _I, _L, _L, _L, _L, _L, _P]),
 }
