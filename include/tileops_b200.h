@@ -78,7 +78,8 @@ TO_API int to_ipc_free(void* ptr);
  * usable. out (device memory, 2 x u64) receives {completed ? 1 : 0, nanoseconds waited}.
  * Asynchronous on stream. */
 TO_API int to_wait_limit_selftest(int limit_us, int arrive, unsigned long long* out, void* stream);
-/* Launch overlap for the streaming small-M AWQ kernel (programmatic dependent launch): with
+/* Launch overlap for the streaming small-M AWQ kernels, the 2-CTA W8A8 kernel and to_gemv
+ * (programmatic dependent launch; the GEMV's A counts as its weights): with
  * enable = 1, a launch may start reading its weights, zeros and scales while the previous
  * kernel in the stream is still running; x is read and y written only after that kernel has
  * completed. Use it for chains of layers whose weights no kernel in the stream writes (a

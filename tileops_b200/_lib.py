@@ -211,8 +211,8 @@ def version() -> str:
 
 
 def set_launch_overlap(enable: bool) -> bool:
-    """Turns programmatic dependent launch on or off for the small-M AWQ streaming kernel and
-    returns the previous setting. With it on, a call may read its weights while the previous
+    """Turns programmatic dependent launch on or off for the small-M AWQ streaming kernels, the
+    2-CTA W8A8 kernel and the dense GEMV, and returns the previous setting. With it on, a call may read its weights while the previous
     kernel in the stream is still running, so no kernel that writes those weights may be the
     launch immediately before it (a decode loop over fixed weights is the intended use)."""
     return bool(load().to_set_launch_overlap(1 if enable else 0))
