@@ -364,11 +364,7 @@ int launch_awq_gemm(const void* x, const int32_t* qw, const void* s, const int32
                     void* const* ys, int ny, int64_t n_full, int64_t ycol0, int64_t M, int64_t K,
                     int64_t N, int64_t G, int dtype, cudaStream_t st) {
   auto kern = k_awq_gemm_sm100<T>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAwqSmem);
-  });
+  const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)kAwqSmem);
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "awq tcgen05 gemm: shared memory attribute");
   if (ny < 1 || ny > kAwqMaxRanks) return fail(TO_EINVAL, "awq tcgen05 gemm: %d outputs", ny);
   const int group_rows = G >= kAwqBK ? 1 : (int)(kAwqBK / G);

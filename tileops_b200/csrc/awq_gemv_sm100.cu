@@ -386,12 +386,7 @@ int launch_small_m(const void* x, const int32_t* qw, const void* s, const int32_
   }
   ksplit = (int)ceil_div(K, kchunk);
   auto kern = k_awq_small_m<T, NT, WPQ>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kSmSmemLimit);
-  });
+  const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)kSmSmemLimit);
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "awq small-M gemm: shared memory attribute");
   CUtensorMap tx, tw, ts, tz;
   int rc = make_tmap_x_blocks(&tx, x, M, K, 8 * NT, kchunk / 64);

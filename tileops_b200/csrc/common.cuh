@@ -25,6 +25,10 @@ inline int check_launch(const char* what) {
 }
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Raises the dynamic shared-memory limit of kernel `func` to `bytes` on the current device, once
+// per (kernel, device): the attribute belongs to the kernel in that device's context. Returns the
+// status of the first call.
+cudaError_t ensure_smem_attr(const void* func, int bytes);
 // Device address of the library's error word on the current device (nullptr on failure).
 int* device_error_ptr();
 // Process-wide launch-overlap switch (programmatic dependent launch for streaming kernels).

@@ -4,7 +4,9 @@
 #include <string.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -38,6 +40,22 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+cudaError_t ensure_smem_attr(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, cudaError_t> done;
+  int dev = 0;
+  const cudaError_t ge = cudaGetDevice(&dev);
+  if (ge != cudaSuccess) return ge;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(func, dev);
+  const auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  done.emplace(key, e);
+  return e;
 }
 
 }  // namespace tob

@@ -1507,11 +1507,7 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
                     cudaStream_t st) {
   using C = GemmCfg<KD, BM, BN, STAGES>;
   auto kern = k_gemm_sm100<KD, BM, BN, STAGES, KS2, BMN>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
-  });
+  const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)C::kSmem);
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "tcgen05 gemm: shared memory attribute");
   CUtensorMap ta, tb, tc32, tc16;
   int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, BM);
@@ -1559,11 +1555,7 @@ int launch_gemm_pair(const void* a, const void* b, int64_t M, int64_t N, int64_t
                      cudaStream_t st) {
   using C = PairCfg<KD, BN, STAGES, KC>;
   auto kern = k_gemm_pair<KD, BN, STAGES, KC>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
-  });
+  const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)C::kSmem);
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "tcgen05 2-CTA gemm: shared memory attribute");
   CUtensorMap ta, tb, tc32, tc16;
   int rc = make_tmap_kmajor(&ta, a, M, K, C::kElem, 128, KC);
@@ -1673,11 +1665,7 @@ int launch_gemm_bs(const void* a, const void* b, int64_t M, int64_t N, int64_t K
                    cudaStream_t st) {
   using C = BsCfg<KD, kStages, KC>;
   auto kern = k_gemm_bs<KD, kStages, KC>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
-  });
+  const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)C::kSmem);
   if (attr_err != cudaSuccess)
     return cuda_fail(attr_err, "tcgen05 block-scaled gemm: shared memory attribute");
   CUtensorMap ta, tb, tc32;

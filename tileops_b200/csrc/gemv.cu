@@ -9,8 +9,6 @@
 // grid. With launch overlap on (to_set_launch_overlap), a launch prefetches its first vectors of
 // A into L2 while the previous kernel in the stream finishes, and reads x and writes y only after
 // that kernel has completed.
-#include <mutex>
-
 #include "sm100.cuh"
 
 namespace tob {
@@ -238,16 +236,8 @@ template <typename T>
 int launch_gemv_bulk(const void* a, const void* x, void* y, int64_t M, int64_t K,
                      cudaStream_t st) {
   auto kern = k_gemv_bulk<T>;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static std::once_flag once[64];
-  static cudaError_t attr_err[64];
-  std::call_once(once[dev & 63], [&] {
-    attr_err[dev & 63] =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
-  });
-  if (attr_err[dev & 63] != cudaSuccess)
-    return cuda_fail(attr_err[dev & 63], "gemv: shared memory attribute");
+  const cudaError_t attr_err = ensure_smem_attr((const void*)kern, kBulkSmem);
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "gemv: shared memory attribute");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sm_count(), 1, 1);
   cfg.blockDim = dim3(kBulkWarps * 32, 1, 1);
