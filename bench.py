@@ -818,6 +818,16 @@ def time_cpu(workload_cls, reps: int):
     return units / t, t, threads, sample
 
 
+def arm_config(wl_cls, world: int, decode_m: int) -> dict:
+    """The `config` a workload reports, built without a device (the CPU reference arm quotes the
+    same config as the GPU arm)."""
+    probe = wl_cls.__new__(wl_cls)
+    probe.world = world
+    probe.m = decode_m
+    probe.gather = os.environ.get("TOB_BENCH_GATHER", "fused")
+    return probe.config(world)
+
+
 def run_reference_arm(args, rank: int, wl) -> None:
     if rank != 0:
         return
@@ -834,7 +844,7 @@ def run_reference_arm(args, rank: int, wl) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": wl.unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
-        "data": wl.data, "config": {"workload": wl.name, "parallelism": "cpu"},
+        "data": wl.data, "config": arm_config(wl, args.gpus, args.decode_m),
         "cpu_baseline": {"value": value, "unit": wl.unit, "cores": cores, "kind": "port",
                          "sample": f"{sample}; median {statistics.median(secs):.3f} s per pass"},
         "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
