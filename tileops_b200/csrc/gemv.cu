@@ -1,12 +1,15 @@
 // Dense matrix-vector product (tileops/blas/gemv.py:22, kernel tileops/backend/cuda/blas/gemv.py:10-46):
 //   y [M] = A [M, K] @ x [K], A row-major, fp32 accumulation, y rounded once to the dtype.
-// HBM-bound: every byte of A is read once with 16-byte streaming loads (no L1 allocation), x is
-// re-read by every row team out of L1/L2. A team of TW warps owns one row; TW grows (1, 2, 4, 8)
-// while the teams would leave the SMs short of warps and each lane still has at least four
-// vectors of the row, so short-and-wide matrices keep enough loads in flight. Each lane keeps
-// four loads of A in flight before its multiply-adds; the reduction order (lane stride, then the
-// warp's shuffle tree, then the team's warps in order) is fixed, so results do not depend on the
-// grid. With launch overlap on (to_set_launch_overlap), a launch prefetches its first vectors of
+// HBM-bound: every byte of A is read once, x is re-read out of L1/L2, and 16-bit products are
+// accumulated with the mixed-precision FMA (two conversions per element would otherwise bound
+// the kernel below the HBM rate). Tall matrices with aligned rows of at least 2 KB stream A
+// through per-warp bulk-copy rings (k_gemv_bulk below); every other shape runs k_gemv, where A
+// arrives by 16-byte streaming loads (no L1 allocation) and a team of TW warps owns one row. TW
+// grows (1, 2, 4, 8) while the teams would leave the SMs short of warps and each lane still has
+// at least four vectors of the row, so short-and-wide matrices keep enough loads in flight; each
+// lane issues four loads of A before their multiply-adds. The reduction order (lane stride, then
+// the warp's shuffle tree, then the team's warps in order) is fixed, so results do not depend on
+// the grid. With launch overlap on (to_set_launch_overlap), a launch prefetches its first vectors of
 // A into L2 while the previous kernel in the stream finishes, and reads x and writes y only after
 // that kernel has completed.
 #include "sm100.cuh"
