@@ -21,11 +21,18 @@ def input_to_float8(x_f32: np.ndarray, dtype: str):
     rnd = rounder(dtype)
     x = rnd(np.asarray(x_f32, dtype=np.float32))
     amax = np.float32(np.max(np.abs(x)))
-    amax = rnd(np.maximum(amax, np.float32(1e-12)))
-    r = rnd(np.float32(1.0) / amax)
-    s = rnd(np.float32(r) * np.float32(FP8_MAX))
-    y = np.clip(rnd(x * np.float32(s)), -FP8_MAX, FP8_MAX)
-    return f32_to_e4m3(y), np.float32(np.float32(1.0) / np.float32(s))
+    with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
+        # In float16, 1e-12 rounds to 0: an all-zero tensor divides by zero (s = inf) and
+        # 0 * inf is NaN, which torch's clamp keeps; the reference run on x86 turns that
+        # (sign-set) NaN into the e4m3 code 0xFF.
+        amax = rnd(np.maximum(amax, np.float32(1e-12)))
+        r = rnd(np.float32(1.0) / amax)
+        s = rnd(np.float32(r) * np.float32(FP8_MAX))
+        y = rnd(x * np.float32(s))
+        nan = np.isnan(y)
+        codes = f32_to_e4m3(np.clip(np.where(nan, np.float32(0), y), -FP8_MAX, FP8_MAX))
+        codes = np.where(nan, np.uint8(0xFF), codes).astype(np.uint8)
+        return codes, np.float32(np.float32(1.0) / np.float32(s))
 
 
 def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10, use_ue8m0: bool = False,

@@ -15,13 +15,17 @@ def input_to_int8(x_f32: np.ndarray, dtype: str):
     rnd = rounder(dtype)
     x = rnd(np.asarray(x_f32, dtype=np.float32))
     amax = np.float32(np.max(np.abs(x))) if x.size else np.float32(0)
-    amax = rnd(np.maximum(amax, np.float32(1e-12)))
-    r = rnd(np.float32(1.0) / amax)
-    s = rnd(np.float32(r) * np.float32(127.0))
-    y = rnd(x * np.float32(s))
-    y = np.clip(y, -128.0, 127.0)
-    q = np.trunc(y).astype(np.int8)
-    return q, np.float32(np.float32(1.0) / np.float32(s))
+    with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
+        # In float16, 1e-12 rounds to 0: an all-zero tensor divides by zero (s = inf) and
+        # 0 * inf is NaN, which torch's clamp keeps and its int8 cast turns into 0.
+        amax = rnd(np.maximum(amax, np.float32(1e-12)))
+        r = rnd(np.float32(1.0) / amax)
+        s = rnd(np.float32(r) * np.float32(127.0))
+        y = rnd(x * np.float32(s))
+        nan = np.isnan(y)
+        y = np.clip(np.where(nan, np.float32(0), y), -128.0, 127.0)
+        q = np.trunc(y).astype(np.int8)
+        return q, np.float32(np.float32(1.0) / np.float32(s))
 
 
 def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10):

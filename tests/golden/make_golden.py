@@ -147,6 +147,22 @@ def make_int8() -> None:
         c.put(name, "q", q)
         c.put(name, "s", s)
 
+    # Degenerate tensors: all zeros, and float16 values too small for float16's 1e-12 clamp
+    # (1e-12 rounds to 0 in float16, so the reference divides by a zero amax: scale inf,
+    # x * scale NaN, which its int8 cast turns into 0 and the dequant scale into 0).
+    for dt in (torch.float32, torch.float16, torch.bfloat16):
+        x = torch.zeros(40, dtype=dt)
+        q, s = i8.input_to_int8(x)
+        name = f"input_zeros_{str(dt).replace('torch.', '')}"
+        c.put(name, "x", x)
+        c.put(name, "q", q)
+        c.put(name, "s", s)
+    x = torch.tensor([1e-9, -2e-9, 0.0, 3e-8], dtype=torch.float32).to(torch.float16)
+    q, s = i8.input_to_int8(x)
+    c.put("input_tiny_float16", "x", x)
+    c.put("input_tiny_float16", "q", q)
+    c.put("input_tiny_float16", "s", s)
+
     for i, (name, shape, dt, scale) in enumerate([
         ("token_2d", (4, 16), torch.float32, 0.5),
         ("token_nd", (2, 3, 8), torch.float16, 1.0),
@@ -173,6 +189,21 @@ def make_int8() -> None:
         c.put(name, "group_size", np.array(g))
         c.put(name, "q", q)
         c.put(name, "s", s)
+
+    # Zero rows and groups (scale = eps / 127) and exact round-half-even ties (absmax 127
+    # makes the scale exactly 1, so x / scale = x).
+    x = torch.tensor([[127.0, 0.5, 1.5, 2.5, -0.5, -2.5, 63.5, -126.5],
+                      [0.0] * 8,
+                      [0.0, 0.0, 0.0, 0.0, 1e-12, -3e-11, 0.0, 0.0]], dtype=torch.float32)
+    q, s = i8.per_token_quant_int8(x)
+    c.put("token_edges", "x", x)
+    c.put("token_edges", "q", q)
+    c.put("token_edges", "s", s)
+    q, s = i8.per_token_group_quant_int8(x, 4)
+    c.put("group_edges", "x", x)
+    c.put("group_edges", "group_size", np.array(4))
+    c.put("group_edges", "q", q)
+    c.put("group_edges", "s", s)
 
     seed(70)
     bs = [4, 8]
@@ -253,6 +284,14 @@ def make_fp8() -> None:
         c.put(name, "q", q)
         c.put(name, "s", s)
 
+    for dt in (torch.float32, torch.float16, torch.bfloat16):
+        x = torch.zeros(40, dtype=dt)
+        q, s = fp8.input_to_float8(x, dtype=FP8)
+        name = f"input_zeros_{str(dt).replace('torch.', '')}"
+        c.put(name, "x", x)
+        c.put(name, "q", q)
+        c.put(name, "s", s)
+
     for i, (name, shape, g, dt, ue, cm) in enumerate([
         ("group_f32", (3, 32), 8, torch.float32, False, False),
         ("group_ue8m0", (2, 16), 8, torch.float32, True, False),
@@ -280,6 +319,7 @@ def make_fp8() -> None:
             v[3] = 448.0 * (2.0 ** e) * (1.0 + d)
             v[5] = -0.3 * (2.0 ** e)
             rows.append(v)
+    rows.append(torch.zeros(8))  # a zero group: scale = eps / 448 (rounded up to 2^-42)
     x = torch.stack(rows).to(torch.float32)
     q, s = fp8.per_token_group_quant_fp8(x, 8, use_ue8m0=True)
     c.put("ue8m0_edges", "x", x)

@@ -103,7 +103,9 @@ def test_empty_inputs(cuda):
 
 
 # ------------------------------------------------------------------ dynamic INT8
-@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16"])
+@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
+                                  "input_zeros_float32", "input_zeros_float16",
+                                  "input_zeros_bfloat16", "input_tiny_float16"])
 def test_input_to_int8_golden(cuda, golden, name):
     c = golden("int8.npz")[name]
     q, s = tob.input_to_int8(c.tensor("x", cuda))
@@ -123,7 +125,8 @@ def test_input_to_int8_vs_oracle(cuda, dtype, n):
     assert np.float32(s.item()) == ws
 
 
-@pytest.mark.parametrize("name", ["token_2d", "token_nd", "token_bf16", "token_1d", "token_wide"])
+@pytest.mark.parametrize("name", ["token_2d", "token_nd", "token_bf16", "token_1d", "token_wide",
+                                  "token_edges"])
 def test_per_token_quant_int8_golden(cuda, golden, name):
     c = golden("int8.npz")[name]
     q, s = tob.per_token_quant_int8(c.tensor("x", cuda))
@@ -132,7 +135,7 @@ def test_per_token_quant_int8_golden(cuda, golden, name):
     assert np.array_equal(s.cpu().numpy(), c["s"])
 
 
-@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d"])
+@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d", "group_edges"])
 def test_per_token_group_quant_int8_golden(cuda, golden, name):
     c = golden("int8.npz")[name]
     q, s = tob.per_token_group_quant_int8(c.tensor("x", cuda), int(c["group_size"]))
@@ -154,7 +157,9 @@ def test_group_quant_int8_vs_oracle(cuda, dtype, rows, k, g):
 
 
 # ------------------------------------------------------------------ dynamic FP8
-@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16"])
+@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
+                                  "input_zeros_float32", "input_zeros_float16",
+                                  "input_zeros_bfloat16"])
 def test_input_to_float8_golden(cuda, golden, name):
     c = golden("fp8.npz")[name]
     q, s = tob.input_to_float8(c.tensor("x", cuda))

@@ -87,7 +87,9 @@ def test_awq_split_k_invariance(golden):
 
 
 # ------------------------------------------------------------------ INT8
-@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16"])
+@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
+                                  "input_zeros_float32", "input_zeros_float16",
+                                  "input_zeros_bfloat16", "input_tiny_float16"])
 def test_input_to_int8(golden, name):
     c = golden("int8.npz")[name]
     q, s = int8.input_to_int8(_np(c, "x"), c.dtype_name("x"))
@@ -95,7 +97,8 @@ def test_input_to_int8(golden, name):
     assert np.float32(s) == np.float32(_np(c, "s"))
 
 
-@pytest.mark.parametrize("name", ["token_2d", "token_nd", "token_bf16", "token_1d", "token_wide"])
+@pytest.mark.parametrize("name", ["token_2d", "token_nd", "token_bf16", "token_1d", "token_wide",
+                                  "token_edges"])
 def test_per_token_quant_int8(golden, name):
     c = golden("int8.npz")[name]
     x = _np(c, "x")
@@ -104,7 +107,7 @@ def test_per_token_quant_int8(golden, name):
     assert np.array_equal(s.reshape(-1), _np(c, "s").reshape(-1))
 
 
-@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d"])
+@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d", "group_edges"])
 def test_group_quant_int8(golden, name):
     c = golden("int8.npz")[name]
     q, s = int8.group_quant(_np(c, "x"), int(c["group_size"]))
@@ -138,7 +141,9 @@ def test_w8a8_reference_cpu_port_matches(golden):
 
 
 # ------------------------------------------------------------------ FP8
-@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16"])
+@pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
+                                  "input_zeros_float32", "input_zeros_float16",
+                                  "input_zeros_bfloat16"])
 def test_input_to_float8(golden, name):
     c = golden("fp8.npz")[name]
     q, s = fp8.input_to_float8(_np(c, "x"), c.dtype_name("x"))

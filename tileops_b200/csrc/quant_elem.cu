@@ -292,7 +292,8 @@ __global__ void __launch_bounds__(kThreads) k_absmax(const T* __restrict__ x, in
 }
 
 // Pass 2, in the input dtype T exactly as the reference's expression evaluates:
-//   amax = T(max(amax, 1e-12)); s = T(T(1/amax) * qmax); q = cast(clamp(T(x*s), qmin, qmax)).
+//   amax = T(max(amax, 1e-12)); s = T(T(1/amax) * qmax); q = cast(clamp(T(x*s), qmin, qmax)),
+// NaN products included (see quant1).
 // The int8 cast truncates toward zero (torch .to(int8)); the fp8 cast rounds to nearest even.
 template <typename T, bool FP8, int V>
 __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__ x, int64_t n,
@@ -307,6 +308,10 @@ __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__
   if (blockIdx.x == 0 && threadIdx.x == 0) *dq_scale = __frcp_rn(s);
   auto quant1 = [&](float xv) -> uint8_t {
     float y = round_to<T>(__fmul_rn(xv, s));
+    // NaN (0 * inf: in float16 the 1e-12 floor rounds to 0, so an all-zero tensor has s = inf)
+    // survives the reference's clamp; its int8 cast gives 0 and, on the CPU it is pinned to,
+    // its e4m3 cast the sign-set NaN code 0xFF.
+    if (isnan(y)) return FP8 ? (uint8_t)0xFF : (uint8_t)0;
     y = fminf(fmaxf(y, qmin), qmax);
     if (FP8) return f32_to_e4m3(y);
     return (uint8_t)(int8_t)(int)y;  // truncation toward zero
