@@ -209,3 +209,7 @@ def test_dropin_fused_and_blas_names():
     assert tileops.silu_and_mul is tob.silu_and_mul and tf.gelu_and_mul is tob.gelu_and_mul
     assert tileops.gemm is tob.gemm and tileops.mm is tob.mm
     assert tileops.gemv is tob.gemv and tileops.mv is tob.mv
+    from tileops.blas import gemm, gemv, mm, mv
+    from tileops.blas.gemv import gemv as gemv2
+
+    assert (gemm, gemv, mm, mv, gemv2) == (tob.gemm, tob.gemv, tob.mm, tob.mv, tob.gemv)
