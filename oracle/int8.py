@@ -38,7 +38,9 @@ def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10):
     absmax = np.maximum(np.max(np.abs(flat), axis=-1), np.float32(eps)) if flat.size else \
         np.zeros(flat.shape[0], np.float32)
     scale = (absmax / np.float32(127.0)).astype(np.float32)
-    q = np.clip(np.rint(flat / scale[:, None]), -128, 127).astype(np.int8)
+    with np.errstate(invalid="ignore"):
+        y = np.rint(flat / scale[:, None])
+    q = np.clip(np.where(np.isnan(y), np.float32(0), y), -128, 127).astype(np.int8)  # NaN in: 0
     return q.reshape(*lead, k), scale.reshape(*lead, k // group_size)
 
 

@@ -22,8 +22,11 @@ def quantize(x_f32: np.ndarray, scale, dim=None) -> np.ndarray:
     """q = clamp(round_half_even(float32(x) / scale), -128, 127) (quant.py:53, :144)."""
     x = np.asarray(x_f32, np.float32)
     d = None if dim is None else (dim if dim >= 0 else dim + x.ndim)
-    y = x / _scale_view(scale, x.ndim, d)
-    return np.clip(np.rint(y.astype(np.float32)), -128, 127).astype(np.int8)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        y = np.rint((x / _scale_view(scale, x.ndim, d)).astype(np.float32))
+    # a zero scale gives +-inf (clamped to 127 / -128) and, for x = 0, NaN: torch's clamp keeps
+    # it and its int8 cast makes it 0
+    return np.clip(np.where(np.isnan(y), np.float32(0), y), -128, 127).astype(np.int8)
 
 
 def dequantize(q: np.ndarray, scale, out_dtype: str, dim=None) -> np.ndarray:

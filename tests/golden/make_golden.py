@@ -412,6 +412,19 @@ def make_sym() -> None:
     c.put("q_ties", "x", x)
     c.put("q_ties", "s", s)
     c.put("q_ties", "q", rt._ref_quantize_per_tensor(x, s))
+    # NaN inputs: round and clamp keep NaN, the int8 cast makes it 0
+    x = torch.tensor([float("nan"), 1.0, -0.3, float("nan"), 100.0], dtype=torch.float32)
+    s = torch.tensor([0.5], dtype=torch.float32)
+    c.put("q_nan", "x", x)
+    c.put("q_nan", "s", s)
+    c.put("q_nan", "q", rt._ref_quantize_per_tensor(x, s))
+    # a zero scale (the public functions reject it; this pins the kernel expression): x / 0 is
+    # +-inf (clamped) or, for x = +-0, NaN (int8 cast: 0)
+    x = torch.tensor([0.0, 1.0, -2.0, -0.0, 3.5e-3, -1e30], dtype=torch.float32)
+    s = torch.tensor([0.0], dtype=torch.float32)
+    c.put("q_zero_scale", "x", x)
+    c.put("q_zero_scale", "s", s)
+    c.put("q_zero_scale", "q", rt._ref_quantize_per_tensor(x, s))
     seed(110)
     x = torch.randn(32, 64) * 0.3
     s = torch.tensor([x.abs().max().item() / 127.0 + 1e-6])
@@ -434,6 +447,13 @@ def make_sym() -> None:
     c.put("ch_inner", "s", s)
     c.put("ch_inner", "dim", np.array(1))
     c.put("ch_inner", "q", rt._ref_quantize_per_channel(x, s, 1))
+    # one channel with a zero scale, zeros included
+    x = torch.tensor([[0.0, 0.3, -0.0], [1.0, -0.5, 0.0], [-2.0, 0.0, 0.25]], dtype=torch.float32)
+    s = torch.tensor([0.1, 0.0, 0.05], dtype=torch.float32)
+    c.put("ch_zero_scale", "x", x)
+    c.put("ch_zero_scale", "s", s)
+    c.put("ch_zero_scale", "dim", np.array(-1))
+    c.put("ch_zero_scale", "q", rt._ref_quantize_per_channel(x, s, -1))
     seed(113)
     s = torch.tensor([0.1, 0.2, 0.15])
     x = torch.randn(2, 3)

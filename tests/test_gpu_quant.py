@@ -28,7 +28,7 @@ def _f(t: torch.Tensor) -> np.ndarray:
 
 
 # ------------------------------------------------------------------ symmetric INT8
-@pytest.mark.parametrize("name", ["q_known", "q_ties", "roundtrip"])
+@pytest.mark.parametrize("name", ["q_known", "q_ties", "roundtrip", "q_nan"])
 def test_quantize_per_tensor_golden(cuda, golden, name):
     c = golden("sym.npz")[name]
     q = tob.quantize_per_tensor(c.tensor("x", cuda), c.tensor("s", cuda))

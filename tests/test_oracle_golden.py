@@ -187,7 +187,7 @@ def test_fp8_layer(golden):
 
 
 # ------------------------------------------------------------------ symmetric INT8
-@pytest.mark.parametrize("name", ["q_known", "q_ties", "roundtrip"])
+@pytest.mark.parametrize("name", ["q_known", "q_ties", "roundtrip", "q_zero_scale", "q_nan"])
 def test_sym_quant_per_tensor(golden, name):
     c = golden("sym.npz")[name]
     assert np.array_equal(sym.quantize(_np(c, "x"), _np(c, "s")), _np(c, "q"))
@@ -203,7 +203,7 @@ def test_sym_dequant(golden):
     assert np.array_equal(sym.dequantize(_np(c, "q"), _np(c, "s"), "f32", int(c["dim"])), _np(c, "y"))
 
 
-@pytest.mark.parametrize("name", ["ch_last", "ch_inner"])
+@pytest.mark.parametrize("name", ["ch_last", "ch_inner", "ch_zero_scale"])
 def test_sym_quant_per_channel(golden, name):
     c = golden("sym.npz")[name]
     assert np.array_equal(sym.quantize(_np(c, "x"), _np(c, "s"), int(c["dim"])), _np(c, "q"))

@@ -107,9 +107,11 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t v) {
   return __half2float(__half(h));
 }
 
-// Round-half-even then clamp to int8, as torch.clamp(torch.round(v), -128, 127).
+// Round-half-even then clamp to int8, as torch.clamp(torch.round(v), -128, 127).to(int8). A NaN
+// (0 / 0 with a zero scale) passes torch's clamp and its int8 cast makes it 0.
 __device__ __forceinline__ int8_t rne_clamp_i8(float v) {
   float r = rintf(v);
+  if (isnan(r)) return 0;
   r = fminf(fmaxf(r, -128.f), 127.f);
   return (int8_t)(int)r;
 }
