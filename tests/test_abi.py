@@ -213,3 +213,27 @@ def test_dropin_fused_and_blas_names():
     from tileops.blas.gemv import gemv as gemv2
 
     assert (gemm, gemv, mm, mv, gemv2) == (tob.gemm, tob.gemv, tob.mm, tob.mv, tob.gemv)
+
+
+def test_public_signatures_match_the_reference():
+    """Every public function of the replaced reference modules exists under the same module
+    path of the drop-in package with the same parameter names, kinds and defaults
+    (tests/golden/signatures.json, recorded from the reference by make_signatures.py)."""
+    import importlib
+    import inspect
+    import json
+
+    import tileops  # noqa: F401  (installs the module aliases)
+
+    spec = json.loads((Path(__file__).resolve().parent / "golden" / "signatures.json").read_text())
+    assert sum(len(v) for v in spec.values()) >= 30
+    for mod_name, funcs in spec.items():
+        mod = importlib.import_module(mod_name)
+        for name, params in funcs.items():
+            fn = getattr(mod, name, None)
+            assert fn is not None, f"{mod_name}.{name} missing"
+            got = []
+            for p in inspect.signature(fn).parameters.values():
+                d = "" if p.default is inspect.Parameter.empty else f"={p.default!r}"
+                got.append(f"{p.name}:{p.kind.name}{d}")
+            assert got == params, f"{mod_name}.{name}: {got} != {params}"
