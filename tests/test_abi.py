@@ -6,6 +6,7 @@ from __future__ import annotations
 
 import ctypes
 import re
+import sys
 from pathlib import Path
 
 import pytest
@@ -237,3 +238,24 @@ def test_public_signatures_match_the_reference():
                 d = "" if p.default is inspect.Parameter.empty else f"={p.default!r}"
                 got.append(f"{p.name}:{p.kind.name}{d}")
             assert got == params, f"{mod_name}.{name}: {got} != {params}"
+
+
+def test_argument_errors_match_the_reference():
+    """Each invalid call of tests/golden/error_cases.py raises the exception type and message the
+    reference raises for it (tests/golden/errors.json, recorded by make_errors.py)."""
+    import json
+
+    import tileops  # noqa: F401  (installs the module aliases)
+    from tileops import fused, quant, quant_awq, quant_fp8, quant_int8
+
+    golden_dir = Path(__file__).resolve().parent / "golden"
+    sys.path.insert(0, str(golden_dir))
+    try:
+        import error_cases
+    finally:
+        sys.path.remove(str(golden_dir))
+    want = json.loads((golden_dir / "errors.json").read_text())
+    got = error_cases.run(error_cases.cases(quant_awq, quant_int8, quant_fp8, quant, fused))
+    assert set(got) == set(want)
+    for name in want:
+        assert got[name] == want[name], f"{name}: {got[name]} != {want[name]}"
