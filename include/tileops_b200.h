@@ -123,8 +123,10 @@ TO_API int to_input_to_fp8(const void* x, int x_dtype, int64_t n, void* q, float
  * scratch (33 KB per GPU, held until the process exits) is built into the library, which caps
  * n at 134,217,728 elements (TO_EINVAL beyond). It allocates nothing. The first call on each
  * device looks up the scratch address with that device current; make that first call before
- * any stream capture. All calls share the one scratch buffer: calls that overlap on the GPU
- * (several streams or host threads at once) race and must be serialised. */
+ * any stream capture. The looked-up address is kept for the life of the process, so the entry
+ * must not be used after cudaDeviceReset (or anything else that destroys the device's primary
+ * context) in the same process. All calls share the one scratch buffer: calls that overlap on
+ * the GPU (several streams or host threads at once) race and must be serialised. */
 TO_API int to_input_to_fp8_noalloc(const void* x, int x_dtype, int64_t n, void* q,
                                    float* dq_scale, void* stream);
 /* replaces tileops/quant_int8.py:109 per_token_group_quant_int8 and :54 per_token_quant_int8

@@ -10,36 +10,57 @@ FP8_MAX = 448.0  # torch.finfo(torch.float8_e4m3fn).max (quant_fp8.py:39-45)
 
 
 def ue8m0(scale: np.ndarray) -> np.ndarray:
-    """quant_fp8.py:48-49: exp2(ceil(log2(max(s, 1e-30)))) with log2 rounded to fp32."""
+    """quant_fp8.py:48-49: exp2(ceil(log2(max(s, 1e-30)))) with log2 rounded to fp32. NaN and
+    inf scales pass through unchanged, as they do through torch's clamp, log2, ceil and exp2."""
     s = np.maximum(np.asarray(scale, np.float32), np.float32(1e-30))
-    return np.ldexp(np.float32(1.0), np.ceil(log2_f32(s)).astype(np.int32)).astype(np.float32)
+    keep = ~np.isfinite(s)
+    with np.errstate(invalid="ignore"):
+        e = np.ceil(log2_f32(np.where(keep, np.float32(1), s))).astype(np.int32)
+    return np.where(keep, s, np.ldexp(np.float32(1.0), e)).astype(np.float32)
 
 
 def input_to_float8(x_f32: np.ndarray, dtype: str):
     """quant_fp8.py:52-63 in ``dtype``: amax = T(max(amax, 1e-12)); s = T(T(1/amax) * 448);
-    q = e4m3(clamp(T(x * s), -448, 448)); returns (codes, float32(1 / s))."""
+    q = e4m3(clamp(T(x * s), -448, 448)); returns (codes, float32(1 / s)).
+
+    NaN products keep their NaN through the clamp, and the e4m3 cast keeps the NaN's sign:
+    0x7F or 0xFF. Which sign the reference's x86 run gives them (single-threaded torch):
+      * bfloat16: torch's vectorised bf16 rounding writes NaN as 0xFFFF (sign set) for every
+        element in whole 32-element blocks from the start of the tensor; the scalar tail
+        rounds NaN to the sign-clear 0x7FC0;
+      * float32 / float16: a NaN in the tensor makes amax, s and every product a sign-clear NaN
+        (0x7F); with a numeric s, a NaN product is 0 * inf, x86's sign-set default NaN (0xFF).
+        In float16, 1e-12 rounds to 0, so an all-zero tensor has s = inf and every product is
+        0 * inf."""
     rnd = rounder(dtype)
-    x = rnd(np.asarray(x_f32, dtype=np.float32))
-    amax = np.float32(np.max(np.abs(x)))
+    x = rnd(np.asarray(x_f32, dtype=np.float32)).reshape(-1)
+    amax = np.float32(np.max(np.abs(x)))  # NaN if any element is NaN, as aminmax
     with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
-        # In float16, 1e-12 rounds to 0: an all-zero tensor divides by zero (s = inf) and
-        # 0 * inf is NaN, which torch's clamp keeps; the reference run on x86 turns that
-        # (sign-set) NaN into the e4m3 code 0xFF.
         amax = rnd(np.maximum(amax, np.float32(1e-12)))
         r = rnd(np.float32(1.0) / amax)
         s = rnd(np.float32(r) * np.float32(FP8_MAX))
         y = rnd(x * np.float32(s))
         nan = np.isnan(y)
         codes = f32_to_e4m3(np.clip(np.where(nan, np.float32(0), y), -FP8_MAX, FP8_MAX))
-        codes = np.where(nan, np.uint8(0xFF), codes).astype(np.uint8)
-        return codes, np.float32(np.float32(1.0) / np.float32(s))
+        if dtype == "bf16":
+            blocked = np.arange(x.size) < (x.size // 32) * 32
+            nan_code = np.where(blocked, np.uint8(0xFF), np.uint8(0x7F))
+        else:
+            nan_code = np.uint8(0x7F) if np.isnan(s) else np.uint8(0xFF)
+        codes = np.where(nan, nan_code, codes).astype(np.uint8)
+        return codes.reshape(np.shape(x_f32)), np.float32(np.float32(1.0) / np.float32(s))
 
 
 def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10, use_ue8m0: bool = False,
                 column_major: bool = False):
     """quant_fp8.py:66-140: scale = max(absmax, eps) / 448 [-> ue8m0];
     q = e4m3(clamp(x / scale, +-448)). Returns (codes shaped like x, scales [..., K/G]; with
-    column_major, the reference's reshape-then-transpose of the flat scales)."""
+    column_major, the reference's reshape-then-transpose of the flat scales).
+
+    A NaN in a group makes its absmax and scale NaN (sign clear). A NaN quotient x / scale keeps
+    the sign the reference's x86 run gives it: with a NaN scale, x's own sign when x is NaN,
+    else clear (0x7F); with a numeric scale (inf / inf, 0 / 0) the sign-set default NaN
+    (0xFF)."""
     x = np.asarray(x_f32, dtype=np.float32)
     lead, k = x.shape[:-1], x.shape[-1]
     flat = x.reshape(-1, group_size)
@@ -47,8 +68,14 @@ def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10, use_ue8m
     scale = (absmax / np.float32(FP8_MAX)).astype(np.float32)
     if use_ue8m0:
         scale = ue8m0(scale)
-    y = np.clip(flat / scale[:, None], -FP8_MAX, FP8_MAX).astype(np.float32)
-    q = f32_to_e4m3(y).reshape(*lead, k)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        y = np.clip(flat / scale[:, None], -FP8_MAX, FP8_MAX).astype(np.float32)
+    nan = np.isnan(y)
+    codes = f32_to_e4m3(np.where(nan, np.float32(0), y))
+    nan_scale = np.isnan(scale)[:, None]
+    neg_nan_x = np.isnan(flat) & np.signbit(flat)
+    nan_code = np.where(nan_scale & ~neg_nan_x, np.uint8(0x7F), np.uint8(0xFF))
+    q = np.where(nan, nan_code, codes).astype(np.uint8).reshape(*lead, k)
     if column_major:
         # quant_fp8.py:134-136: s_flat.reshape(..., G_, M).transpose(-2, -1).contiguous()
         m = x.shape[-2]

@@ -41,6 +41,11 @@ class GoldenCase(dict):
         dt = _TORCH_DTYPES[str(dt)]
         if dt == torch.float8_e4m3fn:
             return torch.from_numpy(np.array(arr, dtype=np.uint8)).view(torch.float8_e4m3fn).to(device)
+        if dt == torch.bfloat16:
+            # bf16 values are stored as their exact fp32 values: keep the top 16 bits, so a NaN
+            # keeps its sign (torch's vectorised fp32 -> bf16 cast would rewrite it)
+            bits = (np.array(arr, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+            return torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(device)
         return torch.from_numpy(np.array(arr)).to(dt).to(device)
 
     def dtype_name(self, field: str) -> str:

@@ -3,7 +3,7 @@ error_cases.py in errors.json. Run from the repository root:
 
     python tests/golden/make_errors.py
 
-The reference is imported from $TILEOPS_REF (default /root/reference)."""
+The reference is imported from the checkout named by the required TILEOPS_REF variable."""
 
 from __future__ import annotations
 
@@ -14,7 +14,9 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TILEOPS_REF", "/root/reference"))
+if not os.environ.get("TILEOPS_REF"):
+    sys.exit("set TILEOPS_REF to the TileOps checkout to record")
+REF = Path(os.environ["TILEOPS_REF"])
 sys.path.insert(0, str(REF))
 sys.path.insert(1, str(HERE))
 

@@ -1,8 +1,8 @@
 """Generates the golden fixtures in this folder by running the REFERENCE implementation
-(llongmarch/TileOps, importable from a checkout at $TILEOPS_REF, default /root/reference)
+(llongmarch/TileOps, imported from the checkout named by the required TILEOPS_REF variable)
 on seeded CPU inputs.
 
-    python tests/golden/make_golden.py
+    TILEOPS_REF=<path to a TileOps checkout> python tests/golden/make_golden.py
 
 Writes awq.npz, int8.npz, fp8.npz, sym.npz, fused.npz (or only the files named on the command
 line: awq, int8, fp8, sym, fused). Each case stores its inputs and the reference's
@@ -27,7 +27,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TILEOPS_REF", "/root/reference"))
+if not os.environ.get("TILEOPS_REF"):
+    sys.exit("set TILEOPS_REF to the TileOps checkout whose outputs the goldens record")
+REF = Path(os.environ["TILEOPS_REF"])
 sys.path.insert(0, str(REF))
 
 import torch  # noqa: E402
@@ -205,6 +207,33 @@ def make_int8() -> None:
     c.put("group_edges", "q", q)
     c.put("group_edges", "s", s)
 
+    # NaN and inf inputs. torch's amax / aminmax propagate NaN: the group's (or tensor's) scale
+    # is NaN and every code of it 0 (the int8 cast of NaN); an inf makes the scale inf.
+    for i, dt in enumerate((torch.float32, torch.float16, torch.bfloat16)):
+        tag = str(dt).replace("torch.", "")
+        seed(74 + i)
+        x = torch.randn(100).to(dt)
+        x[5] = float("nan")
+        q, s = i8.input_to_int8(x)
+        c.put(f"input_nan_{tag}", "x", x)
+        c.put(f"input_nan_{tag}", "q", q)
+        c.put(f"input_nan_{tag}", "s", s)
+        x = torch.randn(4, 64).to(dt)
+        x[2, 17] = float("nan")
+        q, s = i8.per_token_quant_int8(x)
+        c.put(f"token_nan_{tag}", "x", x)
+        c.put(f"token_nan_{tag}", "q", q)
+        c.put(f"token_nan_{tag}", "s", s)
+        x = torch.randn(3, 64).to(dt)
+        x[0, 3] = float("nan")
+        x[1, 40] = float("inf")
+        x[2, 63] = float("-inf")
+        q, s = i8.per_token_group_quant_int8(x, 16)
+        c.put(f"group_nan_{tag}", "x", x)
+        c.put(f"group_nan_{tag}", "group_size", np.array(16))
+        c.put(f"group_nan_{tag}", "q", q)
+        c.put(f"group_nan_{tag}", "s", s)
+
     seed(70)
     bs = [4, 8]
     wq = torch.randint(-128, 127, (10, 24), dtype=torch.int8)
@@ -328,6 +357,55 @@ def make_fp8() -> None:
     c.put("ue8m0_edges", "column_major", np.array(False))
     c.put("ue8m0_edges", "q", q)
     c.put("ue8m0_edges", "s", s)
+
+    # NaN and inf inputs. A NaN makes the tensor's / group's scale NaN; the NaN codes carry the
+    # sign the reference's x86 run gives them (0x7F or 0xFF). 100 elements = three whole
+    # 32-element blocks and a tail of 4, where bfloat16's vectorised and scalar roundings
+    # differ. A sign-set NaN input is written through the bit pattern (float16, float32).
+    neg_nan = torch.tensor([0xFFC00000], dtype=torch.int64).to(torch.int32).view(torch.float32)
+    for i, dt in enumerate((torch.float32, torch.float16, torch.bfloat16)):
+        tag = str(dt).replace("torch.", "")
+        seed(104 + i)
+        x = torch.randn(100).to(dt)
+        x[5] = float("nan")
+        x[98] = float("nan")
+        q, s = fp8.input_to_float8(x, dtype=FP8)
+        c.put(f"input_nan_{tag}", "x", x)
+        c.put(f"input_nan_{tag}", "q", q)
+        c.put(f"input_nan_{tag}", "s", s)
+        x = torch.randn(100).to(dt)
+        x[2] = float("-inf")
+        x[97] = float("inf")
+        q, s = fp8.input_to_float8(x, dtype=FP8)
+        c.put(f"input_inf_{tag}", "x", x)
+        c.put(f"input_inf_{tag}", "q", q)
+        c.put(f"input_inf_{tag}", "s", s)
+        x = torch.randn(4, 64).to(dt)
+        x[0, 3] = float("nan")
+        if dt != torch.bfloat16:
+            x[1, 20] = neg_nan.to(dt)[0]
+        x[2, 40] = float("inf")
+        x[3, 63] = float("-inf")
+        for ue in (False, True):
+            q, s = fp8.per_token_group_quant_fp8(x, 16, dtype=FP8, use_ue8m0=ue)
+            name = f"group_nan_{tag}" + ("_ue8m0" if ue else "")
+            c.put(name, "x", x)
+            c.put(name, "group_size", np.array(16))
+            c.put(name, "ue8m0", np.array(ue))
+            c.put(name, "column_major", np.array(False))
+            c.put(name, "q", q)
+            c.put(name, "s", s)
+    # a zero group with eps = 0: scale 0, every quotient 0 / 0
+    x = torch.zeros(2, 16)
+    x[1, :] = torch.randn(16)
+    q, s = fp8.per_token_group_quant_fp8(x, 16, eps=0.0, dtype=FP8)
+    c.put("group_zero_eps0", "x", x)
+    c.put("group_zero_eps0", "group_size", np.array(16))
+    c.put("group_zero_eps0", "eps", np.array(0.0))
+    c.put("group_zero_eps0", "ue8m0", np.array(False))
+    c.put("group_zero_eps0", "column_major", np.array(False))
+    c.put("group_zero_eps0", "q", q)
+    c.put("group_zero_eps0", "s", s)
 
     seed(100)
     bs = [4, 8]

@@ -4,7 +4,7 @@ drop-in API without the reference checkout. Run from the repository root:
 
     python tests/golden/make_signatures.py
 
-The reference is imported from $TILEOPS_REF (default /root/reference)."""
+The reference is imported from the checkout named by the required TILEOPS_REF variable."""
 
 from __future__ import annotations
 
@@ -16,7 +16,9 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TILEOPS_REF", "/root/reference"))
+if not os.environ.get("TILEOPS_REF"):
+    sys.exit("set TILEOPS_REF to the TileOps checkout to record")
+REF = Path(os.environ["TILEOPS_REF"])
 sys.path.insert(0, str(REF))
 
 # module -> the public functions this library provides from it (None: every public function

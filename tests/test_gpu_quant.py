@@ -27,6 +27,16 @@ def _f(t: torch.Tensor) -> np.ndarray:
     return t.float().cpu().numpy()
 
 
+def _same(a, b) -> bool:
+    """Equal values, a NaN matching a NaN (scales of groups that hold a NaN)."""
+    if isinstance(a, torch.Tensor):
+        a = a.float().cpu().numpy()
+    return np.array_equal(np.asarray(a, np.float32), np.asarray(b, np.float32), equal_nan=True)
+
+
+_NAN = ("float32", "float16", "bfloat16")
+
+
 # ------------------------------------------------------------------ symmetric INT8
 @pytest.mark.parametrize("name", ["q_known", "q_ties", "roundtrip", "q_nan"])
 def test_quantize_per_tensor_golden(cuda, golden, name):
@@ -105,13 +115,14 @@ def test_empty_inputs(cuda):
 # ------------------------------------------------------------------ dynamic INT8
 @pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
                                   "input_zeros_float32", "input_zeros_float16",
-                                  "input_zeros_bfloat16", "input_tiny_float16"])
+                                  "input_zeros_bfloat16", "input_tiny_float16"]
+                         + [f"input_nan_{d}" for d in _NAN])
 def test_input_to_int8_golden(cuda, golden, name):
     c = golden("int8.npz")[name]
     q, s = tob.input_to_int8(c.tensor("x", cuda))
     assert q.dtype == torch.int8
     assert np.array_equal(q.cpu().numpy(), c["q"])
-    assert s.item() == float(c["s"])
+    assert _same(s, c["s"])
 
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
@@ -126,21 +137,22 @@ def test_input_to_int8_vs_oracle(cuda, dtype, n):
 
 
 @pytest.mark.parametrize("name", ["token_2d", "token_nd", "token_bf16", "token_1d", "token_wide",
-                                  "token_edges"])
+                                  "token_edges"] + [f"token_nan_{d}" for d in _NAN])
 def test_per_token_quant_int8_golden(cuda, golden, name):
     c = golden("int8.npz")[name]
     q, s = tob.per_token_quant_int8(c.tensor("x", cuda))
     assert q.shape == tuple(c["q"].shape) and s.shape == tuple(c["s"].shape)
     assert np.array_equal(q.cpu().numpy(), c["q"])
-    assert np.array_equal(s.cpu().numpy(), c["s"])
+    assert _same(s, c["s"])
 
 
-@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d", "group_edges"])
+@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d", "group_edges"]
+                         + [f"group_nan_{d}" for d in _NAN])
 def test_per_token_group_quant_int8_golden(cuda, golden, name):
     c = golden("int8.npz")[name]
     q, s = tob.per_token_group_quant_int8(c.tensor("x", cuda), int(c["group_size"]))
     assert np.array_equal(q.cpu().numpy(), c["q"])
-    assert np.array_equal(s.cpu().numpy(), c["s"])
+    assert _same(s, c["s"])
 
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
@@ -159,13 +171,14 @@ def test_group_quant_int8_vs_oracle(cuda, dtype, rows, k, g):
 # ------------------------------------------------------------------ dynamic FP8
 @pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
                                   "input_zeros_float32", "input_zeros_float16",
-                                  "input_zeros_bfloat16"])
+                                  "input_zeros_bfloat16"]
+                         + [f"input_{k}_{d}" for k in ("nan", "inf") for d in _NAN])
 def test_input_to_float8_golden(cuda, golden, name):
     c = golden("fp8.npz")[name]
     q, s = tob.input_to_float8(c.tensor("x", cuda))
     assert q.dtype == torch.float8_e4m3fn
     assert np.array_equal(_codes(q), c["q"])
-    assert s.item() == float(c["s"])
+    assert _same(s, c["s"])
 
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
@@ -181,15 +194,18 @@ def test_input_to_float8_vs_oracle(cuda, dtype, n):
 
 @pytest.mark.parametrize("name", ["group_f32", "group_ue8m0", "group_bf16_token", "group_f16",
                                   "group_colmajor", "group_colmajor_3d", "group_ue8m0_bf16",
-                                  "ue8m0_edges"])
+                                  "ue8m0_edges"]
+                         + [f"group_nan_{d}{u}" for d in _NAN for u in ("", "_ue8m0")]
+                         + ["group_zero_eps0"])
 def test_per_token_group_quant_fp8_golden(cuda, golden, name):
     c = golden("fp8.npz")[name]
-    q, s = tob.per_token_group_quant_fp8(c.tensor("x", cuda), int(c["group_size"]),
+    eps = float(c["eps"]) if "eps" in c else 1e-10
+    q, s = tob.per_token_group_quant_fp8(c.tensor("x", cuda), int(c["group_size"]), eps=eps,
                                          column_major_scales=bool(c["column_major"]),
                                          use_ue8m0=bool(c["ue8m0"]))
     assert np.array_equal(_codes(q), c["q"])
     assert s.shape == tuple(c["s"].shape)
-    assert np.array_equal(s.cpu().numpy(), c["s"])
+    assert _same(s, c["s"])
 
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
@@ -203,6 +219,47 @@ def test_group_quant_fp8_vs_oracle(cuda, dtype, rows, k, g, ue8m0):
     wq, ws = ofp8.group_quant(_f(x), g, use_ue8m0=ue8m0)
     assert np.array_equal(_codes(q), wq)
     assert np.array_equal(s.cpu().numpy(), ws)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("n", [37, 4099, (1 << 20) + 13])
+def test_tensor_wide_nan_vs_oracle(cuda, dtype, n):
+    """A NaN anywhere makes the tensor's scale NaN: every int8 code 0, every e4m3 code a NaN
+    code with the sign the reference's host run gives it."""
+    g = torch.Generator().manual_seed(n + 11)
+    x = (torch.randn(n, generator=g) * 2).to(_DT[dtype])
+    x[torch.randint(0, n, (3,), generator=g)] = float("nan")
+    q, s = tob.input_to_float8(x.to(cuda))
+    wq, ws = ofp8.input_to_float8(_f(x), dtype)
+    assert np.array_equal(_codes(q), wq)
+    assert _same(s, ws)
+    q, s = tob.input_to_int8(x.to(cuda))
+    wq, ws = oi8.input_to_int8(_f(x), dtype)
+    assert np.array_equal(q.cpu().numpy(), wq)
+    assert _same(s, ws)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("rows,k,g", [(37, 24, 8), (64, 8192, 8192), (256, 4096, 128),
+                                      (5, 65536, 65536)])
+def test_group_nan_inf_vs_oracle(cuda, dtype, rows, k, g):
+    """NaN and +-inf inside groups, for every team shape of the group kernel."""
+    gen = torch.Generator().manual_seed(rows + k + 3)
+    x = (torch.randn(rows, k, generator=gen) * 2).to(_DT[dtype])
+    flat = x.view(-1)
+    idx = torch.randint(0, flat.numel(), (6,), generator=gen)
+    flat[idx[:3]] = float("nan")
+    flat[idx[3]] = float("inf")
+    flat[idx[4]] = float("-inf")
+    for ue8m0 in (False, True):
+        q, s = tob.per_token_group_quant_fp8(x.to(cuda), g, use_ue8m0=ue8m0)
+        wq, ws = ofp8.group_quant(_f(x), g, use_ue8m0=ue8m0)
+        assert np.array_equal(_codes(q), wq)
+        assert _same(s, ws)
+    q, s = tob.per_token_group_quant_int8(x.to(cuda), g)
+    wq, ws = oi8.group_quant(_f(x), g)
+    assert np.array_equal(q.cpu().numpy(), wq)
+    assert _same(s, ws)
 
 
 def test_group_quant_fp8_out_q(cuda):

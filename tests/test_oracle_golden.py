@@ -87,32 +87,43 @@ def test_awq_split_k_invariance(golden):
 
 
 # ------------------------------------------------------------------ INT8
+_NAN_INPUTS = ["input_nan_float32", "input_nan_float16", "input_nan_bfloat16"]
+_NAN_TOKENS = ["token_nan_float32", "token_nan_float16", "token_nan_bfloat16"]
+_NAN_GROUPS = ["group_nan_float32", "group_nan_float16", "group_nan_bfloat16"]
+
+
+def _same(a, b) -> bool:
+    """Equal values, a NaN matching a NaN (scales of groups that hold a NaN)."""
+    return np.array_equal(np.asarray(a, np.float32), np.asarray(b, np.float32), equal_nan=True)
+
+
 @pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
                                   "input_zeros_float32", "input_zeros_float16",
-                                  "input_zeros_bfloat16", "input_tiny_float16"])
+                                  "input_zeros_bfloat16", "input_tiny_float16"] + _NAN_INPUTS)
 def test_input_to_int8(golden, name):
     c = golden("int8.npz")[name]
     q, s = int8.input_to_int8(_np(c, "x"), c.dtype_name("x"))
     assert np.array_equal(q, _np(c, "q"))
-    assert np.float32(s) == np.float32(_np(c, "s"))
+    assert _same(s, _np(c, "s"))
 
 
 @pytest.mark.parametrize("name", ["token_2d", "token_nd", "token_bf16", "token_1d", "token_wide",
-                                  "token_edges"])
+                                  "token_edges"] + _NAN_TOKENS)
 def test_per_token_quant_int8(golden, name):
     c = golden("int8.npz")[name]
     x = _np(c, "x")
     q, s = int8.group_quant(x.reshape(-1, x.shape[-1]), x.shape[-1])
     assert np.array_equal(q.reshape(x.shape), _np(c, "q"))
-    assert np.array_equal(s.reshape(-1), _np(c, "s").reshape(-1))
+    assert _same(s.reshape(-1), _np(c, "s").reshape(-1))
 
 
-@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d", "group_edges"])
+@pytest.mark.parametrize("name", ["group_f32", "group_bf16", "group_f16_3d", "group_edges"]
+                         + _NAN_GROUPS)
 def test_group_quant_int8(golden, name):
     c = golden("int8.npz")[name]
     q, s = int8.group_quant(_np(c, "x"), int(c["group_size"]))
     assert np.array_equal(q, _np(c, "q"))
-    assert np.array_equal(s, _np(c, "s"))
+    assert _same(s, _np(c, "s"))
 
 
 def test_block_dequant_int8(golden):
@@ -141,25 +152,32 @@ def test_w8a8_reference_cpu_port_matches(golden):
 
 
 # ------------------------------------------------------------------ FP8
+_FP8_NAN_INPUTS = [f"input_{k}_{dt}" for k in ("nan", "inf")
+                   for dt in ("float32", "float16", "bfloat16")]
+_FP8_NAN_GROUPS = [f"group_nan_{dt}{u}" for dt in ("float32", "float16", "bfloat16")
+                   for u in ("", "_ue8m0")] + ["group_zero_eps0"]
+
+
 @pytest.mark.parametrize("name", ["input_known", "input_float32", "input_float16", "input_bfloat16",
                                   "input_zeros_float32", "input_zeros_float16",
-                                  "input_zeros_bfloat16"])
+                                  "input_zeros_bfloat16"] + _FP8_NAN_INPUTS)
 def test_input_to_float8(golden, name):
     c = golden("fp8.npz")[name]
     q, s = fp8.input_to_float8(_np(c, "x"), c.dtype_name("x"))
     assert np.array_equal(q, _np(c, "q"))
-    assert np.float32(s) == np.float32(_np(c, "s"))
+    assert _same(s, _np(c, "s"))
 
 
 @pytest.mark.parametrize("name", ["group_f32", "group_ue8m0", "group_bf16_token", "group_f16",
                                   "group_colmajor", "group_colmajor_3d", "group_ue8m0_bf16",
-                                  "ue8m0_edges"])
+                                  "ue8m0_edges"] + _FP8_NAN_GROUPS)
 def test_group_quant_fp8(golden, name):
     c = golden("fp8.npz")[name]
-    q, s = fp8.group_quant(_np(c, "x"), int(c["group_size"]), use_ue8m0=bool(c["ue8m0"]),
+    eps = float(c["eps"]) if "eps" in c else 1e-10
+    q, s = fp8.group_quant(_np(c, "x"), int(c["group_size"]), eps=eps, use_ue8m0=bool(c["ue8m0"]),
                            column_major=bool(c["column_major"]))
     assert np.array_equal(q, _np(c, "q"))
-    assert np.array_equal(s, _np(c, "s"))
+    assert _same(s, _np(c, "s"))
 
 
 def test_block_dequant_fp8(golden):

@@ -40,9 +40,10 @@ def _noalloc(x: torch.Tensor):
 
 
 def _same(a_q, a_s, b_q, b_s):
-    # The tolerance of the quantiser tests: codes and the dequant scale are bit-exact.
+    # The tolerance of the quantiser tests: codes and the dequant scale are bit-exact (a NaN
+    # scale, from a NaN input, matches a NaN scale).
     assert np.array_equal(a_q.view(torch.uint8).cpu().numpy(), b_q.view(torch.uint8).cpu().numpy())
-    assert a_s.item() == b_s.item()
+    assert np.array_equal(a_s.cpu().numpy(), b_s.cpu().numpy(), equal_nan=True)
 
 
 def test_noalloc_matches_workspace_entry_two_calls_in_a_row(cuda):
@@ -65,6 +66,22 @@ def test_noalloc_matches_workspace_entry_two_calls_in_a_row(cuda):
     r3, rs3 = tob.input_to_float8(x3)
     _same(q3, s3, r3, rs3)
     _same(q1b, s1b, r1, rs1)
+
+
+def test_noalloc_nan_input_then_a_clean_one(cuda):
+    # A NaN makes the scale NaN; the next call must not see that NaN left in the scratch.
+    g = torch.Generator().manual_seed(78)
+    x1 = torch.randn(50000, generator=g).to(torch.bfloat16)
+    x1[12345] = float("nan")
+    x1 = x1.to(cuda)
+    x2 = (torch.randn(3000, generator=g) * 0.5).to(cuda)
+    q1, s1 = _noalloc(x1)
+    q2, s2 = _noalloc(x2)
+    r1, rs1 = tob.input_to_float8(x1)
+    r2, rs2 = tob.input_to_float8(x2)
+    assert torch.isnan(s1).item()
+    _same(q1, s1, r1, rs1)
+    _same(q2, s2, r2, rs2)
 
 
 def test_noalloc_rejects_inputs_beyond_its_scratch(cuda):

@@ -330,12 +330,12 @@ int launch_gemv_stream(const void* x, const int32_t* qw, const void* s, const in
 // A/B switches for measurements: TOB_GEMV_GENERAL=1 routes M <= 4 to the general streaming
 // kernel instead of the prefetching one; TOB_AWQ_SMALL_M=0 skips the TMA-fed small-M kernel.
 bool gemv_stream_enabled() {
-  static const bool on = getenv("TOB_GEMV_GENERAL") == nullptr;
+  static const bool on = tuning_env("TOB_GEMV_GENERAL") == nullptr;
   return on;
 }
 bool small_m_enabled() {
   static const bool on = [] {
-    const char* v = getenv("TOB_AWQ_SMALL_M");
+    const char* v = tuning_env("TOB_AWQ_SMALL_M");
     return v == nullptr || v[0] != '0';
   }();
   return on;
@@ -343,7 +343,7 @@ bool small_m_enabled() {
 // Largest M routed to the register-MMA kernel (measurement override TOB_AWQ_SMALL_M_MAX).
 int64_t small_m_max() {
   static const int64_t v = [] {
-    const char* e = getenv("TOB_AWQ_SMALL_M_MAX");
+    const char* e = tuning_env("TOB_AWQ_SMALL_M_MAX");
     const int64_t w = e ? atoll(e) : 0;
     return (w >= 2 && w <= 64) ? w : 64;
   }();

@@ -356,7 +356,7 @@ bool plan_small_m(int64_t K, int64_t G, int kchunk, SmPlan* p) {
   p->z_bytes = round128(p->szrows * CW * 4);
   p->tot_bytes = NT * 8 * CW * 8 * 4;
   p->stages = std::min(kchunk / kRows, kSmMaxStages);
-  if (const char* v = getenv("TOB_SMALL_M_STAGES")) {  // measurement override
+  if (const char* v = tuning_env("TOB_SMALL_M_STAGES")) {  // measurement override
     const int want = atoi(v);
     if (want >= 1) p->stages = std::min(p->stages, want);
   }
@@ -434,7 +434,7 @@ int dispatch_small_m(const void* x, const int32_t* qw, const void* s, const int3
   const int64_t tiles = ceil_div(words, 8 * wpq);
   int ksplit = 1;
   while (ksplit < 8 && tiles * ksplit < 2 * sms && K >= (int64_t)ksplit * 2 * 256) ksplit *= 2;
-  if (const char* v = getenv("TOB_SMALL_M_KSPLIT")) {  // measurement override: 1, 2, 4 or 8
+  if (const char* v = tuning_env("TOB_SMALL_M_KSPLIT")) {  // measurement override: 1, 2, 4 or 8
     const int want = atoi(v);
     if (want == 1 || want == 2 || want == 4 || want == 8) ksplit = want;
   }

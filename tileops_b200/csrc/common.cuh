@@ -8,6 +8,7 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "../../include/tileops_b200.h"
 
@@ -33,6 +34,17 @@ cudaError_t ensure_smem_attr(const void* func, int bytes);
 int* device_error_ptr();
 // Process-wide launch-overlap switch (programmatic dependent launch for streaming kernels).
 bool launch_overlap();
+// Measurement overrides of the kernel dispatch (tile shapes, splits, stage counts) are read from
+// the environment only in a build compiled with -DTOB_TUNING; the product library dispatches on
+// shapes alone, so a stray environment variable cannot change its kernels or numerics.
+inline const char* tuning_env(const char* name) {
+#ifdef TOB_TUNING
+  return getenv(name);
+#else
+  (void)name;
+  return nullptr;
+#endif
+}
 // Codes kernels write into the error word.
 enum DeviceError : int { kErrNone = 0, kErrWaitTimeout = 1, kErrTmemAlloc = 2, kErrSmemAlign = 3 };
 
@@ -154,9 +166,15 @@ template <typename T, int N> struct alignas(sizeof(T) * N) Pack {
   T v[N];
 };
 
-// Warp-level max reduction across the low `width` lanes groups (width power of two <= 32).
-__device__ __forceinline__ float warp_max(float v, int width) {
-  for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+// Ordering key of |v|: the bit pattern of v with the sign cleared. Keys of non-negative floats
+// order like the floats, and every NaN key lies above +inf's, so an unsigned maximum over keys
+// is NaN as soon as one input is NaN -- the result torch's amax / aminmax give (fmaxf would
+// skip the NaN instead).
+__device__ __forceinline__ unsigned abs_key(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
+
+// Unsigned maximum across aligned groups of `width` lanes (width a power of two <= 32).
+__device__ __forceinline__ unsigned warp_max_key(unsigned v, int width) {
+  for (int o = width >> 1; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
 

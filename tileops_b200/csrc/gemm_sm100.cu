@@ -8,10 +8,12 @@
 // Layout: A [M, K] and B [N, K] row-major ("K-major"), both streamed by TMA in 128-byte K
 // slices with the 128-byte swizzle into a STAGES-deep shared-memory ring.
 //
-// CTA roles (192 threads, one CTA per SM, persistent over output tiles):
+// CTA roles (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer (one thread)      full[s]  <- TMA bytes       empty[s] -> wait
 //   warp 1      MMA issuer   (one thread)      empty[s] <- tcgen05.commit  tfull[b] <- commit
-//   warps 2..5  epilogue: TMEM -> registers -> scales -> global, then arrive on tempty[b]
+//   warps 2..9  epilogue, two warps per TMEM lane quarter taking alternate 32-column chunks:
+//               TMEM -> registers -> scales -> staged TMA stores, then arrive on tempty[b]
+// The 2-CTA kernel (k_gemm_pair) adds an eleventh warp that issues the B copies.
 // Accumulators live in tensor memory, double-buffered when two fit in 512 columns, so the
 // epilogue of tile i overlaps the main loop of tile i+1. A tile is BM x BN with BM = 128 or
 // 256 (two M=128 MMAs sharing each B slice, for small-M layers that must spread N over all SMs).
@@ -45,10 +47,6 @@ struct Epi {
   int32_t* acc_out;  // optional [M, N] raw int32 accumulators (kind::i8 only)
   int policy_a;      // L2 policy for A loads: 0 normal, 1 evict_first, 2 evict_last
   int policy_b;
-  // Optional timeline for tuning (null in production): per CTA, per K step, the global time
-  // the producer issued the stage, the MMA thread saw it land, and the MMA thread released it.
-  uint64_t* trace;
-  int trace_steps;
   int tma_store;     // 16-bit C written through shared-memory staging + TMA stores
 };
 
@@ -284,16 +282,8 @@ __device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_
   uint32_t* recv = reinterpret_cast<uint32_t*>(sA + kRecvOff);   // the peer's, for this CTA
   auto slot = [&](int c, int jj) { return ((c * 8 + jj) * 128 + q * 32 + lane) * 4; };
 
-  // Tuning timeline (null in production): per CTA, the chunk-trace slots of the regular
-  // epilogue hold entry, accumulator ready, barrier 1, copy issued, received and end.
-  uint64_t* ptr = (ep.trace != nullptr && warp == 2 && lane == 0)
-                      ? ep.trace + (int64_t)gridDim.x * ep.trace_steps * 3 + gridDim.x * 2 +
-                            (int64_t)blockIdx.x * 32
-                      : nullptr;
-  if (ptr) ptr[0] = globaltimer_ns();
   const bool ok = mbar_wait(tfull, 0, abort_flag, err);
   tc_fence_after();
-  if (ptr) ptr[1] = globaltimer_ns();
   if (ok) {
     // The main loop is done, so this CTA's ring is free: stage the peer's half.
 #pragma unroll 1
@@ -314,7 +304,6 @@ __device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_
   }
   fence_proxy_async_smem();  // the staged words are read by the bulk copy (async proxy)
   cluster_sync_all();        // 1: both halves staged; both rings free to receive
-  if (ptr) ptr[2] = globaltimer_ns();
   if (warp == 2 && lane == 0) {
     const uint32_t dst = mapa_shared(smem_u32(recv), (uint32_t)other);
     const uint32_t bar = mapa_shared(smem_u32(recv_bar), (uint32_t)other);
@@ -324,9 +313,7 @@ __device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_
       bulk_copy_to_peer(dst + off, reinterpret_cast<uint8_t*>(stage) + off,
                         (uint32_t)min(kPiece, kXfer - off), bar);
   }
-  if (ptr) ptr[3] = globaltimer_ns();
   const bool got = mbar_wait(recv_bar, 0, abort_flag, err);
-  if (ptr) ptr[4] = globaltimer_ns();
   // 2 (split): this CTA's copy has landed in the peer once the peer arrives; the peer's shared
   // memory may be released only after that, so the wait is at the very end.
   cluster_arrive_release();
@@ -398,7 +385,6 @@ __device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_
   tc_fence_before();
   __syncwarp();
   if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
-  if (ptr) ptr[5] = globaltimer_ns();
   cluster_wait_acquire();
 }
 
@@ -456,9 +442,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int pre = 0;  // stages of the first tile already requested
   uint64_t pol_a = 0, pol_b = 0;
   if (threadIdx.x == 0) {
-    if (KS2 && ep.trace != nullptr)  // tuning timeline: kernel entry of this CTA
-      ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + gridDim.x * 2 + blockIdx.x * 32 + 6] =
-          globaltimer_ns();
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
@@ -491,8 +474,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       pre = min(STAGES, kb_n);
       for (int it = 0; it < pre; ++it) {
         const int kb = kb_lo + (k0 + it) % kb_n;
-        if (ep.trace != nullptr && it < ep.trace_steps)
-          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
         mbar_arrive_expect_tx(full + it, C::kStageBytes);
         tma_load_2d(sA + (size_t)it * C::kABytes, &tmA, kb * C::kBK, mt * BM, full + it, pol_a);
         if constexpr (BMN)
@@ -531,8 +512,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int it = (t == t0 ? pre : 0); it < kb_n; ++it, ++step) {
           const int kb = kb_lo + (k0 + it) % kb_n;
           if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
-          if (ep.trace != nullptr && step < ep.trace_steps)
-            ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 0] = globaltimer_ns();
           mbar_arrive_expect_tx(full + s, C::kStageBytes);
           tma_load_2d(sA + (size_t)s * C::kABytes, &tmA, kb * C::kBK, mt * BM, full + s, pol_a);
           if constexpr (BMN)
@@ -579,8 +558,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int it = 0; it < kb_n; ++it, ++step) {
           if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
           tc_fence_after();
-          const bool tr = ep.trace != nullptr && step < ep.trace_steps;
-          if (tr) ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 1] = globaltimer_ns();
           const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
           const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
 #pragma unroll
@@ -596,7 +573,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           any = true;
           umma_commit(empty + s);
-          if (tr) ep.trace[((int64_t)blockIdx.x * ep.trace_steps + step) * 3 + 2] = globaltimer_ns();
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
@@ -640,10 +616,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!mbar_wait(tfull + buf, aph, abort_flag, err)) break;
       tc_fence_after();
-      // Epilogue timeline (tuning only): slots [2*gridDim.x*steps*3 ...] hold per-CTA
-      // (start, end) of the first tile's epilogue, written by lane 0 of the first epilogue warp.
-      const bool etr = ep.trace != nullptr && i == 0 && warp == 2 && lane == 0;
-      if (etr) ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + blockIdx.x * 2] = globaltimer_ns();
       constexpr int kChunks = (BN + 31) / 32;
 #pragma unroll 1
       for (int h = 0; h < C::kHalves; ++h) {
@@ -654,11 +626,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
           if (((h * kChunks + c0 / 32) & 1) != eg) continue;  // the two warps alternate chunks
-          const bool ctr = etr && h == 0 && c0 / 32 < 8;  // per-chunk epilogue timeline
-          uint64_t* ctp = ctr ? ep.trace + (int64_t)gridDim.x * ep.trace_steps * 3 + gridDim.x * 2 +
-                                    ((int64_t)blockIdx.x * 8 + c0 / 32) * 4
-                              : nullptr;
-          if (ctr) ctp[0] = globaltimer_ns();
           const bool wide = (BN - c0) >= 32;  // BN = 80 ends with a 16-column chunk
           uint32_t r[32];
           const uint32_t taddr =
@@ -666,13 +633,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld16(taddr, r);
           if (wide) tmem_ld16(taddr + 16, r + 16);
           tmem_ld_wait();
-          if (ctr) ctp[1] = globaltimer_ns();
           const int col0 = nt * BN + c0;
           if (col0 >= N) continue;
           const int valid = min(wide ? 32 : 16, N - col0);
           float v[32];
           scale_chunk32<KD, BN>(r, v, sa, sbt, c0);
-          if (ctr) ctp[2] = globaltimer_ns();
           if (KD == Kind::I8 && ep.acc_out != nullptr && row_ok) {
             int32_t* dst = ep.acc_out + (int64_t)row * N + col0;
 #pragma unroll
@@ -704,7 +669,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               tma_store_2d(wide ? &tmC : &tmC16, col0, row0, stg);
               bulk_commit();
             }
-            if (ctr) ctp[3] = globaltimer_ns();
           } else if (row_ok) {
             store_direct<KD>(v, ep, (int64_t)row * N + col0, col0, valid, N);
           }
@@ -712,7 +676,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (etr) ep.trace[(int64_t)gridDim.x * ep.trace_steps * 3 + blockIdx.x * 2 + 1] = globaltimer_ns();
       if (lane == 0) mbar_arrive(tempty + buf);
     }
     if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
@@ -1040,12 +1003,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int kblocks = (K + C::kBK - 1) / C::kBK;
   const bool misaligned = (smem_u32(smem_raw) & 1023u) != 0;
 
-  // Tuning timeline (null in production): per stage the producer's issue time and (leader) the
-  // MMA thread's land time; per CTA entry, roles start, accumulators ready, epilogue end.
-  uint64_t* phases = ep.trace != nullptr ? ep.trace + (int64_t)gridDim.x * ep.trace_steps * 3 +
-                                               gridDim.x * 2 + (int64_t)blockIdx.x * 32
-                                         : nullptr;
-  if (phases && threadIdx.x == 0) phases[0] = globaltimer_ns();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full + s, 1);   // the leader's producer arrives; both CTAs' bytes complete it
@@ -1104,8 +1061,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     for (int it = 0; it < pre; ++it) {
       const int kb = (k0 + it) % kblocks;
       if (a_issuer) {
-        if (ep.trace != nullptr && it < ep.trace_steps)
-          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
         if (rank == 0) mbar_arrive_expect_tx(full + it, 2 * C::kStageBytes);
         load_stage(it, kb, lead_full + it * 8u);
       } else {
@@ -1115,20 +1070,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   };
   // The cluster barrier that publishes both CTAs' barriers is split: every thread arrives at
   // once, the leader's first ring and the tensor-memory allocation run while it completes.
-  if (phases && threadIdx.x == 0) phases[4] = globaltimer_ns();
   cluster_arrive_relaxed();
   if ((a_issuer || b_issuer) && !misaligned && rank == 0) request_first_ring();
-  if (phases && threadIdx.x == 32) phases[6] = globaltimer_ns();
   if (warp == 1) tmem_alloc_pair<C::kTmemCols>(tmem_holder);
-  if (phases && threadIdx.x == 32) phases[7] = globaltimer_ns();
   cluster_wait_acquire();  // both CTAs' barriers exist: copies and commits may signal them
-  if (phases && threadIdx.x == 0) phases[5] = globaltimer_ns();
   if ((a_issuer || b_issuer) && !misaligned && rank == 1) request_first_ring();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  if (phases && threadIdx.x == 0) phases[1] = globaltimer_ns();
 
   if (misaligned) {
     // nothing to do; fall through to the teardown
@@ -1145,8 +1095,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (!mbar_wait(empty + s, ph ^ 1, abort_flag, err)) { ok = false; break; }
         const uint32_t bar = lead_full + (uint32_t)s * 8u;
         if (a_issuer) {
-          if (ep.trace != nullptr && it < ep.trace_steps)
-            ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 0] = globaltimer_ns();
           if (rank == 0) {
             mbar_arrive_expect_tx(full + s, 2 * C::kStageBytes);
             issued_mask |= 1u << s;
@@ -1185,8 +1133,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       for (int it = 0; it < kblocks; ++it) {
         if (!mbar_wait(full + s, ph, abort_flag, err)) { ok = false; break; }
         tc_fence_after();
-        if (ep.trace != nullptr && it < ep.trace_steps)
-          ep.trace[((int64_t)blockIdx.x * ep.trace_steps + it) * 3 + 1] = globaltimer_ns();
         const uint32_t a0 = smem_u32(sA + (size_t)s * C::kABytes);
         const uint32_t b0 = smem_u32(sB + (size_t)s * C::kBBytes);
 #pragma unroll
@@ -1221,7 +1167,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const float sa = row_ok ? __ldg(ep.a_s + (int64_t)row * ep.a_s_ld) : 0.f;
     const bool ok = mbar_wait(tfull, 0, abort_flag, err);
     tc_fence_after();
-    if (phases && warp == 2 && lane == 0) phases[2] = globaltimer_ns();
     if (ok) {
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -1265,7 +1210,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     tc_fence_before();
     __syncwarp();
     if (ep.tma_store && lane == 0) bulk_wait_read<0>();  // stores have read their slabs
-    if (phases && warp == 2 && lane == 0) phases[3] = globaltimer_ns();
   }
 
   tc_fence_before();
@@ -1598,7 +1542,7 @@ int launch_gemm_pair(const void* a, const void* b, int64_t M, int64_t N, int64_t
 // TOB_GEMM_TILE=<BM>x<BN> forces one of the compiled tile shapes (tuning and tests).
 inline int forced_tile() {
   static int v = [] {
-    const char* e = getenv("TOB_GEMM_TILE");
+    const char* e = tuning_env("TOB_GEMM_TILE");
     if (!e) return 0;
     int bm = 0, bn = 0;
     if (sscanf(e, "%dx%d", &bm, &bn) != 2) return 0;
@@ -1625,20 +1569,20 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
   // 128 < M <= 256 with every 256 x 160 tile on a CTA pair in one wave: split K over the pair
   // (half the A and B bytes per SM). TOB_GEMM_KSPLIT=0 disables it (measurements).
   static const bool ks2_on = [] {
-    const char* v = getenv("TOB_GEMM_KSPLIT");
+    const char* v = tuning_env("TOB_GEMM_KSPLIT");
     return v == nullptr || v[0] != '0';
   }();
   // Those with a 16-bit output (TMA-stored rows) run as 2-CTA (cta_group::2) tiles of
   // 256 x 160: the same halved operand bytes per SM, without the partial-sum exchange.
   // TOB_GEMM_PAIR=0 keeps them on the K-split pair (measurements).
   static const bool pair_on = [] {
-    const char* v = getenv("TOB_GEMM_PAIR");
+    const char* v = tuning_env("TOB_GEMM_PAIR");
     return v == nullptr || v[0] != '0';
   }();
   if (pair_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && ep.tma_store) {
     // K slices per copy (measurement override TOB_PAIR_SLICES = 1, 2 or 4)
     static const int slices = [] {
-      const char* v = getenv("TOB_PAIR_SLICES");
+      const char* v = tuning_env("TOB_PAIR_SLICES");
       return v == nullptr ? 2 : atoi(v);
     }();
     if ((K * KindTraits<KD>::kElemBytes) % 128 != 0 || slices == 1)
@@ -1699,7 +1643,6 @@ int w8a8_tc_launch(bool fp8, const void* a, const void* b, const float* a_s, con
     if (!aligned16(a) || !aligned16(b)) return TO_EUNSUPPORTED;
     if (M * N < 128 * 128 || ceil_div(M, 128) * ceil_div(N, 128) > INT32_MAX)
       return TO_EUNSUPPORTED;
-    if (getenv("TOB_GEMM_BS_GENERIC") != nullptr) return TO_EUNSUPPORTED;  // measurement
     const int64_t kt = ceil_div(K, bk);
     sm100::Epi ep;
     memset(&ep, 0, sizeof(ep));
@@ -1740,18 +1683,7 @@ int w8a8_tc_launch(bool fp8, const void* a, const void* b, const float* a_s, con
   const bool small_m = M <= 256;
   ep.policy_a = small_m ? 2 : 0;
   ep.policy_b = small_m ? 1 : 0;
-  ep.trace = nullptr;
-  ep.trace_steps = 0;
-  ep.tma_store = (c_dtype == TO_BF16 || c_dtype == TO_F16) && (N % 8 == 0) && aligned16(c) &&
-                 getenv("TOB_GEMM_DIRECT_STORE") == nullptr;
-  if (const char* e = getenv("TOB_GEMM_TRACE")) {  // "<device pointer>:<steps>" (tuning only)
-    unsigned long long p = 0;
-    int steps = 0;
-    if (sscanf(e, "%llx:%d", &p, &steps) == 2) {
-      ep.trace = reinterpret_cast<uint64_t*>(p);
-      ep.trace_steps = steps;
-    }
-  }
+  ep.tma_store = (c_dtype == TO_BF16 || c_dtype == TO_F16) && (N % 8 == 0) && aligned16(c);
   if (fp8) return sm100::launch_gemm<sm100::Kind::E4M3>(a, b, M, N, K, ep, st);
   return sm100::launch_gemm<sm100::Kind::I8>(a, b, M, N, K, ep, st);
 }

@@ -7,6 +7,7 @@
 // count; all float arithmetic is IEEE round-to-nearest-even so results match the
 // reference's torch expressions bit for bit.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -155,9 +156,20 @@ __device__ __forceinline__ int64_t scale_offset(int64_t g, const ScaleLayout& sl
 // 2^ceil(log2(max(s, 1e-30))) with log2 rounded to fp32 first, as torch evaluates
 // torch.exp2(torch.ceil(torch.log2(s))) (quant_fp8.py:48-49).
 __device__ __forceinline__ float ue8m0_round(float s) {
+  if (isinf(s)) return s;
   s = fmaxf(s, 1e-30f);
   const float l = (float)log2((double)s);
   return ldexpf(1.0f, (int)ceilf(l));
+}
+
+// e4m3 code of a NaN quotient x / scale, as the reference's fp32 division and cast produce it
+// on the x86 host it is pinned to: with a NaN scale (a NaN in the group) the quotient is the
+// NaN operand that comes first -- x itself when x is NaN, else the scale's sign-clear NaN --
+// and the cast keeps its sign (0x7F or 0xFF); with a numeric scale the NaN comes from an
+// invalid operation (inf / inf, 0 / 0), whose default NaN has the sign set (0xFF).
+__device__ __forceinline__ uint8_t nan_code_div(float x, bool nan_scale) {
+  if (!nan_scale) return 0xFF;
+  return (isnan(x) && (__float_as_uint(x) >> 31)) ? (uint8_t)0xFF : (uint8_t)0x7F;
 }
 
 template <typename T, bool FP8, int V, int MAXV>
@@ -171,7 +183,7 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
   const int teams_per_cta = blockDim.x >> team_log2;
   const int team_id = threadIdx.x >> team_log2;
   const int nvec = G / V;
-  __shared__ float red[32];
+  __shared__ unsigned red[32];
   const float qmax = FP8 ? 448.0f : 127.0f;
 
   for (int64_t g0 = (int64_t)blockIdx.x * teams_per_cta; g0 < n_groups;
@@ -180,47 +192,50 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
     const bool active = g < n_groups;
     const T* xg = x + g * (int64_t)G;
     Pack<T, V> cache[MAXV];
-    float amax = 0.f;
+    unsigned amax = 0u;  // abs_key of the group's largest |x|; a NaN anywhere makes it NaN
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
       const int v = lane + i * team;
       if (active && v < nvec) {
         cache[i] = ld_pack<T, V>(xg + (int64_t)v * V);
 #pragma unroll
-        for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(to_f32(cache[i].v[j])));
+        for (int j = 0; j < V; ++j) amax = max(amax, abs_key(to_f32(cache[i].v[j])));
       }
     }
     for (int v = lane + MAXV * team; active && v < nvec; v += team) {
       Pack<T, V> t = ld_pack<T, V>(xg + (int64_t)v * V);
 #pragma unroll
-      for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(to_f32(t.v[j])));
+      for (int j = 0; j < V; ++j) amax = max(amax, abs_key(to_f32(t.v[j])));
     }
     if (team <= 32) {
-      amax = warp_max(amax, team);
+      amax = warp_max_key(amax, team);
     } else {
-      amax = warp_max(amax, 32);
+      amax = warp_max_key(amax, 32);
       if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
       __syncthreads();
       // Several teams of 64..1024 threads can share a CTA; each reads only its own warps.
-      float m = 0.f;
+      unsigned m = 0u;
       const int w0 = (team_id * team) >> 5;
-      for (int w = 0; w < (team >> 5); ++w) m = fmaxf(m, red[w0 + w]);
+      for (int w = 0; w < (team >> 5); ++w) m = max(m, red[w0 + w]);
       amax = m;
       __syncthreads();
     }
-    // scale = clamp(absmax, min=eps) / qmax  (fp32, IEEE division)
-    float scale = __fdiv_rn(fmaxf(amax, eps), qmax);
-    if (FP8 && ue8m0) scale = ue8m0_round(scale);
+    // scale = clamp(absmax, min=eps) / qmax  (fp32, IEEE division). A NaN absmax passes the
+    // reference's clamp, division and UE8M0 rounding unchanged (quiet NaN, sign clear).
+    const float amax_f = __uint_as_float(amax);
+    const bool nan_group = isnan(amax_f);
+    float scale = nan_group ? amax_f : __fdiv_rn(fmaxf(amax_f, eps), qmax);
+    if (FP8 && ue8m0 && !nan_group) scale = ue8m0_round(scale);
     if (active && lane == 0) scales[scale_offset(g, sl)] = scale;
-
     uint8_t* qg = qout + g * (int64_t)G;
     auto emit = [&](int v, const Pack<T, V>& t) {
       Pack<uint8_t, V> o;
 #pragma unroll
       for (int j = 0; j < V; ++j) {
-        const float y = __fdiv_rn(to_f32(t.v[j]), scale);
+        const float xv = to_f32(t.v[j]);
+        const float y = __fdiv_rn(xv, scale);
         if (FP8) {
-          o.v[j] = f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
+          o.v[j] = isnan(y) ? nan_code_div(xv, nan_group) : f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
         } else {
           o.v[j] = (uint8_t)rne_clamp_i8(y);
         }
@@ -265,35 +280,48 @@ int launch_group_quant(const void* x, int64_t n_groups, int64_t G, float eps, in
 }
 
 // ------------------------------------------------------------------ tensor-wide dynamic quant
-// Pass 1: amax = max |x| folded into one word with atomicMax on the float's bit pattern
-// (non-negative floats order like their unsigned bit patterns).
+// Pass 1: amax = max |x| folded into one word with atomicMax on abs_key (NaN above every number,
+// so a NaN anywhere makes the tensor's amax NaN, as the reference's aminmax does).
 template <typename T, int V>
 __global__ void __launch_bounds__(kThreads) k_absmax(const T* __restrict__ x, int64_t n,
                                                     unsigned* __restrict__ amax_bits) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t nvec = n / V;
-  float m = 0.f;
+  unsigned m = 0u;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
     Pack<T, V> v = ld_pack<T, V>(x + i * V);
 #pragma unroll
-    for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f32(v.v[j])));
+    for (int j = 0; j < V; ++j) m = max(m, abs_key(to_f32(v.v[j])));
   }
   for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    m = fmaxf(m, fabsf(to_f32(x[i])));
-  m = warp_max(m, 32);
-  __shared__ float red[kThreads / 32];
+    m = max(m, abs_key(to_f32(x[i])));
+  m = warp_max_key(m, 32);
+  __shared__ unsigned red[kThreads / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float b = 0.f;
-    for (int w = 0; w < kThreads / 32; ++w) b = fmaxf(b, red[w]);
-    atomicMax(amax_bits, __float_as_uint(b));
+    unsigned b = 0u;
+    for (int w = 0; w < kThreads / 32; ++w) b = max(b, red[w]);
+    atomicMax(amax_bits, b);
   }
 }
 
+// e4m3 code of a NaN product T(x * s) in the reference's tensor-wide quantiser, as its x86 run
+// gives it. bfloat16: torch's vectorised bf16 rounding writes every NaN as 0xFFFF (sign set)
+// in whole 32-element blocks from the start of the tensor, its scalar tail rounding as the
+// sign-clear 0x7FC0. float32 / float16: a NaN scale (a NaN in the tensor) gives a sign-clear
+// NaN; with a numeric scale the NaN comes from 0 * inf, the sign-set default NaN.
+template <typename T>
+__device__ __forceinline__ uint8_t nan_code_mul(int64_t i, int64_t n_blocked, bool nan_scale) {
+  if (std::is_same<T, __nv_bfloat16>::value) return i < n_blocked ? (uint8_t)0xFF : (uint8_t)0x7F;
+  return nan_scale ? (uint8_t)0x7F : (uint8_t)0xFF;
+}
+
 // Pass 2, in the input dtype T exactly as the reference's expression evaluates:
-//   amax = T(max(amax, 1e-12)); s = T(T(1/amax) * qmax); q = cast(clamp(T(x*s), qmin, qmax)),
-// NaN products included (see quant1).
+//   amax = T(max(amax, 1e-12)); s = T(T(1/amax) * qmax); q = cast(clamp(T(x*s), qmin, qmax)).
+// A NaN amax passes the clamp, so s and every product are NaN. NaN products survive the clamp;
+// the int8 cast makes them 0, the e4m3 cast a NaN code (nan_code_mul). In float16 the 1e-12
+// floor rounds to 0, so an all-zero tensor has s = inf and NaN products 0 * inf.
 // The int8 cast truncates toward zero (torch .to(int8)); the fp8 cast rounds to nearest even.
 template <typename T, bool FP8, int V>
 __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__ x, int64_t n,
@@ -302,16 +330,16 @@ __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__
                                                           float* __restrict__ dq_scale) {
   const float qmax = FP8 ? 448.0f : 127.0f;
   const float qmin = FP8 ? -448.0f : -128.0f;
-  const float amax = round_to<T>(fmaxf(__uint_as_float(*amax_bits), 1e-12f));
+  const float amax_raw = __uint_as_float(*amax_bits);
+  const bool nan_scale = isnan(amax_raw);
+  const float amax = nan_scale ? amax_raw : round_to<T>(fmaxf(amax_raw, 1e-12f));
   const float r = round_to<T>(__frcp_rn(amax));
   const float s = round_to<T>(__fmul_rn(r, qmax));
+  const int64_t n_blocked = n & ~(int64_t)31;
   if (blockIdx.x == 0 && threadIdx.x == 0) *dq_scale = __frcp_rn(s);
-  auto quant1 = [&](float xv) -> uint8_t {
+  auto quant1 = [&](float xv, int64_t i) -> uint8_t {
     float y = round_to<T>(__fmul_rn(xv, s));
-    // NaN (0 * inf: in float16 the 1e-12 floor rounds to 0, so an all-zero tensor has s = inf)
-    // survives the reference's clamp; its int8 cast gives 0 and, on the CPU it is pinned to,
-    // its e4m3 cast the sign-set NaN code 0xFF.
-    if (isnan(y)) return FP8 ? (uint8_t)0xFF : (uint8_t)0;
+    if (isnan(y)) return FP8 ? nan_code_mul<T>(i, n_blocked, nan_scale) : (uint8_t)0;
     y = fminf(fmaxf(y, qmin), qmax);
     if (FP8) return f32_to_e4m3(y);
     return (uint8_t)(int8_t)(int)y;  // truncation toward zero
@@ -322,11 +350,11 @@ __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__
     Pack<T, V> v = ld_pack<T, V>(x + i * V);
     Pack<uint8_t, V> o;
 #pragma unroll
-    for (int j = 0; j < V; ++j) o.v[j] = quant1(to_f32(v.v[j]));
+    for (int j = 0; j < V; ++j) o.v[j] = quant1(to_f32(v.v[j]), i * V + j);
     st_pack<uint8_t, V>(q + i * V, o);
   }
   for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    q[i] = quant1(to_f32(x[i]));
+    q[i] = quant1(to_f32(x[i]), i);
 }
 
 template <typename T, bool FP8>
@@ -396,47 +424,47 @@ constexpr int64_t kNoAllocChunk = 16384;
 constexpr int64_t kNoAllocMaxElems = (int64_t)kNoAllocSlots * kNoAllocChunk;  // 134,217,728
 static __device__ __align__(256) unsigned g_noalloc_amax[kNoAllocSlots + 64];
 
-// CTA b: max |x| over elements [b * kNoAllocChunk, min(n, (b + 1) * kNoAllocChunk)).
+// CTA b: max |x| (as abs_key) over elements [b * kNoAllocChunk, min(n, (b + 1) * kNoAllocChunk)).
 template <typename T, int V>
 __global__ void __launch_bounds__(kThreads) k_absmax_chunks(const T* __restrict__ x, int64_t n,
                                                            unsigned* __restrict__ partial) {
   const int64_t beg = (int64_t)blockIdx.x * kNoAllocChunk;
   const int64_t end = min(n, beg + kNoAllocChunk);
-  float m = 0.f;
+  unsigned m = 0u;
   const int64_t vbeg = (beg + V - 1) / V, vend = end / V;
   for (int64_t i = vbeg + threadIdx.x; i < vend; i += blockDim.x) {
     Pack<T, V> v = ld_pack<T, V>(x + i * V);
 #pragma unroll
-    for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f32(v.v[j])));
+    for (int j = 0; j < V; ++j) m = max(m, abs_key(to_f32(v.v[j])));
   }
   for (int64_t i = beg + threadIdx.x; i < min(end, vbeg * V); i += blockDim.x)
-    m = fmaxf(m, fabsf(to_f32(x[i])));  // head before the first full vector
+    m = max(m, abs_key(to_f32(x[i])));  // head before the first full vector
   for (int64_t i = max(vend * V, beg) + threadIdx.x; i < end; i += blockDim.x)
-    m = fmaxf(m, fabsf(to_f32(x[i])));  // tail after the last full vector
-  m = warp_max(m, 32);
-  __shared__ float red[kThreads / 32];
+    m = max(m, abs_key(to_f32(x[i])));  // tail after the last full vector
+  m = warp_max_key(m, 32);
+  __shared__ unsigned red[kThreads / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float b = 0.f;
-    for (int w = 0; w < kThreads / 32; ++w) b = fmaxf(b, red[w]);
-    partial[blockIdx.x] = __float_as_uint(b);
+    unsigned b = 0u;
+    for (int w = 0; w < kThreads / 32; ++w) b = max(b, red[w]);
+    partial[blockIdx.x] = b;
   }
 }
 
 // One CTA folds the nparts partial maxima into *out.
 __global__ void __launch_bounds__(1024) k_absmax_final(const unsigned* __restrict__ partial,
                                                       int nparts, unsigned* __restrict__ out) {
-  float m = 0.f;
-  for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = fmaxf(m, __uint_as_float(partial[i]));
-  m = warp_max(m, 32);
-  __shared__ float red[32];
+  unsigned m = 0u;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = max(m, partial[i]);
+  m = warp_max_key(m, 32);
+  __shared__ unsigned red[32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float b = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = fmaxf(b, red[w]);
-    *out = __float_as_uint(b);
+    unsigned b = 0u;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = max(b, red[w]);
+    *out = b;
   }
 }
 
