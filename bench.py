@@ -722,27 +722,34 @@ class Decode:
         import tileops_b200 as tob
         from tileops_b200 import sharded
 
-        self.tob, self.sharded, self.world, self.dev, self.m = tob, sharded, world, dev, m
-        g = torch.Generator().manual_seed(1234 + 5 + 100 * rank)
+        self.tob, self.sharded, self.world, self.dev = tob, sharded, world, dev
+        # 3.6 GB of weights: drawn on the device from a seeded generator
+        g = torch.Generator(device=dev).manual_seed(1234 + 5 + 100 * rank)
         self.layers = []
         for _ in range(self.LAYERS):
             lins = []
             for (k, n) in self.SHAPES:
                 nl = n // world
-                qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k, nl // 8), generator=g, dtype=torch.int32)
+                qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k, nl // 8), generator=g,
+                                   dtype=torch.int32, device=dev)
                 qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k // self.G, nl // 8), generator=g,
-                                   dtype=torch.int32)
-                s = (torch.rand(k // self.G, nl, generator=g) * 0.018 + 0.002).half()
-                lins.append((qw.to(dev), s.to(dev), qz.to(dev)))
+                                   dtype=torch.int32, device=dev)
+                s = (torch.rand(k // self.G, nl, generator=g, device=dev) * 0.018 + 0.002).half()
+                lins.append((qw, s, qz))
             self.layers.append(lins)
-        gx = torch.Generator().manual_seed(1234 + 5)
-        x_cpu = torch.randn(m, 4096, generator=gx).half()
-        self.x = x_cpu.to(dev)
-        self.x_host = x_cpu.pin_memory()
-        self.out_host = torch.empty(m, 4096, dtype=torch.float16).pin_memory()
         self.weight_bytes = self.LAYERS * sum(
             k * n // 2 + (k // self.G) * n * 2 + (k // self.G) * n // 2 for k, n in self.SHAPES)
+        self.set_m(m)
         tob.set_launch_overlap(True)  # layer i+1 streams its weights while layer i finishes
+
+    def set_m(self, m):
+        """Switches the batch to m tokens (the same weights)."""
+        self.m = m
+        gx = torch.Generator().manual_seed(1234 + 5)
+        x_cpu = torch.randn(m, 4096, generator=gx).half()
+        self.x = x_cpu.to(self.dev)
+        self.x_host = x_cpu.pin_memory()
+        self.out_host = torch.empty(m, 4096, dtype=torch.float16).pin_memory()
 
     def _run(self, x):
         gather = self.sharded.gather_columns if self.world > 1 else (lambda y: y)
@@ -785,19 +792,19 @@ class Decode:
                 "launch_overlap": "programmatic dependent launch between consecutive layers"}
 
     @classmethod
-    def cpu_reference(cls, threads):
+    def cpu_reference(cls, threads, m=16):
         from oracle import awq as oawq
 
         torch.set_num_threads(threads)
-        k, n, G = 4096, 4096, cls.G  # one o-projection linear per pass, M=16
+        k, n, G = 4096, 4096, cls.G  # one o-projection linear per pass
         g = torch.Generator().manual_seed(1234 + 5)
-        x = torch.randn(16, k, generator=g).half()
+        x = torch.randn(m, k, generator=g).half()
         qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (k, n // 8), generator=g, dtype=torch.int32)
         qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (k // G, n // 8), generator=g, dtype=torch.int32)
         s = (torch.rand(k // G, n, generator=g) * 0.018 + 0.002).half()
         byts = k * n // 2 + (k // G) * n * 2 + (k // G) * n // 2
         run = lambda: oawq.gemm_reference_cpu_torch(x, qw, s, qz, G)  # noqa: E731
-        return run, byts / 1e9, ("one 4096x4096 linear (M=16) of the 128 per step per pass; "
+        return run, byts / 1e9, (f"one 4096x4096 linear (M={m}) of the 128 per step per pass; "
                                  "torch CPU reference algorithm")
 
 
@@ -805,9 +812,9 @@ WORKLOADS = {c.name: c for c in (Int8Layer, AwqPrefill, Fp8Layer, Fp8BlockGemm, 
                                   AwqGemv, DenseGemv, Decode)}
 
 
-def time_cpu(workload_cls, reps: int):
+def time_cpu(workload_cls, reps: int, **kw):
     threads = os.cpu_count() or 1
-    run, units, sample = workload_cls.cpu_reference(threads)
+    run, units, sample = workload_cls.cpu_reference(threads, **kw)
     run()  # warm-up
     times = []
     for _ in range(reps):
@@ -826,6 +833,21 @@ def arm_config(wl_cls, world: int, decode_m: int) -> dict:
     probe.m = decode_m
     probe.gather = os.environ.get("TOB_BENCH_GATHER", "fused")
     return probe.config(world)
+
+
+# The other configurations of the scope, measured in the default run after the headline one
+# and reported under "workloads": (key, workload, decode M).
+SUB_WORKLOADS = [("awq_gemv", "awq_gemv", None), ("fp8", "fp8", None),
+                 ("awq_prefill", "awq_prefill", None), ("decode_m1", "decode", 1),
+                 ("decode_m4", "decode", 4), ("decode_m16", "decode", 16),
+                 ("decode_m64", "decode", 64)]
+
+
+def cpu_line(wl_cls, reps: int, decode_m: int | None = None) -> dict:
+    kw = {"m": decode_m} if wl_cls is Decode and decode_m is not None else {}
+    v, t, cores, sample = time_cpu(wl_cls, reps, **kw)
+    return {"value": v, "unit": wl_cls.unit, "cores": cores, "kind": "port",
+            "sample": f"{sample}; median {t:.3f} s per pass"}
 
 
 def run_reference_arm(args, rank: int, wl) -> None:
@@ -849,7 +871,98 @@ def run_reference_arm(args, rank: int, wl) -> None:
                          "sample": f"{sample}; median {statistics.median(secs):.3f} s per pass"},
         "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.workload == "int8" and not args.single:
+        subs = {}
+        for key, name, m in SUB_WORKLOADS:
+            sub_cls = WORKLOADS[name]
+            cb = cpu_line(sub_cls, 1, m)
+            subs[key] = {"value": cb["value"], "unit": sub_cls.unit,
+                         "config": arm_config(sub_cls, args.gpus, m or args.decode_m),
+                         "cpu_baseline": cb}
+        line["workloads"] = subs
     print(json.dumps(line), flush=True)
+
+
+def measure(wl, wl_cls, args, dist, dev, rank, world, local, steps, cpu_reps=3,
+            decode_m=None) -> dict | None:
+    """Times one workload: device throughput (graph replay), its dominant kernel (roofline) and
+    the end-to-end path through the public API. Returns rank 0's line fields."""
+    from tileops_b200 import _lib
+
+    wl.step(0)  # first call: tensor maps, kernel attributes, NCCL communicator
+    torch.cuda.synchronize()
+
+    # ---------------- device throughput: K steps from one CUDA graph, inputs resident
+    ms_step, clocks = timed_graph_ms(wl.step, steps, args.warmup, dist, clock_index=local)
+    value = wl.total_units(world) / (ms_step * 1e-3)
+
+    # ---------------- the dominant kernel alone (roofline)
+    k_ms, _ = timed_graph_ms(wl.kernel_step, min(steps, 60), args.warmup, dist)
+
+    # ---------------- end to end through the public API with host buffers
+    for i in range(args.warmup):
+        wl.e2e_step(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        wl.e2e_step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e_value = wl.total_units(world) / (e_ms / steps * 1e-3)
+    assert _lib.device_error_word() == 0
+    if rank != 0:
+        return None
+
+    peaks, peak_kind = measured_peaks()
+    bound, per_launch = wl.roofline_units()
+    if bound == "hbm":
+        achieved = per_launch / (k_ms * 1e-3) / 1e9
+        peak, unit, peak_note = float(peaks["hbm_gbs"]), "GB/s", peak_kind
+    else:
+        achieved = per_launch / (k_ms * 1e-3) / 1e12
+        unit = "TFLOP/s"
+        peak = float(peaks["bf16_tflops"])
+        peak_note = peak_kind + " bf16 burst"
+        if wl.name in ("fp8", "fp8_block"):  # dense e4m3 runs at twice the bf16 rate
+            peak, peak_note = 2 * peak, peak_kind + " bf16 burst x2 (e4m3)"
+    h2d, d2h = wl.h2d_d2h()
+    line = {
+        "value": value, "unit": wl.unit, "ms_per_step": ms_step, "scaling": wl.scaling,
+        "dtype": wl.dtype, "data": wl.data, "config": wl.config(world),
+        "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "traffic": profile_traffic(wl.profile),
+                     "peak_source": peak_note, "kernel_ms": k_ms,
+                     "algorithmic_per_launch": per_launch},
+        "cpu_baseline": cpu_line(wl_cls, cpu_reps, decode_m),
+        "gpu_launches": steps * wl.launches_per_step,
+        "clocks": clocks,
+    }
+    if hasattr(wl, "extra"):
+        line.update(wl.extra(ms_step))
+    return line
+
+
+def make_workload(wl_cls, dev, rank, world, decode_m):
+    return wl_cls(dev, rank, world, decode_m) if wl_cls is Decode else wl_cls(dev, rank, world)
+
+
+def release(wl, dist) -> None:
+    if hasattr(wl, "close"):
+        wl.close()  # collective: releases buffers mapped into the peers
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
 
 
 def main() -> int:
@@ -860,6 +973,8 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="int8", choices=sorted(WORKLOADS))
     ap.add_argument("--decode-m", type=int, default=16)
+    ap.add_argument("--single", action="store_true",
+                    help="measure only --workload (no 'workloads' entries for the other configs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl_cls = WORKLOADS[args.workload]
@@ -871,8 +986,6 @@ def main() -> int:
         run_reference_arm(args, rank, wl_cls)
         return 0
 
-    from tileops_b200 import _lib
-
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
@@ -883,73 +996,43 @@ def main() -> int:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    wl = wl_cls(dev, rank, world, args.decode_m) if wl_cls is Decode else wl_cls(dev, rank, world)
-    wl.step(0)  # first call: tensor maps, kernel attributes, NCCL communicator
-    torch.cuda.synchronize()
+    wl = make_workload(wl_cls, dev, rank, world, args.decode_m)
+    head = measure(wl, wl_cls, args, dist, dev, rank, world, local, args.steps,
+                   decode_m=args.decode_m if wl_cls is Decode else None)
+    release(wl, dist)
+    del wl
 
-    # ---------------- device throughput: K steps from one CUDA graph, inputs resident
-    ms_step, clocks = timed_graph_ms(wl.step, args.steps, args.warmup, dist, clock_index=local)
-    value = wl.total_units(world) / (ms_step * 1e-3)
-
-    # ---------------- the dominant kernel alone (roofline)
-    k_ms, _ = timed_graph_ms(wl.kernel_step, min(args.steps, 60), args.warmup, dist)
-
-    # ---------------- end to end through the public API with host buffers
-    for i in range(args.warmup):
-        wl.e2e_step(i)
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        wl.e2e_step(i)
-    e1.record()
-    torch.cuda.synchronize()
-    e_ms = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_ms = float(t.item())
-    e2e_value = wl.total_units(world) / (e_ms / args.steps * 1e-3)
-    assert _lib.device_error_word() == 0
+    subs = {}
+    if args.workload == "int8" and not args.single:
+        decode = None
+        for key, name, m in SUB_WORKLOADS:
+            sub_cls = WORKLOADS[name]
+            if sub_cls is Decode:
+                if decode is None:
+                    decode = make_workload(sub_cls, dev, rank, world, m)
+                decode.set_m(m)
+                sub = decode
+            else:
+                sub = make_workload(sub_cls, dev, rank, world, None)
+            r = measure(sub, sub_cls, args, dist, dev, rank, world, local, args.steps, cpu_reps=2,
+                        decode_m=m)
+            if r is not None:
+                subs[key] = r
+            if sub is not decode:
+                release(sub, dist)
+            del sub
+        if decode is not None:
+            release(decode, dist)
+            del decode
 
     if rank == 0:
-        peaks, peak_kind = measured_peaks()
-        bound, per_launch = wl.roofline_units()
-        if bound == "hbm":
-            achieved = per_launch / (k_ms * 1e-3) / 1e9
-            peak, unit, peak_note = float(peaks["hbm_gbs"]), "GB/s", peak_kind
-        else:
-            achieved = per_launch / (k_ms * 1e-3) / 1e12
-            unit = "TFLOP/s"
-            peak = float(peaks["bf16_tflops"])
-            peak_note = peak_kind + " bf16 burst"
-            if wl.name in ("fp8", "fp8_block"):  # dense e4m3 runs at twice the bf16 rate
-                peak, peak_note = 2 * peak, peak_kind + " bf16 burst x2 (e4m3)"
-        cpu_v, cpu_t, cores, sample = time_cpu(wl_cls, 3)
-        h2d, d2h = wl.h2d_d2h()
-        line = {
-            "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
-            "dtype": wl.dtype, "data": wl.data, "config": wl.config(world),
-            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                         "frac": achieved / peak, "traffic": profile_traffic(wl.profile),
-                         "peak_source": peak_note, "kernel_ms": k_ms,
-                         "algorithmic_per_launch": per_launch},
-            "cpu_baseline": {"value": cpu_v, "unit": wl.unit, "cores": cores, "kind": "port",
-                             "sample": f"{sample}; median {cpu_t:.3f} s per pass"},
-            "gpu_launches": args.steps * wl.launches_per_step,
-            "clocks": clocks,
-        }
-        if hasattr(wl, "extra"):
-            line.update(wl.extra(ms_step))
+        line = {"metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+                "higher_is_better": True, "scaling": head["scaling"], "vs_baseline": None}
+        line.update({k: v for k, v in head.items() if k not in line})
+        if subs:
+            line["workloads"] = subs
         print(json.dumps(line), flush=True)
-    if hasattr(wl, "close"):
-        wl.close()  # collective: releases buffers mapped into the peers
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -61,3 +61,20 @@ def test_every_workload_has_a_config_and_units(name):
     assert wl.unit in ("GB/s", "TFLOP/s", "TOPS")
     assert wl.bound in ("hbm", "tensor") and wl.scaling in ("weak", "strong")
     assert wl.launches_per_step >= 1
+
+
+def test_reference_arm_reports_every_config():
+    """The default reference arm also times the CPU restatement of the other configurations, so
+    each GPU `workloads` entry has its CPU counterpart."""
+    p = _run({}, "--impl", "reference", "--steps", "1", "--warmup", "3")
+    assert p.returncode == 0, p.stderr
+    line = json.loads([ln for ln in p.stdout.splitlines() if ln.startswith("{")][0])
+    subs = line["workloads"]
+    assert set(subs) == {key for key, _, _ in bench.SUB_WORKLOADS}
+    for key, name, m in bench.SUB_WORKLOADS:
+        wl = bench.WORKLOADS[name]
+        e = subs[key]
+        assert e["value"] > 0 and e["unit"] == wl.unit
+        assert e["cpu_baseline"]["kind"] == "port" and e["cpu_baseline"]["cores"] >= 1
+        if m is not None:
+            assert e["config"]["M"] == m
