@@ -167,10 +167,17 @@ __device__ __forceinline__ float ue8m0_round(float s) {
 // NaN operand that comes first -- x itself when x is NaN, else the scale's sign-clear NaN --
 // and the cast keeps its sign (0x7F or 0xFF); with a numeric scale the NaN comes from an
 // invalid operation (inf / inf, 0 / 0), whose default NaN has the sign set (0xFF).
-__device__ __forceinline__ uint8_t nan_code_div(float x, bool nan_scale) {
+// `neg_x` is the sign bit of x as stored: the conversion of a 16-bit NaN to fp32 does not
+// keep its sign on the GPU.
+__device__ __forceinline__ uint8_t nan_code_div(float x, bool neg_x, bool nan_scale) {
   if (!nan_scale) return 0xFF;
-  return (isnan(x) && (__float_as_uint(x) >> 31)) ? (uint8_t)0xFF : (uint8_t)0x7F;
+  return (isnan(x) && neg_x) ? (uint8_t)0xFF : (uint8_t)0x7F;
 }
+
+// Sign bit of a stored value.
+__device__ __forceinline__ bool sign_of(float v) { return __float_as_uint(v) >> 31; }
+__device__ __forceinline__ bool sign_of(__half v) { return __half_as_ushort(v) >> 15; }
+__device__ __forceinline__ bool sign_of(__nv_bfloat16 v) { return __bfloat16_as_ushort(v) >> 15; }
 
 template <typename T, bool FP8, int V, int MAXV>
 __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
@@ -235,7 +242,8 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
         const float xv = to_f32(t.v[j]);
         const float y = __fdiv_rn(xv, scale);
         if (FP8) {
-          o.v[j] = isnan(y) ? nan_code_div(xv, nan_group) : f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
+          o.v[j] = isnan(y) ? nan_code_div(xv, sign_of(t.v[j]), nan_group)
+                            : f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
         } else {
           o.v[j] = (uint8_t)rne_clamp_i8(y);
         }
