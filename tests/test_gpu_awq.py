@@ -221,3 +221,48 @@ def test_gemv_launch_overlap_chain(cuda):
     for qw, s, qz in layers:
         want = oawq.gemm(want, qw.cpu().numpy(), s.float().cpu().numpy(), qz.cpu().numpy(), "f16")
     np.testing.assert_allclose(ref.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("m,k,n,g", [
+    # stream-K decode kernel (1 <= M <= 32): column tiles of 256 split over K across CTAs
+    (2, 4096, 28672, 128),    # two tokens on a wide layer (112 tiles x 16 K units)
+    (3, 4096, 4096, 128),     # 16 tiles x 16 K units over 128 CTAs: 8 CTAs per tile
+    (7, 4096, 6144, 64),      # scaled every 64 rows
+    (16, 14336, 4096, 128),   # the down projection: 56 K units per tile
+    (31, 4096, 28672, 32),    # four token tiles, scaled every 32 rows
+    (12, 4096, 1056, 4096),   # G == K; a partial last column tile (1056 = 4 x 256 + 32)
+    (2, 320, 256, 64),        # K % 256 != 0: the last K unit is partly outside the tensor
+    (32, 1024, 512, 128),     # a tile split over several CTAs, each holding two units
+])
+def test_decode_kernel_vs_oracle(cuda, dtype, m, k, n, g):
+    gen = torch.Generator().manual_seed(m * 11 + k + 5 * n + g)
+    qw, s, qz = make_awq(k, n, g, _DT[dtype], gen)
+    x = torch.randn(m, k, generator=gen).to(_DT[dtype])
+    args = (x.to(cuda), qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    y = tob.awq_gemm(*args)
+    want = oawq.gemm(x.float().numpy(), qw.numpy(), s.float().numpy(), qz.numpy(), dtype)
+    np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+    assert torch.equal(tob.awq_gemm(*args), y)  # the partial sums are added in a fixed order
+
+
+def test_decode_kernel_graph_replays_with_new_inputs(cuda):
+    """One decode call captured in a CUDA graph and replayed with fresh activations: the
+    per-launch flags of the cross-CTA partial sums are consumed and reset on every replay."""
+    gen = torch.Generator().manual_seed(33)
+    qw, s, qz = (t.to(cuda) for t in make_awq(4096, 4096, 128, torch.float16, gen))
+    x = torch.zeros(16, 4096, dtype=torch.float16, device=cuda)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        tob.awq_gemm(x, qw, s, qz, 1)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = tob.awq_gemm(x, qw, s, qz, 1)
+    for i in range(4):
+        x.copy_(torch.randn(16, 4096, generator=gen).half())
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, tob.awq_gemm(x, qw, s, qz, 1)), i
+    del graph

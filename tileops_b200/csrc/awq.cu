@@ -648,6 +648,20 @@ int awq_gemm_tc_gather_launch(const void* x, const int32_t* qw, const void* s, i
 int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                        const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
                        cudaStream_t st);
+size_t awq_decode_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dtype);
+bool awq_decode_wanted(int64_t M, int64_t K, int64_t N);
+int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                      const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
+                      void* ws, size_t ws_bytes, cudaStream_t st);
+
+// Measurement switch: TOB_AWQ_DECODE=0 keeps decode-sized M off the stream-K decode kernel.
+bool decode_enabled() {
+  static const bool on = [] {
+    const char* v = tuning_env("TOB_AWQ_DECODE");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
 
 // Used by the tensor-core GEMM translation unit when it must stream small M.
 int awq_gemv_dispatch(const void* x, const int32_t* qw, const void* s, int s_dtype,
@@ -726,22 +740,29 @@ int to_awq_dequant(const int32_t* qweight, const void* scales, int s_dtype, cons
 }
 
 size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_t group_size) {
-  (void)M; (void)K; (void)N; (void)group_size;
-  return 0;
+  if (M <= 0 || K <= 0 || N <= 0 || group_size <= 0 || N % 8 != 0 || K % group_size != 0)
+    return 0;
+  if (!decode_enabled()) return 0;
+  return awq_decode_workspace(M, K, N, group_size, TO_F16);
 }
 
 int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
                 const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
                 int64_t group_size, void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace; (void)workspace_bytes;
   int rc = check_awq_shapes("awq_gemm", K, N, group_size);
   if (rc) return rc;
   if (M <= 0) return fail(TO_EINVAL, "awq_gemm: invalid M=%lld", (long long)M);
   if (!aligned16(scales) || !aligned16(x))
     return fail(TO_EINVAL, "awq_gemm: x and scales must be 16-byte aligned");
-  // Prefill-sized M runs on the tcgen05 GEMM; 3 <= M <= 64 on the TMA-fed register-MMA
-  // kernel (33..64 only when the tcgen05 tiles would leave most SMs idle); M <= 2 and the
-  // shapes neither takes (ragged N, unaligned rows) on the streaming SIMT kernels.
+  // Decode-sized M (1..32) runs on the stream-K decode kernel; prefill-sized M on the tcgen05
+  // GEMM; 33 <= M <= 64 on the TMA-fed register-MMA kernel when the tcgen05 tiles would leave
+  // most SMs idle; the shapes none of them takes (ragged N, unaligned rows) on the streaming
+  // SIMT kernels.
+  if (M <= 32 && decode_enabled() && awq_decode_wanted(M, K, N)) {
+    rc = awq_decode_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size,
+                           workspace, workspace_bytes, (cudaStream_t)stream);
+    if (rc != TO_EUNSUPPORTED) return rc;
+  }
   if (M > small_m_max() || tc_for_mid_m(M, N)) {
     const int rc = awq_gemm_tc_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N,
                                       group_size, (cudaStream_t)stream);

@@ -28,6 +28,10 @@ template <> struct Half2Of<__half> {
   }
   static __device__ __forceinline__ __half2 sixteenth() { return __float2half2_rn(0.0625f); }
   static __device__ __forceinline__ float magic_f() { return 1024.f; }
+  static __device__ __forceinline__ float2 to_float2(__half2 v) { return __half22float2(v); }
+  static __device__ __forceinline__ __half2 from_floats(float a, float b) {
+    return __floats2half2_rn(a, b);
+  }
 };
 template <> struct Half2Of<__nv_bfloat16> {
   using type = __nv_bfloat162;
@@ -39,6 +43,12 @@ template <> struct Half2Of<__nv_bfloat16> {
     return __float2bfloat162_rn(0.0625f);
   }
   static __device__ __forceinline__ float magic_f() { return 128.f; }
+  static __device__ __forceinline__ float2 to_float2(__nv_bfloat162 v) {
+    return __bfloat1622float2(v);
+  }
+  static __device__ __forceinline__ __nv_bfloat162 from_floats(float a, float b) {
+    return __floats2bfloat162_rn(a, b);
+  }
 };
 
 // Exact (w - z) for the four column pairs of one word: d[i] holds columns (2i, 2i+1).
