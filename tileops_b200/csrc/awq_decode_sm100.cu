@@ -808,20 +808,20 @@ int dispatch_decode(const void* x, const int32_t* qw, const void* s, const int32
 }  // namespace
 }  // namespace sm100
 
-// Workspace bytes the decode kernel needs for these shapes (0 when it does not take them).
-size_t awq_decode_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dtype) {
-  if (!sm100::dec_supported(M, K, N, G, s_dtype) || !awq_decode_wanted(M, K, N)) return 0;
-  if (M <= 8) return sm100::dec_ws<1>(M, K, N, G);
-  if (M <= 16) return sm100::dec_ws<2>(M, K, N, G);
-  return sm100::dec_ws<4>(M, K, N, G);
-}
-
 // Whether the decode kernel is the faster choice: for 1-2 tokens the streaming GEMV (K split
 // over a thread-block cluster, no global partial sums) wins on layers of fewer than 1024 units
 // (4096 x 28672 runs 21 us here against 29 us there; 4096 x 4096 9 us against 6 us).
 bool awq_decode_wanted(int64_t M, int64_t K, int64_t N) {
   if (M > 2) return true;
   return ceil_div(N / 8, sm100::kDecWords) * ceil_div(K, 256) >= 1024;
+}
+
+// Workspace bytes the decode kernel needs for these shapes (0 when it does not take them).
+size_t awq_decode_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dtype) {
+  if (!sm100::dec_supported(M, K, N, G, s_dtype) || !awq_decode_wanted(M, K, N)) return 0;
+  if (M <= 8) return sm100::dec_ws<1>(M, K, N, G);
+  if (M <= 16) return sm100::dec_ws<2>(M, K, N, G);
+  return sm100::dec_ws<4>(M, K, N, G);
 }
 
 // Routes 1 <= M <= 32 to the decode kernel; TO_EUNSUPPORTED (nothing launched, no error
