@@ -723,6 +723,9 @@ class Decode:
         from tileops_b200 import sharded
 
         self.tob, self.sharded, self.world, self.dev = tob, sharded, world, dev
+        self.bufs = None
+        if world > 1:
+            self.launches_per_step = 160 + 128  # and a gather step after each linear
         # 3.6 GB of weights: drawn on the device from a seeded generator
         g = torch.Generator(device=dev).manual_seed(1234 + 5 + 100 * rank)
         self.layers = []
@@ -744,22 +747,44 @@ class Decode:
 
     def set_m(self, m):
         """Switches the batch to m tokens (the same weights)."""
+        self.close()
         self.m = m
+        self.bufs = None
+        if self.world > 1 and m > 2:
+            # one set of two peer-mapped [m, N] outputs per linear of the layer, shared by the
+            # 32 layers (each set alternates its two buffers)
+            self.bufs = [self.sharded.PeerBuffers(m, n, torch.float16) for _, n in self.SHAPES]
         gx = torch.Generator().manual_seed(1234 + 5)
         x_cpu = torch.randn(m, 4096, generator=gx).half()
         self.x = x_cpu.to(self.dev)
         self.x_host = x_cpu.pin_memory()
         self.out_host = torch.empty(m, 4096, dtype=torch.float16).pin_memory()
 
+    def _linear(self, x, w, j):
+        if self.world == 1:
+            return self.tob.awq_gemm(x, *w, 1)
+        if self.m > 2:
+            # this rank's column slice, all-gathered inside the kernel (peer stores over NVLink
+            # and a GPU rank barrier)
+            y = self.sharded.gathered_gemm(x, *w, self.bufs[j])
+            if y is not None:
+                return y
+        # 1-2 tokens: the streaming GEMV on the slice, then an NCCL all-gather
+        return self.sharded.gather_columns(self.tob.awq_gemm(x, *w, 1))
+
     def _run(self, x):
-        gather = self.sharded.gather_columns if self.world > 1 else (lambda y: y)
         for qkv, o, gu, down in self.layers:
-            h = gather(self.tob.awq_gemm(x, *qkv, 1))
-            a = gather(self.tob.awq_gemm(h[:, :4096].contiguous(), *o, 1))
-            u = gather(self.tob.awq_gemm(a, *gu, 1))
+            h = self._linear(x, qkv, 0)
+            a = self._linear(h[:, :4096].contiguous(), o, 1)
+            u = self._linear(a, gu, 2)
             act = self.tob.silu_and_mul(u[:, :14336], u[:, 14336:])  # gate, up read in place
-            x = gather(self.tob.awq_gemm(act, *down, 1))
+            x = self._linear(act, down, 3)
         return x
+
+    def close(self):
+        for b in getattr(self, "bufs", None) or []:
+            b.close()  # collective
+        self.bufs = None
 
     def step(self, i):
         self._run(self.x)
@@ -785,8 +810,8 @@ class Decode:
 
     def config(self, world):
         return {"workload": f"awq decode step, 32 layers x 4 linears (8B-class), M={self.m} fp16, "
-                            "group 128, silu_and_mul between gate_up and down, N-sharded + "
-                            "all-gather per linear",
+                            "group 128, silu_and_mul between gate_up and down, N-sharded, each "
+                            "linear all-gathered (inside its kernel from 3 tokens, NCCL below)",
                 "M": self.m, "layers": self.LAYERS, "parallelism": f"tp{world} (N-sharded)",
                 "l2": "3.6 GB of weights per step > L2",
                 "launch_overlap": "programmatic dependent launch between consecutive layers"}
@@ -1034,6 +1059,9 @@ def main() -> int:
             line["workloads"] = subs
         print(json.dumps(line), flush=True)
     if dist is not None:
+        from tileops_b200 import sharded
+
+        sharded.close_peer_barriers()  # collective
         dist.barrier()
         dist.destroy_process_group()
     return 0

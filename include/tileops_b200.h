@@ -168,8 +168,12 @@ TO_API int to_awq_dequant(const int32_t* qweight, const void* scales, int s_dtyp
                    const int32_t* qzeros, void* out, int64_t K, int64_t N, int64_t group_size,
                    void* stream);
 /* replaces quant_awq.py:112 awq_gemm_triton: y [M,N] = x [M,K] @ dequant(W), x and y in
- * s_dtype (the facade casts x first, as the reference does), fp32 accumulation. Small M
- * runs the streaming GEMV; larger M the tcgen05 tensor-core GEMM. */
+ * s_dtype (the facade casts x first, as the reference does), fp32 accumulation. 1-32 tokens
+ * run the stream-K decode kernel (1-2 tokens on small layers the streaming GEMV), larger M the
+ * tcgen05 tensor-core GEMM. The decode kernel needs a workspace of
+ * to_awq_gemm_workspace_size(M, K, N, group_size) bytes (16-byte aligned; 0 when no kernel
+ * for these shapes needs one) for the partial sums of column tiles split over SMs; calls that
+ * share a workspace must not overlap on the GPU. */
 TO_API size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_t group_size);
 TO_API int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
                 const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
@@ -177,17 +181,30 @@ TO_API int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales
 /* Library extension for N-sharded layers (no reference counterpart; it fuses to_awq_gemm on a
  * rank's column slice with the all-gather that follows it). The group's `world` ranks each
  * hold N = N_full / world output columns of qweight/scales/qzeros; this rank computes its
- * [M, N] slice on the tensor-core kernel and stores it straight into the [M, N * world]
- * output of every rank, y_ranks[r] (host array of device pointers valid on this device: its
- * own buffer and the peers' buffers mapped with to_ipc_open), at columns
- * [rank * N, (rank + 1) * N). The stores have completed when the kernel has; the caller
- * orders the peers' reads after every rank's kernel (one collective barrier) and must not
- * reuse a buffer a peer may still read. TO_EUNSUPPORTED (nothing launched) for shapes outside
- * the tensor-core kernel: run to_awq_gemm and an all-gather instead. */
+ * [M, N] slice (1-32 tokens on the decode kernel, more on the tensor-core kernel) and stores
+ * it straight into the [M, N * world] output of every rank, y_ranks[r] (host array of device
+ * pointers valid on this device: its own buffer and the peers' buffers mapped with
+ * to_ipc_open), at columns [rank * N, (rank + 1) * N). Workspace as for to_awq_gemm with the
+ * rank's (M, K, N). The stores have completed when the kernel has; the caller orders the
+ * peers' reads after every rank's kernel (to_peer_barrier) and must not reuse a buffer a peer
+ * may still read. TO_EUNSUPPORTED (nothing launched) for shapes outside both kernels: run
+ * to_awq_gemm and an all-gather instead. */
 TO_API int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales,
                               int s_dtype, const int32_t* qzeros, void* const* y_ranks,
                               int world, int rank, int64_t M, int64_t K, int64_t N,
-                              int64_t group_size, void* stream);
+                              int64_t group_size, void* workspace, size_t workspace_bytes,
+                              void* stream);
+/* Rank barrier on the GPU (no reference counterpart; the completion step of the gathering
+ * GEMMs). Each rank owns a flag array of to_peer_flags_bytes() bytes, zeroed, in memory the
+ * others map with to_ipc_open, and an 8-byte counter in its own device memory, zeroed.
+ * flag_ranks[r] is rank r's array as seen from this process. The kernel raises this rank's
+ * slot in every array to the next count and waits until every rank's slot in its own array
+ * has reached it; work queued after it on `stream` sees every rank's earlier stores. Every
+ * rank runs the same sequence of barriers; a wait that reaches the library's limit records a
+ * timeout in the device error word instead of hanging. */
+TO_API size_t to_peer_flags_bytes(void);
+TO_API int to_peer_barrier(unsigned long long* const* flag_ranks, int world, int rank,
+                           unsigned long long* counter, void* stream);
 
 /* ---- W8A8 block-scaled GEMMs --------------------------------------------------------------
  * C[m,n] = sum_kb  (sum_{k in kb} A[m,k]*B[n,k]) * a_s[m,kb] * b_s[n/block_n, kb]

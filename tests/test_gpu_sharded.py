@@ -1,7 +1,8 @@
-"""The gathering AWQ GEMM of N-sharded layers on two GPUs of one node: each rank's tensor-core
-kernel stores its column slice into every rank's [M, N] output over NVLink (CUDA IPC mappings),
-one NCCL barrier follows. Checked against the unsharded layer on the same GPU and against the
-oracle on sampled columns. Needs two GPUs (skipped on a one-GPU box)."""
+"""The gathering AWQ GEMM of N-sharded layers on two GPUs of one node: each rank's kernel (the
+tensor-core GEMM for 40 and 256 tokens, the decode kernel for 1 and 16) stores its column slice
+into every rank's [M, N] output over NVLink (CUDA IPC mappings), then the GPU rank barrier
+orders the reads. Checked against the unsharded layer on the same GPU and against the oracle on
+sampled columns. Needs two GPUs (skipped on a one-GPU box)."""
 
 from __future__ import annotations
 
@@ -52,7 +53,7 @@ def _worker(rank, world, port, q):
         s = s.to(dev)
         layer = sharded.ShardedAWQLinear(qw, s, qz)
         report = {}
-        for m in (256, 40):
+        for m in (256, 40, 16, 1):
             x = torch.randn(m, k, generator=g).bfloat16().to(dev)
             full = tob.awq_gemm(x, qw, s, qz, 1)
             y1 = layer.gathered(x).clone()
@@ -68,6 +69,7 @@ def _worker(rank, world, port, q):
                 float(np.abs(want).max()),
             )
         layer.close()
+        sharded.close_peer_barriers()
         q.put((rank, "ok", report))
     except Exception:  # noqa: BLE001
         q.put((rank, "error", traceback.format_exc()))

@@ -66,7 +66,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_awq_gemm_workspace_size": (_S, [_L, _L, _L, _L]),
     "to_awq_gemm": (_I, [_P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _P, _S, _P]),
     "to_awq_gemm_gather": (_I, [_P, _P, _P, _I, _P, ctypes.POINTER(_P), _I, _I, _L, _L, _L, _L,
-                                _P]),
+                                _P, _S, _P]),
+    "to_peer_flags_bytes": (_S, []),
+    "to_peer_barrier": (_I, [ctypes.POINTER(_P), _I, _I, _P, _P]),
     "to_ipc_alloc": (_I, [_S, ctypes.POINTER(_P), _P]),
     "to_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
     "to_ipc_close": (_I, [_P]),

@@ -650,6 +650,10 @@ int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dt
                        cudaStream_t st);
 size_t awq_decode_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dtype);
 bool awq_decode_wanted(int64_t M, int64_t K, int64_t N);
+int awq_decode_gather_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                             const int32_t* qz, void* const* y_ranks, int world, int rank,
+                             int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
+                             size_t ws_bytes, cudaStream_t st);
 int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
                       void* ws, size_t ws_bytes, cudaStream_t st);
@@ -783,7 +787,8 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
 
 int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
                        const int32_t* qzeros, void* const* y_ranks, int world, int rank,
-                       int64_t M, int64_t K, int64_t N, int64_t group_size, void* stream) {
+                       int64_t M, int64_t K, int64_t N, int64_t group_size, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   int rc = check_awq_shapes("awq_gemm_gather", K, N, group_size);
   if (rc) return rc;
   if (M <= 0) return fail(TO_EINVAL, "awq_gemm_gather: invalid M=%lld", (long long)M);
@@ -794,11 +799,19 @@ int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales
     if (!y_ranks[r]) return fail(TO_EINVAL, "awq_gemm_gather: null output of rank %d", r);
   if (!aligned16(scales) || !aligned16(x))
     return fail(TO_EINVAL, "awq_gemm_gather: x and scales must be 16-byte aligned");
-  rc = awq_gemm_tc_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M,
-                                 K, N, group_size, (cudaStream_t)stream);
+  // Decode-sized M on the stream-K decode kernel, the rest on the tensor-core GEMM; both store
+  // each finished tile into every rank's output.
+  rc = TO_EUNSUPPORTED;
+  if (M <= 32 && decode_enabled())
+    rc = awq_decode_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M, K,
+                                  N, group_size, workspace, workspace_bytes,
+                                  (cudaStream_t)stream);
+  if (rc == TO_EUNSUPPORTED)
+    rc = awq_gemm_tc_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M,
+                                   K, N, group_size, (cudaStream_t)stream);
   if (rc == TO_EUNSUPPORTED)
     return fail(TO_EUNSUPPORTED,
-                "awq_gemm_gather: shapes outside the tensor-core kernel (N %% 32, K %% 8, group "
+                "awq_gemm_gather: shapes outside the gathering kernels (N %% 32, K %% 8, group "
                 "size, alignment); run the local GEMM and an all-gather instead");
   return rc;
 }

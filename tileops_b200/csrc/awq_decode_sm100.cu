@@ -67,6 +67,14 @@ __host__ __device__ __forceinline__ int64_t dec_cta_of(int64_t u, int64_t units,
   return ((u + 1) * ctas - 1) / units;
 }
 
+// Where the output goes: this GPU's y, or (an N-sharded layer whose all-gather is done here)
+// every rank's [M, ld] output at columns [col0, col0 + N), the peers' mapped into this process.
+constexpr int kDecMaxOut = 8;
+struct DecOut {
+  void* y[kDecMaxOut];
+  int ny, ld, col0;
+};
+
 struct DecPlan {
   int tiles, ku, units, grid, maxc, stages, srows;
   int stage_bytes, x_off, s_off, z_off, tx_bytes, red_bytes;
@@ -233,7 +241,7 @@ template <typename T, int NT, int GR, bool EXACT, int WK>
 __global__ void __launch_bounds__(DecGeom<WK>::kThreads, 1) k_awq_decode(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-    T* __restrict__ y, float* __restrict__ part, unsigned long long* __restrict__ flags,
+    const DecOut out, float* __restrict__ part, unsigned long long* __restrict__ flags,
     int M, int N, int G, int g_log2, int ku, int units, int maxc, int stages, int stage_bytes,
     int x_off, int s_off, int z_off, int tx_bytes, unsigned long long epoch, int* err) {
   using H2 = typename Half2Of<T>::type;
@@ -623,12 +631,13 @@ __global__ void __launch_bounds__(DecGeom<WK>::kThreads, 1) k_awq_decode(
             const int c = col0 + 2 * p;
             const int m = 8 * tt + 2 * q;
             if (c < N) {
-              if (m < M)
-                *reinterpret_cast<H2*>(y + (size_t)m * N + c) =
-                    Half2Of<T>::from_floats(acc[p][tt][0], acc[p][tt][2]);
-              if (m + 1 < M)
-                *reinterpret_cast<H2*>(y + (size_t)(m + 1) * N + c) =
-                    Half2Of<T>::from_floats(acc[p][tt][1], acc[p][tt][3]);
+              const H2 v0 = Half2Of<T>::from_floats(acc[p][tt][0], acc[p][tt][2]);
+              const H2 v1 = Half2Of<T>::from_floats(acc[p][tt][1], acc[p][tt][3]);
+              for (int d = 0; d < out.ny; ++d) {
+                T* yd = static_cast<T*>(out.y[d]) + out.col0 + c;
+                if (m < M) *reinterpret_cast<H2*>(yd + (size_t)m * out.ld) = v0;
+                if (m + 1 < M) *reinterpret_cast<H2*>(yd + (size_t)(m + 1) * out.ld) = v1;
+              }
             }
           }
       }
@@ -642,6 +651,9 @@ __global__ void __launch_bounds__(DecGeom<WK>::kThreads, 1) k_awq_decode(
     ++flushes;
     first_r = cur_r;
   }
+  // Stores into the peers' outputs are performed system-wide before the kernel completes (the
+  // caller's rank barrier then publishes them).
+  if (out.ny > 1) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) {
     // Unwinding: copies issued into a stage nobody consumed must land before the CTA's shared
@@ -666,7 +678,8 @@ std::atomic<unsigned long long>& dec_epoch() {
 }
 
 template <typename T, int NT, int GR, bool EXACT, int WK>
-int launch_decode(const void* x, const int32_t* qw, const void* s, const int32_t* qz, void* y,
+int launch_decode(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
+                  const DecOut& out,
                   int64_t M, int64_t K, int64_t N, int64_t G, void* ws, size_t ws_bytes,
                   cudaStream_t st) {
   DecPlan plan;
@@ -704,7 +717,7 @@ int launch_decode(const void* x, const int32_t* qw, const void* s, const int32_t
   cfg.numAttrs = na;
   const unsigned long long epoch = dec_epoch().fetch_add(1) + 1;
   const int g_log2 = (G & (G - 1)) == 0 ? __builtin_ctzll((unsigned long long)G) : -1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, ts, tz, (T*)y, part, flags, (int)M,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, ts, tz, out, part, flags, (int)M,
                                      (int)N, (int)G, g_log2, plan.ku, plan.units, plan.maxc, plan.stages,
                                      plan.stage_bytes, plan.x_off, plan.s_off, plan.z_off,
                                      plan.tx_bytes, epoch, device_error_ptr());
@@ -770,39 +783,40 @@ inline bool dec_exact(bool f16) {
 
 template <typename T, int NT, bool EXACT, int WK>
 int dispatch_decode_gr(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
-                       void* y, int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
+                       const DecOut& out, int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
                        size_t ws_bytes, cudaStream_t st) {
   switch (dec_group_rows(G)) {
     case 128:
-      return launch_decode<T, NT, 128, EXACT, WK>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st);
+      return launch_decode<T, NT, 128, EXACT, WK>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st);
     case 64:
-      return launch_decode<T, NT, 64, EXACT, WK>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st);
+      return launch_decode<T, NT, 64, EXACT, WK>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st);
     case 32:
-      return launch_decode<T, NT, 32, EXACT, WK>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st);
+      return launch_decode<T, NT, 32, EXACT, WK>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st);
   }
   return TO_EUNSUPPORTED;
 }
 
 template <typename T, int NT, bool EXACT>
 int dispatch_decode_wk(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
-                       void* y, int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
+                       const DecOut& out, int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
                        size_t ws_bytes, cudaStream_t st) {
   if constexpr (NT <= 2) {
     if (dec_wk<NT>() == 4)
-      return dispatch_decode_gr<T, NT, EXACT, 4>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st);
+      return dispatch_decode_gr<T, NT, EXACT, 4>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st);
   }
-  return dispatch_decode_gr<T, NT, EXACT, 2>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st);
+  return dispatch_decode_gr<T, NT, EXACT, 2>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st);
 }
 
 template <typename T, int NT>
-int dispatch_decode(const void* x, const int32_t* qw, const void* s, const int32_t* qz, void* y,
+int dispatch_decode(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
+                    const DecOut& out,
                     int64_t M, int64_t K, int64_t N, int64_t G, void* ws, size_t ws_bytes,
                     cudaStream_t st) {
   if constexpr (std::is_same<T, __half>::value) {
     if (!dec_exact(true))
-      return dispatch_decode_wk<T, NT, false>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st);
+      return dispatch_decode_wk<T, NT, false>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st);
   }
-  return dispatch_decode_wk<T, NT, true>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st);
+  return dispatch_decode_wk<T, NT, true>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st);
 }
 
 }  // namespace
@@ -818,7 +832,7 @@ bool awq_decode_wanted(int64_t M, int64_t K, int64_t N) {
 
 // Workspace bytes the decode kernel needs for these shapes (0 when it does not take them).
 size_t awq_decode_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dtype) {
-  if (!sm100::dec_supported(M, K, N, G, s_dtype) || !awq_decode_wanted(M, K, N)) return 0;
+  if (!sm100::dec_supported(M, K, N, G, s_dtype)) return 0;
   if (M <= 8) return sm100::dec_ws<1>(M, K, N, G);
   if (M <= 16) return sm100::dec_ws<2>(M, K, N, G);
   return sm100::dec_ws<4>(M, K, N, G);
@@ -826,6 +840,25 @@ size_t awq_decode_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dt
 
 // Routes 1 <= M <= 32 to the decode kernel; TO_EUNSUPPORTED (nothing launched, no error
 // recorded) for shapes it does not take.
+namespace {
+int decode_dispatch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                    const int32_t* qz, const sm100::DecOut& out, int64_t M, int64_t K, int64_t N,
+                    int64_t G, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const bool f16 = s_dtype == TO_F16;
+  if (M <= 8)
+    return f16 ? sm100::dispatch_decode<__half, 1>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st)
+               : sm100::dispatch_decode<__nv_bfloat16, 1>(x, qw, s, qz, out, M, K, N, G, ws,
+                                                          ws_bytes, st);
+  if (M <= 16)
+    return f16 ? sm100::dispatch_decode<__half, 2>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st)
+               : sm100::dispatch_decode<__nv_bfloat16, 2>(x, qw, s, qz, out, M, K, N, G, ws,
+                                                          ws_bytes, st);
+  return f16 ? sm100::dispatch_decode<__half, 4>(x, qw, s, qz, out, M, K, N, G, ws, ws_bytes, st)
+             : sm100::dispatch_decode<__nv_bfloat16, 4>(x, qw, s, qz, out, M, K, N, G, ws,
+                                                        ws_bytes, st);
+}
+}  // namespace
+
 int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
                       void* ws, size_t ws_bytes, cudaStream_t st) {
@@ -833,18 +866,33 @@ int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dty
   if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz) || !aligned16(y))
     return TO_EUNSUPPORTED;
   if (ws != nullptr && !aligned16(ws)) return TO_EUNSUPPORTED;
-  const bool f16 = s_dtype == TO_F16;
-  if (M <= 8)
-    return f16 ? sm100::dispatch_decode<__half, 1>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st)
-               : sm100::dispatch_decode<__nv_bfloat16, 1>(x, qw, s, qz, y, M, K, N, G, ws,
-                                                          ws_bytes, st);
-  if (M <= 16)
-    return f16 ? sm100::dispatch_decode<__half, 2>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st)
-               : sm100::dispatch_decode<__nv_bfloat16, 2>(x, qw, s, qz, y, M, K, N, G, ws,
-                                                          ws_bytes, st);
-  return f16 ? sm100::dispatch_decode<__half, 4>(x, qw, s, qz, y, M, K, N, G, ws, ws_bytes, st)
-             : sm100::dispatch_decode<__nv_bfloat16, 4>(x, qw, s, qz, y, M, K, N, G, ws,
-                                                        ws_bytes, st);
+  sm100::DecOut out = {};
+  out.y[0] = y;
+  out.ny = 1;
+  out.ld = (int)N;
+  out.col0 = 0;
+  return decode_dispatch(x, qw, s, s_dtype, qz, out, M, K, N, G, ws, ws_bytes, st);
+}
+
+// The gathering form: this rank's [M, N] slice goes into the [M, N x world] output of every
+// rank (y_ranks[r], the peers' mapped into this process) at columns [rank N, (rank + 1) N).
+int awq_decode_gather_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                             const int32_t* qz, void* const* y_ranks, int world, int rank,
+                             int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
+                             size_t ws_bytes, cudaStream_t st) {
+  if (!sm100::dec_supported(M, K, N, G, s_dtype)) return TO_EUNSUPPORTED;
+  if (world < 1 || world > sm100::kDecMaxOut || N * world > INT32_MAX / 2) return TO_EUNSUPPORTED;
+  if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz)) return TO_EUNSUPPORTED;
+  if (ws != nullptr && !aligned16(ws)) return TO_EUNSUPPORTED;
+  sm100::DecOut out = {};
+  for (int r = 0; r < world; ++r) {
+    if (!aligned16(y_ranks[r])) return TO_EUNSUPPORTED;
+    out.y[r] = y_ranks[r];
+  }
+  out.ny = world;
+  out.ld = (int)(N * world);
+  out.col0 = (int)(N * rank);
+  return decode_dispatch(x, qw, s, s_dtype, qz, out, M, K, N, G, ws, ws_bytes, st);
 }
 
 }  // namespace tob

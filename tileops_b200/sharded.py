@@ -11,15 +11,18 @@ lays them out as [M, N].
 The compute step is a constructor argument so the bookkeeping runs unchanged on CPU ranks of a
 gloo group in tests; the default is the sm_100a kernel of this package.
 
-AWQ layers on CUDA can also run the gather inside the GEMM (`ShardedAWQLinear.gathered`): every
-rank maps every peer's output buffer (`PeerBuffers`, CUDA IPC over NVLink), the tensor-core
-kernel stores each output tile of its slice into all of them as the tile completes, and one
-collective barrier orders the peers' reads after every rank's stores. The exchange overlaps the
-GEMM and needs no reshuffle: each buffer is the [M, N] output.
+AWQ layers on CUDA can also run the gather inside the GEMM (`ShardedAWQLinear.gathered`,
+`gathered_gemm`): every rank maps every peer's output buffer (`PeerBuffers`, CUDA IPC over
+NVLink), the kernel (the decode kernel for 1-32 tokens, the tensor-core GEMM above) stores each
+finished output tile of its slice into all of them, and a rank barrier on the GPU
+(`PeerBarrier`: flags raised in every rank's mapped memory, no collective) orders the peers'
+reads after every rank's stores. The exchange overlaps the GEMM and needs no reshuffle: each
+buffer is the [M, N] output.
 """
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional
 
 import torch
@@ -164,6 +167,116 @@ class PeerBuffers:
         self._opened, self._own, self.ptrs = [], [], []
 
 
+class PeerBarrier:
+    """The GPU-side rank barrier of a group (to_peer_barrier): every rank's flag array mapped
+    into every rank's process plus this rank's barrier count. wait() queues the barrier on the
+    current stream: work queued after it sees every rank's stores queued before theirs.
+    Collective: every rank constructs it, calls wait() the same number of times, and closes it."""
+
+    def __init__(self, group=None):
+        from . import _lib
+
+        self.group = group
+        self.rank, self.world = _world(group)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        nbytes = int(_lib.load().to_peer_flags_bytes())
+        own, handle = _lib.ipc_alloc(nbytes)
+        torch.as_tensor(_DeviceArray(own, (nbytes,), "|u1"), device=dev).zero_()
+        self.counter = torch.zeros(1, dtype=torch.int64, device=dev)
+        torch.cuda.synchronize()  # zeroed before any peer can raise a slot
+        self._own, self._opened = own, []
+        try:
+            table: list = [None] * self.world
+            dist.all_gather_object(table, handle, group=group)
+            ptrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(own)
+                else:
+                    q = _lib.ipc_open(table[r])
+                    self._opened.append(q)
+                    ptrs.append(q)
+        except Exception:
+            for q in self._opened:
+                _lib.ipc_close(q)
+            _lib.ipc_free(own)
+            raise
+        self._table = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=group)  # every rank's flags are zero and mapped
+
+    def wait(self) -> None:
+        from . import _lib
+
+        _lib.check(_lib.load().to_peer_barrier(self._table, self.world, self.rank,
+                                               self.counter.data_ptr(), _lib.stream_ptr()),
+                   "peer_barrier")
+
+    def close(self) -> None:
+        from . import _lib
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for q in self._opened:
+            _lib.ipc_close(q)
+        dist.barrier(group=self.group)
+        _lib.ipc_free(self._own)
+        self._own, self._opened = None, []
+
+
+_BARRIERS: dict = {}
+
+
+def peer_barrier(group=None) -> PeerBarrier:
+    """The group's rank barrier, created on first use (collectively) and shared by its layers."""
+    key = id(group) if group is not None else None
+    b = _BARRIERS.get(key)
+    if b is None:
+        b = PeerBarrier(group)
+        _BARRIERS[key] = b
+    return b
+
+
+def close_peer_barriers() -> None:
+    """Releases every group's rank barrier (collective over each group)."""
+    for b in list(_BARRIERS.values()):
+        b.close()
+    _BARRIERS.clear()
+
+
+def gathered_gemm(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                  qzeros: torch.Tensor, bufs: "PeerBuffers", group=None) -> Optional[torch.Tensor]:
+    """y = x @ dequant(W) for this rank's column slice, all-gathered inside the kernel: each
+    rank stores its [M, N/P] slice into every rank's [M, N] buffer of `bufs` (the next one in
+    turn), then the group's GPU rank barrier orders the reads. Returns this rank's full [M, N]
+    buffer, or None (nothing launched) for shapes the gathering kernels do not take."""
+    from . import _lib
+    from .quant_awq import _as_words
+
+    rank, world = _world(group)
+    _lib.ensure_device(x, "awq_gemm_gather")
+    m, k = x.shape
+    dtype = scales.dtype
+    b = bufs.next_index()
+    xx = x.to(dtype).contiguous()
+    qw, qz = _as_words(qweight), _as_words(qzeros)
+    n_local = qweight.shape[1] * 8
+    group_size = k // qzeros.shape[0]
+    lib = _lib.load()
+    ws_bytes = lib.to_awq_gemm_workspace_size(m, k, n_local, group_size)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    table = (ctypes.c_void_p * world)(*bufs.ptrs[b])
+    rc = lib.to_awq_gemm_gather(xx.data_ptr(), qw.data_ptr(), scales.data_ptr(),
+                                _lib.DTYPE_CODES[dtype], qz.data_ptr(), table, world, rank, m, k,
+                                n_local, group_size, _lib.ptr(ws), ws_bytes, _lib.stream_ptr())
+    if rc == _lib.TO_EUNSUPPORTED:
+        return None
+    _lib.check(rc, "awq_gemm_gather")
+    peer_barrier(group).wait()
+    return bufs.tensors[b]
+
+
 class ShardedAWQLinear:
     """y = x @ dequant(W) with W's columns split across the group (tileops/quant_awq.py:112)."""
 
@@ -180,7 +293,6 @@ class ShardedAWQLinear:
             compute = lambda x, qw, s, qz: awq_gemm(x, qw, s, qz, 1)  # noqa: E731
         self.compute = compute
         self._peer_buffers: dict[int, PeerBuffers] = {}
-        self._flag: Optional[torch.Tensor] = None
 
     @classmethod
     def from_shard(cls, qweight, scales, qzeros, group=None,
@@ -197,7 +309,6 @@ class ShardedAWQLinear:
             compute = lambda x, qw, s, qz: awq_gemm(x, qw, s, qz, 1)  # noqa: E731
         self.compute = compute
         self._peer_buffers = {}
-        self._flag = None
         return self
 
     def local(self, x: torch.Tensor) -> torch.Tensor:
@@ -209,42 +320,18 @@ class ShardedAWQLinear:
 
     def gathered(self, x: torch.Tensor) -> torch.Tensor:
         """The whole [M, N] output with the all-gather done inside the GEMM (CUDA ranks of an
-        NCCL group). The result is one of two buffers per M that the layer reuses in turn: it
-        stays valid until the layer's second-next call with the same M. Shapes the fused kernel
-        does not take run the local GEMM and an all-gather instead."""
-        import ctypes
-
-        from . import _lib
-        from .quant_awq import _as_words
-
+        NCCL group) and a GPU rank barrier after it. The result is one of two buffers per M that
+        the layer reuses in turn: it stays valid until the layer's second-next call with the
+        same M. Shapes the fused kernels do not take run the local GEMM and an all-gather."""
         if self.world == 1:
             return self.local(x)
-        _lib.ensure_device(x, "awq_gemm_gather")
         m = x.shape[0]
-        dtype = self.scales.dtype
-        if self._flag is None:
-            self._flag = torch.zeros(1, dtype=torch.int32, device=x.device)
         bufs = self._peer_buffers.get(m)
         if bufs is None:
-            bufs = PeerBuffers(m, self.n, dtype, self.group)
+            bufs = PeerBuffers(m, self.n, self.scales.dtype, self.group)
             self._peer_buffers[m] = bufs
-        b = bufs.next_index()
-        xx = x.to(dtype).contiguous()
-        qw, qz = _as_words(self.qweight), _as_words(self.qzeros)
-        k = xx.shape[1]
-        n_local = self.n // self.world
-        table = (ctypes.c_void_p * self.world)(*bufs.ptrs[b])
-        lib = _lib.load()
-        rc = lib.to_awq_gemm_gather(xx.data_ptr(), qw.data_ptr(), self.scales.data_ptr(),
-                                    _lib.DTYPE_CODES[dtype], qz.data_ptr(), table, self.world,
-                                    self.rank, m, k, n_local, k // self.qzeros.shape[0],
-                                    _lib.stream_ptr())
-        if rc == _lib.TO_EUNSUPPORTED:
-            return gather_columns(self.local(x), self.group)
-        _lib.check(rc, "awq_gemm_gather")
-        # Every rank's kernel (and so its stores into the peers' buffers) precedes the reads.
-        dist.all_reduce(self._flag, group=self.group)
-        return bufs.tensors[b]
+        y = gathered_gemm(x, self.qweight, self.scales, self.qzeros, bufs, self.group)
+        return y if y is not None else gather_columns(self.local(x), self.group)
 
     def close(self) -> None:
         """Releases the peer-mapped output buffers (collective)."""
