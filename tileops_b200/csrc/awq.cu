@@ -24,8 +24,9 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int64_t kTensorCoreMinM = 33;
-// M <= 2 streams on CUDA cores (its cost grows with M); 3 <= M <= 32 runs the register-MMA
-// kernel, whose cost is flat in M.
+// Below the decode kernel's range (M <= 2 on layers of fewer than 1024 weight units) and on the
+// shapes the tensor-core kernels reject, M <= 2 streams on CUDA cores (its cost grows with M);
+// 3 <= M <= 64 runs the TMA-fed register-MMA kernel, whose cost is flat in M.
 constexpr int64_t kStreamMaxM = 2;
 __constant__ int kAwqOrder[8] = {0, 4, 1, 5, 2, 6, 3, 7};
 
