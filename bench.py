@@ -19,7 +19,8 @@ One step = one pass of the hot path over one batch of synthetic, seeded input. W
   dense_gemv   dense fp16 GEMV y = A[4096, 4096] @ x (the decode GEMV, unquantized; replicas).
   decode       32 layers x {qkv 4096->6144, o 4096->4096, gate_up 4096->28672, down 14336->4096}
                AWQ int4 group 128, fp16, M tokens (--decode-m, default 16), silu_and_mul of the
-               gate_up halves into down; N-sharded with an all-gather after every linear.
+               gate_up output (in its kernel) into down; N-sharded with an all-gather after
+               every linear.
                HBM GB/s over the weight bytes.
 
 Reported on one JSON line (rank 0):
@@ -716,7 +717,8 @@ class Decode:
     SHAPES = [(4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096)]  # (K, N) per linear
     G = 128
     data = "synthetic (seeded random packed int4 weights, scales U(0.002,0.02), x N(0,1))"
-    launches_per_step = 160  # 128 linears + 32 silu_and_mul
+    launches_per_step = 128  # counted by _run: 4 linears per layer (silu_and_mul inside the
+    # gate_up kernel up to 128 tokens, a second launch above), a barrier after each gathering one
 
     def __init__(self, dev, rank, world, m=16):
         import tileops_b200 as tob
@@ -724,8 +726,6 @@ class Decode:
 
         self.tob, self.sharded, self.world, self.dev = tob, sharded, world, dev
         self.bufs = None
-        if world > 1:
-            self.launches_per_step = 160 + 128  # and a gather step after each linear
         # 3.6 GB of weights: drawn on the device from a seeded generator
         g = torch.Generator(device=dev).manual_seed(1234 + 5 + 100 * rank)
         self.layers = []
@@ -751,9 +751,11 @@ class Decode:
         self.m = m
         self.bufs = None
         if self.world > 1 and m > 2:
-            # one set of two peer-mapped [m, N] outputs per linear of the layer, shared by the
-            # 32 layers (each set alternates its two buffers)
-            self.bufs = [self.sharded.PeerBuffers(m, n, torch.float16) for _, n in self.SHAPES]
+            # one set of two peer-mapped [m, N] outputs per linear of the layer ([m, N/2] for
+            # gate_up, whose kernel applies silu_and_mul), shared by the 32 layers (each set
+            # alternates its two buffers)
+            self.bufs = [self.sharded.PeerBuffers(m, n // 2 if j == 2 else n, torch.float16)
+                         for j, (_, n) in enumerate(self.SHAPES)]
         gx = torch.Generator().manual_seed(1234 + 5)
         x_cpu = torch.randn(m, 4096, generator=gx).half()
         self.x = x_cpu.to(self.dev)
@@ -761,24 +763,38 @@ class Decode:
         self.out_host = torch.empty(m, 4096, dtype=torch.float16).pin_memory()
 
     def _linear(self, x, w, j):
+        # gate_up (j == 2): gate and up columns interleaved in blocks of 8
+        # (awq_interleave_gate_up), silu_and_mul applied in the GEMM's epilogue
+        gemm = (lambda *a: self.tob.awq_gemm_silu_and_mul(*a)) if j == 2 else \
+            (lambda *a: self.tob.awq_gemm(*a, 1))
+        # this library's kernels per call: the GEMM, the activation after it above 128 tokens
+        own = 2 if (j == 2 and self.m > 128) else 1
         if self.world == 1:
-            return self.tob.awq_gemm(x, *w, 1)
+            self._launches += own
+            return gemm(x, *w)
         if self.m > 2:
             # this rank's column slice, all-gathered inside the kernel (peer stores over NVLink
             # and a GPU rank barrier)
-            y = self.sharded.gathered_gemm(x, *w, self.bufs[j])
+            if j == 2:
+                y = self.sharded.gathered_gemm_act(x, *w, self.bufs[j])
+            else:
+                y = self.sharded.gathered_gemm(x, *w, self.bufs[j])
             if y is not None:
+                self._launches += 2  # the gathering kernel and the rank barrier
                 return y
-        # 1-2 tokens: the streaming GEMV on the slice, then an NCCL all-gather
-        return self.sharded.gather_columns(self.tob.awq_gemm(x, *w, 1))
+        # 1-2 tokens (and shapes the gathering kernels do not take): the local kernel on the
+        # slice, then an NCCL all-gather
+        self._launches += own
+        return self.sharded.gather_columns(gemm(x, *w))
 
     def _run(self, x):
+        self._launches = 0
         for qkv, o, gu, down in self.layers:
             h = self._linear(x, qkv, 0)
             a = self._linear(h[:, :4096].contiguous(), o, 1)
-            u = self._linear(a, gu, 2)
-            act = self.tob.silu_and_mul(u[:, :14336], u[:, 14336:])  # gate, up read in place
+            act = self._linear(a, gu, 2)  # silu(gate) * up, [M, 14336]
             x = self._linear(act, down, 3)
+        self.launches_per_step = self._launches
         return x
 
     def close(self):
@@ -810,8 +826,9 @@ class Decode:
 
     def config(self, world):
         return {"workload": f"awq decode step, 32 layers x 4 linears (8B-class), M={self.m} fp16, "
-                            "group 128, silu_and_mul between gate_up and down, N-sharded, each "
-                            "linear all-gathered (inside its kernel from 3 tokens, NCCL below)",
+                            "group 128, silu_and_mul in the gate_up kernel (gate/up columns "
+                            "interleaved by 8), N-sharded, each linear all-gathered (inside its "
+                            "kernel for 3-128 tokens, NCCL otherwise)",
                 "M": self.m, "layers": self.LAYERS, "parallelism": f"tp{world} (N-sharded)",
                 "l2": "3.6 GB of weights per step > L2",
                 "launch_overlap": "programmatic dependent launch between consecutive layers"}

@@ -169,11 +169,11 @@ TO_API int to_awq_dequant(const int32_t* qweight, const void* scales, int s_dtyp
                    void* stream);
 /* replaces quant_awq.py:112 awq_gemm_triton: y [M,N] = x [M,K] @ dequant(W), x and y in
  * s_dtype (the facade casts x first, as the reference does), fp32 accumulation. 1-32 tokens
- * run the stream-K decode kernel (1-2 tokens on small layers the streaming GEMV), larger M the
- * tcgen05 tensor-core GEMM. The decode kernel needs a workspace of
- * to_awq_gemm_workspace_size(M, K, N, group_size) bytes (16-byte aligned; 0 when no kernel
- * for these shapes needs one) for the partial sums of column tiles split over SMs; calls that
- * share a workspace must not overlap on the GPU. */
+ * run the stream-K decode kernel (1-2 tokens on small layers the streaming GEMV), 33-128 the
+ * stream-K tcgen05 kernel, larger M the tcgen05 tile GEMM. The stream-K kernels need a
+ * workspace of to_awq_gemm_workspace_size(M, K, N, group_size) bytes (16-byte aligned; 0 when
+ * no kernel for these shapes needs one) for the partial sums of column tiles split over SMs;
+ * calls that share a workspace must not overlap on the GPU. */
 TO_API size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_t group_size);
 TO_API int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
                 const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
@@ -194,6 +194,34 @@ TO_API int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void*
                               int world, int rank, int64_t M, int64_t K, int64_t N,
                               int64_t group_size, void* workspace, size_t workspace_bytes,
                               void* stream);
+/* Library extension: the gate_up linear of an MLP block with its gated activation (no
+ * reference counterpart; it fuses to_awq_gemm with tileops/fused.py:97 silu_and_mul or :107
+ * gelu_and_mul). qweight/scales/qzeros hold the gate and up columns interleaved in blocks of 8
+ * (block 2j = gate columns 8j..8j+7, block 2j + 1 = up columns 8j..8j+7; N = 2F, N % 16 == 0);
+ * y[M, F] = act(gate) * up, act TO_ACT_SILU or TO_ACT_GELU_TANH, equal to to_awq_gemm on the
+ * un-interleaved weights followed by the activation kernel on its two halves (each GEMM output
+ * rounded to the scales' dtype first). 1-128 tokens apply it in the epilogue of the decode or
+ * stream-K kernel; other shapes run the GEMM into the workspace and the activation after it.
+ * Bit for bit it is to_awq_gemm on these weights followed by the activation. The workspace is
+ * to_awq_gemm_act_workspace_size(M, K, N, group_size) bytes, 16-byte aligned. */
+#define TO_ACT_SILU 0
+#define TO_ACT_GELU_TANH 1
+TO_API size_t to_awq_gemm_act_workspace_size(int64_t M, int64_t K, int64_t N,
+                                             int64_t group_size);
+TO_API int to_awq_gemm_act(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
+                           const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
+                           int64_t group_size, int act, void* workspace, size_t workspace_bytes,
+                           void* stream);
+/* to_awq_gemm_act on a rank's column slice (N = this rank's interleaved columns) with the
+ * all-gather inside the decode kernel, as to_awq_gemm_gather: this rank's [M, N/2] activation
+ * slice goes into every rank's [M, N/2 * world] output at columns [rank N/2, (rank + 1) N/2).
+ * Workspace as for to_awq_gemm with the rank's (M, K, N). 1-128 tokens only; TO_EUNSUPPORTED
+ * (nothing launched) otherwise: run to_awq_gemm_act and an all-gather instead. */
+TO_API int to_awq_gemm_act_gather(const void* x, const int32_t* qweight, const void* scales,
+                                  int s_dtype, const int32_t* qzeros, void* const* y_ranks,
+                                  int world, int rank, int64_t M, int64_t K, int64_t N,
+                                  int64_t group_size, int act, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 /* Rank barrier on the GPU (no reference counterpart; the completion step of the gathering
  * GEMMs). Each rank owns a flag array of to_peer_flags_bytes() bytes, zeroed, in memory the
  * others map with to_ipc_open, and an 8-byte counter in its own device memory, zeroed.

@@ -9,6 +9,7 @@ import re
 import sys
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -253,3 +254,28 @@ def test_argument_errors_match_the_reference():
     assert set(got) == set(want)
     for name in want:
         assert got[name] == want[name], f"{name}: {got[name]} != {want[name]}"
+
+
+def test_interleave_gate_up_is_a_column_permutation():
+    """awq_interleave_gate_up reorders whole packed words and scale columns: the dequantised
+    interleaved weight is the original's columns in the order gate block j, up block j."""
+    import torch
+
+    from oracle import awq as oawq
+    from tileops_b200.quant_awq import awq_interleave_gate_up
+
+    gen = torch.Generator().manual_seed(5)
+    k, n, g = 256, 96, 64
+    w = torch.randint(0, 16, (k, n), generator=gen, dtype=torch.int64)
+    z = torch.randint(0, 16, (k // g, n), generator=gen, dtype=torch.int64)
+    s = torch.rand(k // g, n, generator=gen).half()
+    qw, qz = torch.from_numpy(oawq.pack(w.numpy())), torch.from_numpy(oawq.pack(z.numpy()))
+    qw_i, s_i, qz_i = awq_interleave_gate_up(qw, s, qz)
+    perm = []
+    for j in range(n // 16):
+        perm += list(range(8 * j, 8 * j + 8)) + list(range(n // 2 + 8 * j, n // 2 + 8 * j + 8))
+    full = oawq.dequant(qw.numpy(), s.float().numpy(), qz.numpy(), "f16")
+    inter = oawq.dequant(qw_i.numpy(), s_i.float().numpy(), qz_i.numpy(), "f16")
+    assert np.array_equal(inter, full[:, perm])
+    with pytest.raises(ValueError):
+        awq_interleave_gate_up(qw[:, :1], s[:, :8], qz[:, :1])

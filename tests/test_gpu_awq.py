@@ -10,6 +10,7 @@ import torch
 
 import tileops_b200 as tob
 from oracle import awq as oawq
+from oracle import fused as ofused
 
 pytestmark = pytest.mark.gpu
 
@@ -262,6 +263,99 @@ def test_decode_kernel_graph_replays_with_new_inputs(cuda):
         out = tob.awq_gemm(x, qw, s, qz, 1)
     for i in range(4):
         x.copy_(torch.randn(16, 4096, generator=gen).half())
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, tob.awq_gemm(x, qw, s, qz, 1)), i
+    del graph
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu"])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("m,k,n,g", [
+    (1, 4096, 28672, 128),    # decode kernel, activation in its epilogue
+    (16, 4096, 28672, 128),   # the decode step's gate_up
+    (5, 1024, 1056, 64),      # a partial last column tile
+    (32, 512, 512, 128),      # tiles split over several CTAs
+    (2, 512, 528, 128),       # N % 32 != 0: GEMM into the workspace, then the activation
+    (48, 1024, 2048, 128),    # stream-K tensor-core kernel, activation in its epilogue
+    (300, 1024, 4096, 128),   # tensor-core GEMM + activation
+])
+def test_gemm_act_equals_gemm_then_act(cuda, act, dtype, m, k, n, g):
+    """The gate_up linear with its activation equals the GEMM on the same (interleaved) weights
+    followed by silu_and_mul / gelu_and_mul on its gate and up blocks, bit for bit; and the
+    GEMM on the original weights + the activation, and the oracle, within the GEMM tolerance
+    (the kernels' fp32 summation order depends on a column's tile, which the interleaving
+    moves)."""
+    gen = torch.Generator().manual_seed(m * 7 + k + 3 * n + g + (act == "gelu"))
+    qw, s, qz = make_awq(k, n, g, _DT[dtype], gen)
+    x = torch.randn(m, k, generator=gen).to(_DT[dtype])
+    qw_i, s_i, qz_i = (t.to(cuda) for t in tob.awq_interleave_gate_up(qw, s, qz))
+    xd = x.to(cuda)
+    fused = tob.awq_gemm_silu_and_mul if act == "silu" else tob.awq_gemm_gelu_and_mul
+    act_mul = tob.silu_and_mul if act == "silu" else tob.gelu_and_mul
+    y = fused(xd, qw_i, s_i, qz_i)
+    assert y.shape == (m, n // 2) and y.dtype == _DT[dtype]
+    # the same GEMM, unfused: blocks of 8 columns alternate gate, up
+    yi = tob.awq_gemm(xd, qw_i, s_i, qz_i, 1).view(m, n // 16, 2, 8)
+    gate = yi[:, :, 0, :].reshape(m, n // 2)
+    up = yi[:, :, 1, :].reshape(m, n // 2)
+    assert torch.equal(y, act_mul(gate, up))
+    # the activation against the oracle's, on that GEMM output (within two 16-bit ulps)
+    mine = ofused.act_and_mul(gate.float().cpu().numpy(), up.float().cpu().numpy(), act, dtype)
+    ulp2 = 2.0 ** -9 if dtype == "f16" else 2.0 ** -6
+    np.testing.assert_allclose(y.float().cpu().numpy(), mine, rtol=ulp2, atol=1e-6)
+    # the original layout's GEMM + activation, and the oracle GEMM + activation
+    full = tob.awq_gemm(xd, qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    sep = act_mul(full[:, :n // 2], full[:, n // 2:])
+    np.testing.assert_allclose(y.float().cpu().numpy(), sep.float().cpu().numpy(), rtol=5e-2,
+                               atol=5e-2)
+    want = oawq.gemm(x.float().numpy(), qw.numpy(), s.float().numpy(), qz.numpy(), dtype)
+    ref = ofused.act_and_mul(want[:, :n // 2], want[:, n // 2:], act, dtype)
+    np.testing.assert_allclose(y.float().cpu().numpy(), ref, rtol=5e-2, atol=5e-2)
+    assert torch.equal(fused(xd, qw_i, s_i, qz_i), y)
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("m,k,n,g", [
+    # stream-K tensor-core kernel (33 <= M <= 128): 64-row K blocks of 256-column tiles split
+    # over all SMs, later K ranges left as fp32 sums for the tile's owner
+    (33, 4096, 4096, 128),    # 16 tiles x 64 K blocks over 148 CTAs
+    (64, 4096, 6144, 128),    # the decode step's qkv at 64 tokens
+    (64, 14336, 4096, 128),   # down: 224 K blocks per tile
+    (100, 1024, 1056, 64),    # a partial last column tile
+    (128, 2048, 4096, 32),    # two scale rows per K block, a full 128-row x block
+    (40, 200, 256, 200),      # K % 64 != 0 (zero-filled tail), G == K
+    (77, 512, 768, 32),
+    (48, 8192, 256, 128),     # one tile over 32 CTAs: 31 partial sums added by its owner
+    (65, 64, 512, 64),        # one K block per tile
+])
+def test_stream_k_vs_oracle(cuda, dtype, m, k, n, g):
+    gen = torch.Generator().manual_seed(m * 5 + k + 7 * n + g)
+    qw, s, qz = make_awq(k, n, g, _DT[dtype], gen)
+    x = torch.randn(m, k, generator=gen).to(_DT[dtype])
+    args = (x.to(cuda), qw.to(cuda), s.to(cuda), qz.to(cuda), 1)
+    y = tob.awq_gemm(*args)
+    want = oawq.gemm(x.float().numpy(), qw.numpy(), s.float().numpy(), qz.numpy(), dtype)
+    np.testing.assert_allclose(y.float().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+    assert torch.equal(tob.awq_gemm(*args), y)  # the partial sums are added in a fixed order
+
+
+def test_stream_k_graph_replays_with_new_inputs(cuda):
+    """The stream-K kernel captured in a CUDA graph and replayed with fresh activations: the
+    owners consume and reset the per-launch flags of the partial sums on every replay."""
+    gen = torch.Generator().manual_seed(35)
+    qw, s, qz = (t.to(cuda) for t in make_awq(4096, 4096, 128, torch.float16, gen))
+    x = torch.zeros(64, 4096, dtype=torch.float16, device=cuda)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        tob.awq_gemm(x, qw, s, qz, 1)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = tob.awq_gemm(x, qw, s, qz, 1)
+    for i in range(4):
+        x.copy_(torch.randn(64, 4096, generator=gen).half())
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, tob.awq_gemm(x, qw, s, qz, 1)), i

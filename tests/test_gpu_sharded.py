@@ -2,7 +2,9 @@
 tensor-core GEMM for 40 and 256 tokens, the decode kernel for 1 and 16) stores its column slice
 into every rank's [M, N] output over NVLink (CUDA IPC mappings), then the GPU rank barrier
 orders the reads. Checked against the unsharded layer on the same GPU and against the oracle on
-sampled columns. Needs two GPUs (skipped on a one-GPU box)."""
+sampled columns; the gate_up form with silu_and_mul inside the decode kernel is checked against
+the unfused unsharded layer and, bit for bit on its own slice, the local fused kernel. Needs two
+GPUs (skipped on a one-GPU box)."""
 
 from __future__ import annotations
 
@@ -69,6 +71,28 @@ def _worker(rank, world, port, q):
                 float(np.abs(want).max()),
             )
         layer.close()
+        # gate_up with silu_and_mul in the decode kernel, gathered: this rank's slice of the
+        # interleaved weights holds gate and up blocks of the same columns
+        qw_i, s_i, qz_i = tob.awq_interleave_gate_up(qw, s, qz)
+        qw_l, s_l, qz_l = sharded.shard_awq(qw_i, s_i, qz_i, rank, world)
+        f = n // 2
+        for m in (16, 1):
+            x = torch.randn(m, k, generator=g).bfloat16().to(dev)
+            bufs = sharded.PeerBuffers(m, f, torch.bfloat16)
+            ya = sharded.gathered_gemm_act(x, qw_l, s_l, qz_l, bufs).clone()
+            # every rank's slice, computed here by the local fused kernel on that slice
+            local = torch.cat([tob.awq_gemm_silu_and_mul(
+                x, *sharded.shard_awq(qw_i, s_i, qz_i, r, world)) for r in range(world)], 1)
+            full = tob.awq_gemm(x, qw, s, qz, 1)
+            want = tob.silu_and_mul(full[:, :f], full[:, f:])
+            torch.cuda.synchronize()
+            report[f"act{m}"] = (
+                float((ya.float() - want.float()).abs().max()),
+                bool(torch.equal(ya, local)),
+                0.0,
+                float(want.float().abs().max()),
+            )
+            bufs.close()
         sharded.close_peer_barriers()
         q.put((rank, "ok", report))
     except Exception:  # noqa: BLE001
@@ -93,6 +117,9 @@ def test_awq_gathered_two_gpus():
     for rank, status, payload in results:
         assert status == "ok", f"rank {rank}:\n{payload}"
         for m, (vs_full, stable, vs_oracle, scale) in payload.items():
-            assert vs_full <= 1e-2 * max(1.0, scale), (rank, m, vs_full)
+            # the activation carries the GEMM's rounding differences (another K split) through
+            # silu(gate) * up: bounded relative to the largest output
+            tol = (4e-2 if str(m).startswith("act") else 1e-2) * max(1.0, scale)
+            assert vs_full <= tol, (rank, m, vs_full)
             assert stable, (rank, m)
             assert vs_oracle <= 1e-2 + 1e-2 * scale, (rank, m, vs_oracle)

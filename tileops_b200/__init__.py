@@ -19,7 +19,10 @@ from .quant_awq import (
     awq_dequantize,
     awq_dequantize_triton,
     awq_gemm,
+    awq_gemm_gelu_and_mul,
+    awq_gemm_silu_and_mul,
     awq_gemm_triton,
+    awq_interleave_gate_up,
     pack_awq_int4,
     unpack_awq_int4,
 )
@@ -74,7 +77,10 @@ __all__ = [
     "awq_dequantize",
     "awq_dequantize_triton",
     "awq_gemm",
+    "awq_gemm_gelu_and_mul",
+    "awq_gemm_silu_and_mul",
     "awq_gemm_triton",
+    "awq_interleave_gate_up",
     "pack_awq_int4",
     "unpack_awq_int4",
     "version",

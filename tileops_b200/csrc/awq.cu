@@ -14,6 +14,7 @@
 
 #include <type_traits>
 
+#include "act.cuh"
 #include "awq_common.cuh"
 #include "common.cuh"
 
@@ -654,10 +655,20 @@ bool awq_decode_wanted(int64_t M, int64_t K, int64_t N);
 int awq_decode_gather_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                              const int32_t* qz, void* const* y_ranks, int world, int rank,
                              int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
-                             size_t ws_bytes, cudaStream_t st);
+                             size_t ws_bytes, cudaStream_t st, int act = -1);
 int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
-                      void* ws, size_t ws_bytes, cudaStream_t st);
+                      void* ws, size_t ws_bytes, cudaStream_t st, int act = -1);
+int act_mul_interleaved_launch(const void* y, void* c, int dtype, int64_t rows, int64_t cols,
+                               int64_t ldy, int64_t ldc, int act, cudaStream_t st);
+size_t awq_sk_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dtype);
+int awq_sk_launch(const void* x, const int32_t* qw, const void* s, int s_dtype, const int32_t* qz,
+                  void* y, int64_t M, int64_t K, int64_t N, int64_t G, void* ws, size_t ws_bytes,
+                  cudaStream_t st, int act);
+int awq_sk_gather_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
+                         const int32_t* qz, void* const* y_ranks, int world, int rank, int64_t M,
+                         int64_t K, int64_t N, int64_t G, void* ws, size_t ws_bytes,
+                         cudaStream_t st, int act);
 
 // Measurement switch: TOB_AWQ_DECODE=0 keeps decode-sized M off the stream-K decode kernel.
 bool decode_enabled() {
@@ -666,6 +677,20 @@ bool decode_enabled() {
     return v == nullptr || v[0] != '0';
   }();
   return on;
+}
+
+// Token counts the stream-K tensor-core kernel takes: 33-128 (below, the decode kernel's
+// register-operand MMAs stream faster). Measurement switch TOB_AWQ_SK: "0" off, "all" for every
+// M <= 128.
+constexpr int64_t kSkMinM = 33, kSkMaxM = 128;
+bool sk_wanted(int64_t M) {
+  static const int mode = [] {
+    const char* v = tuning_env("TOB_AWQ_SK");
+    if (v == nullptr) return 1;
+    return v[0] == '0' ? 0 : (v[0] == 'a' ? 2 : 1);
+  }();
+  if (mode == 0 || M > kSkMaxM) return false;
+  return mode == 2 || M >= kSkMinM;
 }
 
 // Used by the tensor-core GEMM translation unit when it must stream small M.
@@ -747,6 +772,7 @@ int to_awq_dequant(const int32_t* qweight, const void* scales, int s_dtype, cons
 size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_t group_size) {
   if (M <= 0 || K <= 0 || N <= 0 || group_size <= 0 || N % 8 != 0 || K % group_size != 0)
     return 0;
+  if (sk_wanted(M)) return awq_sk_workspace(M, K, N, group_size, TO_F16);
   if (!decode_enabled()) return 0;
   return awq_decode_workspace(M, K, N, group_size, TO_F16);
 }
@@ -763,7 +789,11 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
   // GEMM; 33 <= M <= 64 on the TMA-fed register-MMA kernel when the tcgen05 tiles would leave
   // most SMs idle; the shapes none of them takes (ragged N, unaligned rows) on the streaming
   // SIMT kernels.
-  if (M <= 32 && decode_enabled() && awq_decode_wanted(M, K, N)) {
+  if (sk_wanted(M)) {
+    rc = awq_sk_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size, workspace,
+                       workspace_bytes, (cudaStream_t)stream, -1);
+    if (rc != TO_EUNSUPPORTED) return rc;
+  } else if (M <= 32 && decode_enabled() && awq_decode_wanted(M, K, N)) {
     rc = awq_decode_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size,
                            workspace, workspace_bytes, (cudaStream_t)stream);
     if (rc != TO_EUNSUPPORTED) return rc;
@@ -786,6 +816,91 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
                            (cudaStream_t)stream);
 }
 
+// The gate_up linear with its activation: the decode (1-32 tokens) and stream-K (33-128) kernels
+// apply it in their epilogue, on the shapes to_awq_gemm routes to them; other shapes run
+// to_awq_gemm into the front of the workspace ([M, N] in the scales' dtype, 256-byte aligned
+// size) and the activation over it. Either way the result is to_awq_gemm's output on these
+// weights, rounded, then the activation.
+static size_t act_tmp_bytes(int64_t M, int64_t N) { return ((size_t)(M * N * 2) + 255) & ~(size_t)255; }
+
+size_t to_awq_gemm_act_workspace_size(int64_t M, int64_t K, int64_t N, int64_t group_size) {
+  if (M <= 0 || K <= 0 || N <= 0 || group_size <= 0 || N % 16 != 0 || K % group_size != 0)
+    return 0;
+  return act_tmp_bytes(M, N) + to_awq_gemm_workspace_size(M, K, N, group_size);
+}
+
+int to_awq_gemm_act(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
+                    const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
+                    int64_t group_size, int act, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  int rc = check_awq_shapes("awq_gemm_act", K, N, group_size);
+  if (rc) return rc;
+  if (M <= 0) return fail(TO_EINVAL, "awq_gemm_act: invalid M=%lld", (long long)M);
+  if (act != kSilu && act != kGeluTanh)
+    return fail(TO_EINVAL, "awq_gemm_act: unknown activation %d", act);
+  if (N % 16 != 0)
+    return fail(TO_EINVAL, "awq_gemm_act: N=%lld is not a multiple of 16 (gate and up blocks of 8)",
+                (long long)N);
+  if (s_dtype != TO_F16 && s_dtype != TO_BF16)
+    return fail(TO_EUNSUPPORTED, "awq_gemm_act: scales dtype %s (fp16, bf16)", dtype_name(s_dtype));
+  if (!aligned16(scales) || !aligned16(x) || !aligned16(y))
+    return fail(TO_EINVAL, "awq_gemm_act: x, scales and y must be 16-byte aligned");
+  const size_t need = to_awq_gemm_act_workspace_size(M, K, N, group_size);
+  if (workspace_bytes < need || (need > 0 && (workspace == nullptr || !aligned16(workspace))))
+    return fail(TO_ENOSPACE, "awq_gemm_act: workspace of %zu bytes, %zu needed (16-byte aligned)",
+                workspace_bytes, need);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* tmp = static_cast<char*>(workspace);
+  char* gemm_ws = tmp + act_tmp_bytes(M, N);
+  const size_t gemm_ws_bytes = workspace_bytes - act_tmp_bytes(M, N);
+  if (sk_wanted(M)) {
+    rc = awq_sk_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size, gemm_ws,
+                       gemm_ws_bytes, st, act);
+    if (rc != TO_EUNSUPPORTED) return rc;
+  } else if (M <= 32 && decode_enabled() && awq_decode_wanted(M, K, N)) {
+    rc = awq_decode_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size, gemm_ws,
+                           gemm_ws_bytes, st, act);
+    if (rc != TO_EUNSUPPORTED) return rc;
+  }
+  rc = to_awq_gemm(x, qweight, scales, s_dtype, qzeros, tmp, M, K, N, group_size, gemm_ws,
+                   gemm_ws_bytes, stream);
+  if (rc) return rc;
+  return act_mul_interleaved_launch(tmp, y, s_dtype, M, N, N, N / 2, act, st);
+}
+
+int to_awq_gemm_act_gather(const void* x, const int32_t* qweight, const void* scales,
+                           int s_dtype, const int32_t* qzeros, void* const* y_ranks, int world,
+                           int rank, int64_t M, int64_t K, int64_t N, int64_t group_size, int act,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_awq_shapes("awq_gemm_act_gather", K, N, group_size);
+  if (rc) return rc;
+  if (M <= 0) return fail(TO_EINVAL, "awq_gemm_act_gather: invalid M=%lld", (long long)M);
+  if (act != kSilu && act != kGeluTanh)
+    return fail(TO_EINVAL, "awq_gemm_act_gather: unknown activation %d", act);
+  if (N % 16 != 0)
+    return fail(TO_EINVAL, "awq_gemm_act_gather: N=%lld is not a multiple of 16", (long long)N);
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(TO_EINVAL, "awq_gemm_act_gather: rank %d of %d (1 to 8 ranks)", rank, world);
+  if (!y_ranks) return fail(TO_EINVAL, "awq_gemm_act_gather: null output table");
+  for (int r = 0; r < world; ++r)
+    if (!y_ranks[r]) return fail(TO_EINVAL, "awq_gemm_act_gather: null output of rank %d", r);
+  if (!aligned16(scales) || !aligned16(x))
+    return fail(TO_EINVAL, "awq_gemm_act_gather: x and scales must be 16-byte aligned");
+  rc = TO_EUNSUPPORTED;
+  if (sk_wanted(M))
+    rc = awq_sk_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M, K, N,
+                              group_size, workspace, workspace_bytes, (cudaStream_t)stream, act);
+  else if (M <= 32 && decode_enabled())
+    rc = awq_decode_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M,
+                                  K, N, group_size, workspace, workspace_bytes,
+                                  (cudaStream_t)stream, act);
+  if (rc == TO_EUNSUPPORTED)
+    return fail(TO_EUNSUPPORTED,
+                "awq_gemm_act_gather: only the decode and stream-K kernels (1-128 tokens) gather "
+                "the activation; run to_awq_gemm_act and an all-gather instead");
+  return rc;
+}
+
 int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
                        const int32_t* qzeros, void* const* y_ranks, int world, int rank,
                        int64_t M, int64_t K, int64_t N, int64_t group_size, void* workspace,
@@ -803,7 +918,10 @@ int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales
   // Decode-sized M on the stream-K decode kernel, the rest on the tensor-core GEMM; both store
   // each finished tile into every rank's output.
   rc = TO_EUNSUPPORTED;
-  if (M <= 32 && decode_enabled())
+  if (sk_wanted(M))
+    rc = awq_sk_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M, K, N,
+                              group_size, workspace, workspace_bytes, (cudaStream_t)stream, -1);
+  else if (M <= 32 && decode_enabled())
     rc = awq_decode_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M, K,
                                   N, group_size, workspace, workspace_bytes,
                                   (cudaStream_t)stream);

@@ -40,6 +40,7 @@
 
 #include <unistd.h>
 
+#include "act.cuh"
 #include "awq_common.cuh"
 #include "sm100.cuh"
 
@@ -69,10 +70,13 @@ __host__ __device__ __forceinline__ int64_t dec_cta_of(int64_t u, int64_t units,
 
 // Where the output goes: this GPU's y, or (an N-sharded layer whose all-gather is done here)
 // every rank's [M, ld] output at columns [col0, col0 + N), the peers' mapped into this process.
+// act >= 0 (kSilu, kGeluTanh): the weights are a gate_up linear whose gate and up columns
+// alternate in blocks of 8 (one packed word each), and the output is act(gate) * up, N / 2
+// columns wide (col0 and ld count those columns).
 constexpr int kDecMaxOut = 8;
 struct DecOut {
   void* y[kDecMaxOut];
-  int ny, ld, col0;
+  int ny, ld, col0, act;
 };
 
 struct DecPlan {
@@ -624,22 +628,66 @@ __global__ void __launch_bounds__(DecGeom<WK>::kThreads, 1) k_awq_decode(
         if (lane < nc) fl[4 * lane] = 0ull;  // consumed: ready for the next launch's epoch
         for (int c = 32 + lane; c < nc; c += 32) fl[4 * c] = 0ull;
         if (!ok) break;
+        if (out.act < 0) {
 #pragma unroll
-        for (int tt = 0; tt < NT; ++tt)
+          for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const int c = col0 + 2 * p;
-            const int m = 8 * tt + 2 * q;
-            if (c < N) {
-              const H2 v0 = Half2Of<T>::from_floats(acc[p][tt][0], acc[p][tt][2]);
-              const H2 v1 = Half2Of<T>::from_floats(acc[p][tt][1], acc[p][tt][3]);
-              for (int d = 0; d < out.ny; ++d) {
-                T* yd = static_cast<T*>(out.y[d]) + out.col0 + c;
-                if (m < M) *reinterpret_cast<H2*>(yd + (size_t)m * out.ld) = v0;
-                if (m + 1 < M) *reinterpret_cast<H2*>(yd + (size_t)(m + 1) * out.ld) = v1;
+            for (int p = 0; p < 4; ++p) {
+              const int c = col0 + 2 * p;
+              const int m = 8 * tt + 2 * q;
+              if (c < N) {
+                const H2 v0 = Half2Of<T>::from_floats(acc[p][tt][0], acc[p][tt][2]);
+                const H2 v1 = Half2Of<T>::from_floats(acc[p][tt][1], acc[p][tt][3]);
+                for (int d = 0; d < out.ny; ++d) {
+                  T* yd = static_cast<T*>(out.y[d]) + out.col0 + c;
+                  if (m < M) *reinterpret_cast<H2*>(yd + (size_t)m * out.ld) = v0;
+                  if (m + 1 < M) *reinterpret_cast<H2*>(yd + (size_t)(m + 1) * out.ld) = v1;
+                }
               }
             }
-          }
+        } else {
+          // Gate and up blocks alternate word by word, so this thread's word (g) and the word
+          // of lane ^ 4 (g ^ 1) hold the gate and up sums of the same 8 columns. The even lane
+          // takes columns 0-3 of the pair, the odd lane columns 4-7; each receives the other
+          // half's sums by one exchange. Each sum is rounded to T (the GEMM's output) before
+          // the activation, so the result equals the unfused GEMM + silu_and_mul.
+          const bool is_gate = (g & 1) == 0;
+          const int pair0 = col0 - (is_gate ? 0 : 8);    // the gate word's first column
+          const int a_col = (pair0 >> 1) + (is_gate ? 0 : 4);  // first output column here
+#pragma unroll
+          for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+            for (int pp = 0; pp < 2; ++pp) {
+              float gv[4], uv[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float mine = is_gate ? acc[pp + 2][tt][e] : acc[pp][tt][e];
+                const float other = __shfl_xor_sync(0xffffffffu, mine, 4);
+                gv[e] = is_gate ? acc[pp][tt][e] : other;
+                uv[e] = is_gate ? other : acc[pp + 2][tt][e];
+              }
+              T r[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const T gt = from_f32<T>(gv[e]), ut = from_f32<T>(uv[e]);
+                r[e] = out.act == kSilu ? act_mul<T, kSilu>(gt, ut) : act_mul<T, kGeluTanh>(gt, ut);
+              }
+              const int c = a_col + 2 * pp;
+              const int m = 8 * tt + 2 * q;
+              if (pair0 < N) {
+                H2 v0, v1;
+                v0.x = r[0];
+                v0.y = r[2];
+                v1.x = r[1];
+                v1.y = r[3];
+                for (int d = 0; d < out.ny; ++d) {
+                  T* yd = static_cast<T*>(out.y[d]) + out.col0 + c;
+                  if (m < M) *reinterpret_cast<H2*>(yd + (size_t)m * out.ld) = v0;
+                  if (m + 1 < M) *reinterpret_cast<H2*>(yd + (size_t)(m + 1) * out.ld) = v1;
+                }
+              }
+            }
+        }
       }
     }
 #pragma unroll
@@ -859,9 +907,11 @@ int decode_dispatch(const void* x, const int32_t* qw, const void* s, int s_dtype
 }
 }  // namespace
 
+// act < 0: y = x @ dequant(W), [M, N]; act >= 0: y = act(gate) * up, [M, N / 2], of a gate_up
+// weight interleaved in blocks of 8 columns.
 int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
-                      void* ws, size_t ws_bytes, cudaStream_t st) {
+                      void* ws, size_t ws_bytes, cudaStream_t st, int act) {
   if (!sm100::dec_supported(M, K, N, G, s_dtype)) return TO_EUNSUPPORTED;
   if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz) || !aligned16(y))
     return TO_EUNSUPPORTED;
@@ -869,17 +919,19 @@ int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dty
   sm100::DecOut out = {};
   out.y[0] = y;
   out.ny = 1;
-  out.ld = (int)N;
+  out.ld = (int)(act >= 0 ? N / 2 : N);
   out.col0 = 0;
+  out.act = act;
   return decode_dispatch(x, qw, s, s_dtype, qz, out, M, K, N, G, ws, ws_bytes, st);
 }
 
 // The gathering form: this rank's [M, N] slice goes into the [M, N x world] output of every
-// rank (y_ranks[r], the peers' mapped into this process) at columns [rank N, (rank + 1) N).
+// rank (y_ranks[r], the peers' mapped into this process) at columns [rank N, (rank + 1) N)
+// (with act >= 0: its [M, N / 2] activation slice into [M, N / 2 x world]).
 int awq_decode_gather_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                              const int32_t* qz, void* const* y_ranks, int world, int rank,
                              int64_t M, int64_t K, int64_t N, int64_t G, void* ws,
-                             size_t ws_bytes, cudaStream_t st) {
+                             size_t ws_bytes, cudaStream_t st, int act) {
   if (!sm100::dec_supported(M, K, N, G, s_dtype)) return TO_EUNSUPPORTED;
   if (world < 1 || world > sm100::kDecMaxOut || N * world > INT32_MAX / 2) return TO_EUNSUPPORTED;
   if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz)) return TO_EUNSUPPORTED;
@@ -890,8 +942,10 @@ int awq_decode_gather_launch(const void* x, const int32_t* qw, const void* s, in
     out.y[r] = y_ranks[r];
   }
   out.ny = world;
-  out.ld = (int)(N * world);
-  out.col0 = (int)(N * rank);
+  const int64_t n_out = act >= 0 ? N / 2 : N;  // this rank's output columns
+  out.ld = (int)(n_out * world);
+  out.col0 = (int)(n_out * rank);
+  out.act = act;
   return decode_dispatch(x, qw, s, s_dtype, qz, out, M, K, N, G, ws, ws_bytes, st);
 }
 

@@ -124,6 +124,42 @@ def awq_dequantize_triton(
     return out
 
 
+def _gemm_args(op: str, input: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+               qzeros: torch.Tensor, split_k_iters: int):
+    """The reference's checks of awq_gemm_triton (quant_awq.py:125-151), in its order and with
+    its messages; returns (M, K, N, group size)."""
+    if input.ndim != 2:
+        raise ValueError(f"{op}: input must be 2-D [M, K]")
+    m, k = input.shape
+    if qweight.shape[0] != k:
+        raise ValueError(f"{op}: qweight rows {qweight.shape[0]} != K={k}")
+    n = qweight.shape[1] * 8
+    num_groups = qzeros.shape[0]
+    group_size = _infer_group_size(k, num_groups)
+    if n <= 0 or m <= 0:
+        raise ValueError(f"{op}: invalid M={m}, N={n}, K={k}")
+    if qweight.shape[1] != n // 8:
+        raise ValueError(f"{op}: qweight column count mismatch")
+    if qzeros.shape[1] != n // 8:
+        raise ValueError(f"{op}: qzeros column count mismatch")
+    if scales.shape != (num_groups, n):
+        raise ValueError(
+            f"{op}: scales shape {tuple(scales.shape)} expected "
+            f"({num_groups}, {n})"
+        )
+    if split_k_iters <= 0 or (split_k_iters & (split_k_iters - 1)) != 0:
+        raise ValueError(f"{op}: split_k_iters must be a positive power of 2")
+    if split_k_iters > 32:
+        raise ValueError(f"{op}: split_k_iters must be <= 32")
+    _validate_group_size(group_size, k)
+    _lib.ensure_device(input, op)
+    _lib.same_device(op, input, qweight, scales, qzeros)
+    if scales.dtype not in (torch.float16, torch.bfloat16):
+        raise NotImplementedError(f"{op}: scales dtype {scales.dtype} (fp16 and bf16 are "
+                                  "supported)")
+    return m, k, n, group_size
+
+
 def awq_gemm_triton(
     input: torch.Tensor,
     qweight: torch.Tensor,
@@ -138,36 +174,9 @@ def awq_gemm_triton(
     (quant_awq.py:112-155). ``split_k_iters`` is validated as in the reference and does not
     change the result; the kernel picks its own K split."""
     del block_size_m, block_size_n, block_size_k
-    op = "awq_gemm_triton"
-    if input.ndim != 2:
-        raise ValueError("awq_gemm_triton: input must be 2-D [M, K]")
-    m, k = input.shape
-    if qweight.shape[0] != k:
-        raise ValueError(f"awq_gemm_triton: qweight rows {qweight.shape[0]} != K={k}")
-    n = qweight.shape[1] * 8
-    num_groups = qzeros.shape[0]
-    group_size = _infer_group_size(k, num_groups)
-    if n <= 0 or m <= 0:
-        raise ValueError(f"awq_gemm_triton: invalid M={m}, N={n}, K={k}")
-    if qweight.shape[1] != n // 8:
-        raise ValueError("awq_gemm_triton: qweight column count mismatch")
-    if qzeros.shape[1] != n // 8:
-        raise ValueError("awq_gemm_triton: qzeros column count mismatch")
-    if scales.shape != (num_groups, n):
-        raise ValueError(
-            f"awq_gemm_triton: scales shape {tuple(scales.shape)} expected "
-            f"({num_groups}, {n})"
-        )
-    if split_k_iters <= 0 or (split_k_iters & (split_k_iters - 1)) != 0:
-        raise ValueError("awq_gemm_triton: split_k_iters must be a positive power of 2")
-    if split_k_iters > 32:
-        raise ValueError("awq_gemm_triton: split_k_iters must be <= 32")
-    _validate_group_size(group_size, k)
-    _lib.ensure_device(input, op)
-    _lib.same_device(op, input, qweight, scales, qzeros)
+    m, k, n, group_size = _gemm_args("awq_gemm_triton", input, qweight, scales, qzeros,
+                                     split_k_iters)
     out_dtype = scales.dtype
-    if out_dtype not in (torch.float16, torch.bfloat16):
-        raise NotImplementedError(f"{op}: scales dtype {out_dtype} (fp16 and bf16 are supported)")
     x = input.to(out_dtype).contiguous()
     qw = _as_words(qweight)
     qz = _as_words(qzeros)
@@ -182,6 +191,71 @@ def awq_gemm_triton(
     return y
 
 
+# ---------------------------------------------------------------- library extensions
+# The gate_up linear of an MLP block with its gated activation in the GEMM (no reference
+# counterpart: the reference runs awq_gemm, then tileops/fused.py:97 silu_and_mul on the two
+# halves of its output).
+
+ACT_SILU = 0
+ACT_GELU_TANH = 1
+
+
+def awq_interleave_gate_up(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor):
+    """The weight layout awq_gemm_silu_and_mul / awq_gemm_gelu_and_mul read, from a gate_up
+    linear whose N columns hold gate in [0, N/2) and up in [N/2, N): gate and up alternate in
+    blocks of 8 columns (one packed word): block 2j = gate columns 8j..8j+7, block 2j + 1 = up
+    columns 8j..8j+7. A one-time reordering of whole words and scale columns (CPU or CUDA
+    tensors); returns contiguous (qweight, scales, qzeros)."""
+    n = qweight.shape[1] * 8
+    if n % 16 != 0:
+        raise ValueError(f"awq_interleave_gate_up: N={n} is not a multiple of 16")
+    if scales.shape[-1] != n or qzeros.shape[-1] != n // 8:
+        raise ValueError("awq_interleave_gate_up: scales / qzeros do not match qweight's N")
+
+    def words(t: torch.Tensor) -> torch.Tensor:
+        r = t.shape[0]
+        return t.reshape(r, 2, n // 16).transpose(1, 2).reshape(r, n // 8).contiguous()
+
+    g = scales.shape[0]
+    s = scales.reshape(g, 2, n // 16, 8).transpose(1, 2).reshape(g, n).contiguous()
+    return words(qweight), s, words(qzeros)
+
+
+def _gemm_act(op: str, act: int, input, qweight, scales, qzeros, split_k_iters) -> torch.Tensor:
+    m, k, n, group_size = _gemm_args(op, input, qweight, scales, qzeros, split_k_iters)
+    if n % 16 != 0:
+        raise ValueError(f"{op}: N={n} is not a multiple of 16 (gate and up blocks of 8)")
+    out_dtype = scales.dtype
+    x = input.to(out_dtype).contiguous()
+    qw = _as_words(qweight)
+    qz = _as_words(qzeros)
+    s = scales.contiguous()
+    y = torch.empty(m, n // 2, dtype=out_dtype, device=input.device)
+    lib = _lib.load()
+    ws_bytes = lib.to_awq_gemm_act_workspace_size(m, k, n, group_size)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device) if ws_bytes else None
+    _lib.call("to_awq_gemm_act", x.data_ptr(), qw.data_ptr(), s.data_ptr(),
+              _lib.DTYPE_CODES[out_dtype], qz.data_ptr(), y.data_ptr(), m, k, n, group_size,
+              act, _lib.ptr(ws), ws_bytes, _lib.stream_ptr())
+    return y
+
+
+def awq_gemm_silu_and_mul(input: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                          qzeros: torch.Tensor, split_k_iters: int = 1) -> torch.Tensor:
+    """``silu(gate) * up`` of the gate_up linear ``input @ dequant(W)``, W interleaved by
+    awq_interleave_gate_up: [M, N/2], equal to awq_gemm on the original weights followed by
+    silu_and_mul(y[:, :N/2], y[:, N/2:]). Arguments and checks as awq_gemm_triton."""
+    return _gemm_act("awq_gemm_silu_and_mul", ACT_SILU, input, qweight, scales, qzeros,
+                     split_k_iters)
+
+
+def awq_gemm_gelu_and_mul(input: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                          qzeros: torch.Tensor, split_k_iters: int = 1) -> torch.Tensor:
+    """``gelu_tanh(gate) * up`` of the gate_up linear, as awq_gemm_silu_and_mul."""
+    return _gemm_act("awq_gemm_gelu_and_mul", ACT_GELU_TANH, input, qweight, scales, qzeros,
+                     split_k_iters)
+
+
 # vLLM names kept as primary entry points (quant_awq.py:159-160).
 awq_dequantize = awq_dequantize_triton
 awq_gemm = awq_gemm_triton
@@ -192,7 +266,10 @@ __all__ = [
     "awq_dequantize",
     "awq_dequantize_triton",
     "awq_gemm",
+    "awq_gemm_gelu_and_mul",
+    "awq_gemm_silu_and_mul",
     "awq_gemm_triton",
+    "awq_interleave_gate_up",
     "pack_awq_int4",
     "unpack_awq_int4",
 ]

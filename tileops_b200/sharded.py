@@ -277,6 +277,41 @@ def gathered_gemm(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     return bufs.tensors[b]
 
 
+def gathered_gemm_act(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                      qzeros: torch.Tensor, bufs: "PeerBuffers", act: int = 0,
+                      group=None) -> Optional[torch.Tensor]:
+    """act(gate) * up of this rank's slice of a gate_up linear (interleaved by
+    awq_interleave_gate_up; N/P columns, N/(2P) outputs), all-gathered inside the decode kernel
+    into every rank's [M, N/2] buffer of `bufs`, then the GPU rank barrier. Returns this rank's
+    full [M, N/2] buffer, or None (nothing launched) where the decode kernel does not take the
+    shapes (more than 32 tokens): run awq_gemm_silu_and_mul and gather_columns instead."""
+    from . import _lib
+    from .quant_awq import _as_words
+
+    rank, world = _world(group)
+    _lib.ensure_device(x, "awq_gemm_act_gather")
+    m, k = x.shape
+    dtype = scales.dtype
+    b = bufs.next_index()
+    xx = x.to(dtype).contiguous()
+    qw, qz = _as_words(qweight), _as_words(qzeros)
+    n_local = qweight.shape[1] * 8
+    group_size = k // qzeros.shape[0]
+    lib = _lib.load()
+    ws_bytes = lib.to_awq_gemm_workspace_size(m, k, n_local, group_size)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    table = (ctypes.c_void_p * world)(*bufs.ptrs[b])
+    rc = lib.to_awq_gemm_act_gather(xx.data_ptr(), qw.data_ptr(), scales.data_ptr(),
+                                    _lib.DTYPE_CODES[dtype], qz.data_ptr(), table, world, rank,
+                                    m, k, n_local, group_size, act, _lib.ptr(ws), ws_bytes,
+                                    _lib.stream_ptr())
+    if rc == _lib.TO_EUNSUPPORTED:
+        return None
+    _lib.check(rc, "awq_gemm_act_gather")
+    peer_barrier(group).wait()
+    return bufs.tensors[b]
+
+
 class ShardedAWQLinear:
     """y = x @ dequant(W) with W's columns split across the group (tileops/quant_awq.py:112)."""
 
