@@ -718,7 +718,7 @@ class Decode:
     G = 128
     data = "synthetic (seeded random packed int4 weights, scales U(0.002,0.02), x N(0,1))"
     launches_per_step = 128  # counted by _run: 4 linears per layer (silu_and_mul inside the
-    # gate_up kernel up to 128 tokens, a second launch above), a barrier after each gathering one
+    # gate_up kernel up to 32 tokens, a second launch above), a barrier after each gathering one
 
     def __init__(self, dev, rank, world, m=16):
         import tileops_b200 as tob
@@ -767,8 +767,9 @@ class Decode:
         # (awq_interleave_gate_up), silu_and_mul applied in the GEMM's epilogue
         gemm = (lambda *a: self.tob.awq_gemm_silu_and_mul(*a)) if j == 2 else \
             (lambda *a: self.tob.awq_gemm(*a, 1))
-        # this library's kernels per call: the GEMM, the activation after it above 128 tokens
-        own = 2 if (j == 2 and self.m > 128) else 1
+        # this library's kernels per call: the GEMM, and the activation after it where the GEMM
+        # has no fused epilogue (gate_up, K = 4096, above 32 tokens)
+        own = 2 if (j == 2 and self.m > 32) else 1
         if self.world == 1:
             self._launches += own
             return gemm(x, *w)
@@ -828,7 +829,7 @@ class Decode:
         return {"workload": f"awq decode step, 32 layers x 4 linears (8B-class), M={self.m} fp16, "
                             "group 128, silu_and_mul in the gate_up kernel (gate/up columns "
                             "interleaved by 8), N-sharded, each linear all-gathered (inside its "
-                            "kernel for 3-128 tokens, NCCL otherwise)",
+                            "kernel where it has a gathering form, NCCL otherwise)",
                 "M": self.m, "layers": self.LAYERS, "parallelism": f"tp{world} (N-sharded)",
                 "l2": "3.6 GB of weights per step > L2",
                 "launch_overlap": "programmatic dependent launch between consecutive layers"}

@@ -143,6 +143,17 @@ TO_API int to_per_token_group_quant_i8(const void* x, int x_dtype, int64_t n_gro
 TO_API int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups,
                                  int64_t group_size, float eps, int ue8m0, int64_t cm_rows,
                                  int64_t cm_groups, void* q, float* scales, void* stream);
+/* The same two quantisers with dtype = torch.float8_e4m3fnuz (quant_fp8.py:52, :83 with that
+ * dtype): codes in the e4m3fnuz encoding (exponent bias 8, max 240, no negative zero, NaN 0x80).
+ * The tensor-wide form scales to finfo(e4m3fnuz).max = 240 and clamps to +-240; the group form
+ * uses get_fp8_min_max's +-224 (quant_fp8.py:42-43). Every NaN code is 0x80. No sm_100 GEMM
+ * consumes these codes; they are for exchange with e4m3fnuz consumers. */
+TO_API int to_input_to_fp8_fnuz(const void* x, int x_dtype, int64_t n, void* q, float* dq_scale,
+                                void* workspace, size_t workspace_bytes, void* stream);
+TO_API int to_per_token_group_quant_fp8_fnuz(const void* x, int x_dtype, int64_t n_groups,
+                                             int64_t group_size, float eps, int ue8m0,
+                                             int64_t cm_rows, int64_t cm_groups, void* q,
+                                             float* scales, void* stream);
 
 /* ---- block dequantisation ------------------------------------------------------------- */
 /* replaces tileops/quant_int8.py:136 block_dequant: y[n,k] = float(q[n,k]) * s[n/bn, k/bk]. */
@@ -151,6 +162,9 @@ TO_API int to_block_dequant_i8(const int8_t* q, const float* s, float* y, int64_
 /* replaces tileops/quant_fp8.py:143 block_dequant (e4m3fn input). */
 TO_API int to_block_dequant_fp8(const void* q, const float* s, float* y, int64_t n, int64_t k,
                          int64_t block_n, int64_t block_k, void* stream);
+/* replaces tileops/quant_fp8.py:143 block_dequant for e4m3fnuz input (0x80 reads as NaN). */
+TO_API int to_block_dequant_fp8_fnuz(const void* q, const float* s, float* y, int64_t n,
+                                     int64_t k, int64_t block_n, int64_t block_k, void* stream);
 
 /* ---- AWQ W4A16 (tileops/quant_awq.py) --------------------------------------------------
  * Packed layout: eight 4-bit values per 32-bit word; logical column 8c+i sits in nibble
@@ -169,8 +183,9 @@ TO_API int to_awq_dequant(const int32_t* qweight, const void* scales, int s_dtyp
                    void* stream);
 /* replaces quant_awq.py:112 awq_gemm_triton: y [M,N] = x [M,K] @ dequant(W), x and y in
  * s_dtype (the facade casts x first, as the reference does), fp32 accumulation. 1-32 tokens
- * run the stream-K decode kernel (1-2 tokens on small layers the streaming GEMV), 33-128 the
- * stream-K tcgen05 kernel, larger M the tcgen05 tile GEMM. The stream-K kernels need a
+ * run the stream-K decode kernel (1-2 tokens on small layers the streaming GEMV); 33-128 tokens
+ * the stream-K tcgen05 kernel on long-K layers of few column tiles, else the register-MMA
+ * kernel or the tcgen05 tile GEMM, which takes all larger M. The stream-K kernels need a
  * workspace of to_awq_gemm_workspace_size(M, K, N, group_size) bytes (16-byte aligned; 0 when
  * no kernel for these shapes needs one) for the partial sums of column tiles split over SMs;
  * calls that share a workspace must not overlap on the GPU. */
@@ -200,8 +215,9 @@ TO_API int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void*
  * (block 2j = gate columns 8j..8j+7, block 2j + 1 = up columns 8j..8j+7; N = 2F, N % 16 == 0);
  * y[M, F] = act(gate) * up, act TO_ACT_SILU or TO_ACT_GELU_TANH, equal to to_awq_gemm on the
  * un-interleaved weights followed by the activation kernel on its two halves (each GEMM output
- * rounded to the scales' dtype first). 1-128 tokens apply it in the epilogue of the decode or
- * stream-K kernel; other shapes run the GEMM into the workspace and the activation after it.
+ * rounded to the scales' dtype first). The decode and stream-K kernels apply it in their
+ * epilogue on the shapes to_awq_gemm routes to them; other shapes run the GEMM into the
+ * workspace and the activation after it.
  * Bit for bit it is to_awq_gemm on these weights followed by the activation. The workspace is
  * to_awq_gemm_act_workspace_size(M, K, N, group_size) bytes, 16-byte aligned. */
 #define TO_ACT_SILU 0
@@ -215,8 +231,9 @@ TO_API int to_awq_gemm_act(const void* x, const int32_t* qweight, const void* sc
 /* to_awq_gemm_act on a rank's column slice (N = this rank's interleaved columns) with the
  * all-gather inside the decode kernel, as to_awq_gemm_gather: this rank's [M, N/2] activation
  * slice goes into every rank's [M, N/2 * world] output at columns [rank N/2, (rank + 1) N/2).
- * Workspace as for to_awq_gemm with the rank's (M, K, N). 1-128 tokens only; TO_EUNSUPPORTED
- * (nothing launched) otherwise: run to_awq_gemm_act and an all-gather instead. */
+ * Workspace as for to_awq_gemm with the rank's (M, K, N). Shapes of the decode and stream-K
+ * kernels only; TO_EUNSUPPORTED (nothing launched) otherwise: run to_awq_gemm_act and an
+ * all-gather instead. */
 TO_API int to_awq_gemm_act_gather(const void* x, const int32_t* qweight, const void* scales,
                                   int s_dtype, const int32_t* qzeros, void* const* y_ranks,
                                   int world, int rank, int64_t M, int64_t K, int64_t N,

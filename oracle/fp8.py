@@ -4,9 +4,12 @@ from __future__ import annotations
 
 import numpy as np
 
-from .numerics import e4m3_to_f32, f32_to_e4m3, log2_f32, rounder
+from .numerics import (e4m3_to_f32, e4m3fnuz_to_f32, f32_to_e4m3, f32_to_e4m3fnuz, log2_f32,
+                       rounder)
 
 FP8_MAX = 448.0  # torch.finfo(torch.float8_e4m3fn).max (quant_fp8.py:39-45)
+FNUZ_MAX = 240.0  # torch.finfo(torch.float8_e4m3fnuz).max: input_to_float8's bound
+FNUZ_GROUP_MAX = 224.0  # get_fp8_min_max's override for e4m3fnuz (quant_fp8.py:42-43)
 
 
 def ue8m0(scale: np.ndarray) -> np.ndarray:
@@ -19,7 +22,7 @@ def ue8m0(scale: np.ndarray) -> np.ndarray:
     return np.where(keep, s, np.ldexp(np.float32(1.0), e)).astype(np.float32)
 
 
-def input_to_float8(x_f32: np.ndarray, dtype: str):
+def input_to_float8(x_f32: np.ndarray, dtype: str, fnuz: bool = False):
     """quant_fp8.py:52-63 in ``dtype``: amax = T(max(amax, 1e-12)); s = T(T(1/amax) * 448);
     q = e4m3(clamp(T(x * s), -448, 448)); returns (codes, float32(1 / s)).
 
@@ -31,18 +34,23 @@ def input_to_float8(x_f32: np.ndarray, dtype: str):
       * float32 / float16: a NaN in the tensor makes amax, s and every product a sign-clear NaN
         (0x7F); with a numeric s, a NaN product is 0 * inf, x86's sign-set default NaN (0xFF).
         In float16, 1e-12 rounds to 0, so an all-zero tensor has s = inf and every product is
-        0 * inf."""
+        0 * inf.
+    With fnuz (dtype=torch.float8_e4m3fnuz) the bound is 240 and every NaN code is 0x80."""
     rnd = rounder(dtype)
+    fmax = np.float32(FNUZ_MAX if fnuz else FP8_MAX)
     x = rnd(np.asarray(x_f32, dtype=np.float32)).reshape(-1)
     amax = np.float32(np.max(np.abs(x)))  # NaN if any element is NaN, as aminmax
     with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
         amax = rnd(np.maximum(amax, np.float32(1e-12)))
         r = rnd(np.float32(1.0) / amax)
-        s = rnd(np.float32(r) * np.float32(FP8_MAX))
+        s = rnd(np.float32(r) * fmax)
         y = rnd(x * np.float32(s))
         nan = np.isnan(y)
-        codes = f32_to_e4m3(np.clip(np.where(nan, np.float32(0), y), -FP8_MAX, FP8_MAX))
-        if dtype == "bf16":
+        enc = f32_to_e4m3fnuz if fnuz else f32_to_e4m3
+        codes = enc(np.clip(np.where(nan, np.float32(0), y), -fmax, fmax))
+        if fnuz:
+            nan_code = np.uint8(0x80)
+        elif dtype == "bf16":
             blocked = np.arange(x.size) < (x.size // 32) * 32
             nan_code = np.where(blocked, np.uint8(0xFF), np.uint8(0x7F))
         else:
@@ -52,7 +60,7 @@ def input_to_float8(x_f32: np.ndarray, dtype: str):
 
 
 def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10, use_ue8m0: bool = False,
-                column_major: bool = False):
+                column_major: bool = False, fnuz: bool = False):
     """quant_fp8.py:66-140: scale = max(absmax, eps) / 448 [-> ue8m0];
     q = e4m3(clamp(x / scale, +-448)). Returns (codes shaped like x, scales [..., K/G]; with
     column_major, the reference's reshape-then-transpose of the flat scales).
@@ -60,21 +68,24 @@ def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10, use_ue8m
     A NaN in a group makes its absmax and scale NaN (sign clear). A NaN quotient x / scale keeps
     the sign the reference's x86 run gives it: with a NaN scale, x's own sign when x is NaN,
     else clear (0x7F); with a numeric scale (inf / inf, 0 / 0) the sign-set default NaN
-    (0xFF)."""
+    (0xFF). With fnuz (dtype=torch.float8_e4m3fnuz) the bound is 224 and every NaN code 0x80."""
+    fmax = np.float32(FNUZ_GROUP_MAX if fnuz else FP8_MAX)
     x = np.asarray(x_f32, dtype=np.float32)
     lead, k = x.shape[:-1], x.shape[-1]
     flat = x.reshape(-1, group_size)
     absmax = np.maximum(np.max(np.abs(flat), axis=-1), np.float32(eps))
-    scale = (absmax / np.float32(FP8_MAX)).astype(np.float32)
+    scale = (absmax / fmax).astype(np.float32)
     if use_ue8m0:
         scale = ue8m0(scale)
     with np.errstate(divide="ignore", invalid="ignore"):
-        y = np.clip(flat / scale[:, None], -FP8_MAX, FP8_MAX).astype(np.float32)
+        y = np.clip(flat / scale[:, None], -fmax, fmax).astype(np.float32)
     nan = np.isnan(y)
-    codes = f32_to_e4m3(np.where(nan, np.float32(0), y))
+    codes = (f32_to_e4m3fnuz if fnuz else f32_to_e4m3)(np.where(nan, np.float32(0), y))
     nan_scale = np.isnan(scale)[:, None]
     neg_nan_x = np.isnan(flat) & np.signbit(flat)
     nan_code = np.where(nan_scale & ~neg_nan_x, np.uint8(0x7F), np.uint8(0xFF))
+    if fnuz:
+        nan_code = np.uint8(0x80)
     q = np.where(nan, nan_code, codes).astype(np.uint8).reshape(*lead, k)
     if column_major:
         # quant_fp8.py:134-136: s_flat.reshape(..., G_, M).transpose(-2, -1).contiguous()
@@ -85,13 +96,14 @@ def group_quant(x_f32: np.ndarray, group_size: int, eps: float = 1e-10, use_ue8m
     return q, s
 
 
-def block_dequant(codes: np.ndarray, s: np.ndarray, block_size) -> np.ndarray:
+def block_dequant(codes: np.ndarray, s: np.ndarray, block_size, fnuz: bool = False) -> np.ndarray:
     """quant_fp8.py:143-168: y[n, k] = float32(q[n, k]) * s[n // bn, k // bk]."""
     bn, bk = block_size
     n, k = codes.shape
     rows = np.arange(n) // bn
     cols = np.arange(k) // bk
-    return (e4m3_to_f32(codes) * np.asarray(s, np.float32)[rows][:, cols]).astype(np.float32)
+    dec = e4m3fnuz_to_f32 if fnuz else e4m3_to_f32
+    return (dec(codes) * np.asarray(s, np.float32)[rows][:, cols]).astype(np.float32)
 
 
 def block_matmul(a_codes, b_codes, a_s, b_s, block_size, out_dtype: str) -> np.ndarray:

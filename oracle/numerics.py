@@ -98,6 +98,46 @@ def f32_to_e4m3(x: np.ndarray) -> np.ndarray:
     return out
 
 
+# ------------------------------------------------------------------ float8 e4m3fnuz
+def _e4m3fnuz_table() -> np.ndarray:
+    """Values of the 256 e4m3fnuz codes: exponent bias 8, subnormals m * 2^-10, no infinities,
+    no negative zero; 0x80 is the only NaN and 0x7F / 0xFF are +-240."""
+    vals = np.zeros(256, dtype=np.float32)
+    for code in range(256):
+        if code == 0x80:
+            vals[code] = np.nan
+            continue
+        s = -1.0 if code & 0x80 else 1.0
+        e = (code >> 3) & 0xF
+        m = code & 0x7
+        vals[code] = s * (m * 2.0 ** -10 if e == 0 else (1.0 + m / 8.0) * 2.0 ** (e - 8))
+    return vals
+
+
+E4M3FNUZ_VALUES = _e4m3fnuz_table()
+
+
+def e4m3fnuz_to_f32(codes: np.ndarray) -> np.ndarray:
+    return E4M3FNUZ_VALUES[np.asarray(codes, dtype=np.uint8)]
+
+
+def f32_to_e4m3fnuz(x: np.ndarray) -> np.ndarray:
+    """fp32 -> e4m3fnuz codes by round to nearest even over the code values (|x| <= 240 on
+    this path, every input is clamped first): the two neighbouring codes of |x|, the nearer
+    one, on a tie the even code; a result of zero is +0 (the encoding has no -0); NaN -> 0x80.
+    torch's CPU cast gives the same codes (pinned in the tests)."""
+    x = np.asarray(x, dtype=np.float32)
+    a = np.abs(x).astype(np.float64)
+    pos = E4M3FNUZ_VALUES[:128].astype(np.float64)  # ascending with the code
+    hi = np.clip(np.searchsorted(pos, a, side="left"), 1, 127)
+    lo = hi - 1
+    d_lo, d_hi = a - pos[lo], pos[hi] - a
+    code = np.where((d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0)), hi, lo).astype(np.int64)
+    sign = np.where(np.signbit(x) & (code != 0), 0x80, 0)
+    out = (code | sign).astype(np.uint8)
+    return np.where(np.isnan(x), np.uint8(0x80), out).astype(np.uint8)
+
+
 def log2_f32(x: np.ndarray) -> np.ndarray:
     """log2 rounded to fp32 (evaluated in float64, then rounded once)."""
     return np.log2(np.asarray(x, dtype=np.float64)).astype(np.float32)

@@ -20,6 +20,7 @@ _TORCH_DTYPES = {
     "float16": torch.float16,
     "bfloat16": torch.bfloat16,
     "float8_e4m3fn": torch.float8_e4m3fn,
+    "float8_e4m3fnuz": torch.float8_e4m3fnuz,
     "int8": torch.int8,
     "int32": torch.int32,
     "int64": torch.int64,
@@ -39,8 +40,8 @@ class GoldenCase(dict):
         if dt is None:
             return torch.from_numpy(np.array(arr)).to(device)
         dt = _TORCH_DTYPES[str(dt)]
-        if dt == torch.float8_e4m3fn:
-            return torch.from_numpy(np.array(arr, dtype=np.uint8)).view(torch.float8_e4m3fn).to(device)
+        if dt in (torch.float8_e4m3fn, torch.float8_e4m3fnuz):
+            return torch.from_numpy(np.array(arr, dtype=np.uint8)).view(dt).to(device)
         if dt == torch.bfloat16:
             # bf16 values are stored as their exact fp32 values: keep the top 16 bits, so a NaN
             # keeps its sign (torch's vectorised fp32 -> bf16 cast would rewrite it)

@@ -4,8 +4,8 @@ on seeded CPU inputs.
 
     TILEOPS_REF=<path to a TileOps checkout> python tests/golden/make_golden.py
 
-Writes awq.npz, int8.npz, fp8.npz, sym.npz, fused.npz (or only the files named on the command
-line: awq, int8, fp8, sym, fused). Each case stores its inputs and the reference's
+Writes awq.npz, int8.npz, fp8.npz, fnuz.npz, sym.npz, fused.npz (or only the files named on the
+command line: awq, int8, fp8, fnuz, sym, fused). Each case stores its inputs and the reference's
 outputs; float tensors are stored as float32 values (bf16/fp16 values are exact in fp32)
 with the source dtype under "<case>/<field>.dtype", FP8 tensors as uint8 codes. The
 symmetric-INT8 ops have no CPU path in the reference (its TileLang kernels need a GPU
@@ -42,6 +42,7 @@ import tileops.quant_int8 as i8  # noqa: E402
 assert Path(tileops.__file__).resolve().is_relative_to(REF.resolve()), tileops.__file__
 
 FP8 = torch.float8_e4m3fn
+FNUZ = torch.float8_e4m3fnuz
 
 
 class Cases:
@@ -52,7 +53,7 @@ class Cases:
         key = f"{case}/{field}"
         if isinstance(t, torch.Tensor):
             dt = str(t.dtype).replace("torch.", "")
-            if t.dtype == FP8:
+            if t.dtype in (FP8, FNUZ):
                 arr = t.contiguous().view(torch.uint8).numpy().copy()
             elif t.dtype in (torch.bfloat16, torch.float16):
                 arr = t.float().numpy().copy()
@@ -575,9 +576,67 @@ def make_fused() -> None:
     c.save("fused.npz")
 
 
+# ------------------------------------------------------------------ FP8 e4m3fnuz
+def make_fnuz() -> None:
+    """The FP8 quantisers with dtype=torch.float8_e4m3fnuz: tensor-wide to +-240 (finfo), per
+    group to get_fp8_min_max's +-224, every NaN code 0x80; block_dequant of fnuz codes."""
+    c = Cases()
+    for i, dt in enumerate((torch.float32, torch.float16, torch.bfloat16)):
+        tag = str(dt).replace("torch.", "")
+        seed(300 + i)
+        x = (torch.randn(4000) * 3.0).to(dt)
+        q, s = fp8.input_to_float8(x, dtype=FNUZ)
+        c.put(f"input_{tag}", "x", x)
+        c.put(f"input_{tag}", "q", q)
+        c.put(f"input_{tag}", "s", s)
+        x = torch.randn(100).to(dt)
+        x[5] = float("nan")
+        q, s = fp8.input_to_float8(x, dtype=FNUZ)
+        c.put(f"input_nan_{tag}", "x", x)
+        c.put(f"input_nan_{tag}", "q", q)
+        c.put(f"input_nan_{tag}", "s", s)
+        x = torch.zeros(40, dtype=dt)
+        q, s = fp8.input_to_float8(x, dtype=FNUZ)
+        c.put(f"input_zeros_{tag}", "x", x)
+        c.put(f"input_zeros_{tag}", "q", q)
+        c.put(f"input_zeros_{tag}", "s", s)
+        for ue in (False, True):
+            seed(310 + i)
+            x = torch.randn(6, 256).to(dt)
+            x[2, 7] = float("nan")
+            x[4, 100] = float("inf")
+            x[5, :] = 0.0
+            q, s = fp8.per_token_group_quant_fp8(x, 64, dtype=FNUZ, use_ue8m0=ue)
+            name = f"group_{tag}" + ("_ue8m0" if ue else "")
+            c.put(name, "x", x)
+            c.put(name, "group_size", np.array(64))
+            c.put(name, "ue8m0", np.array(ue))
+            c.put(name, "column_major", np.array(False))
+            c.put(name, "q", q)
+            c.put(name, "s", s)
+    seed(320)
+    x = torch.randn(4, 32)
+    q, s = fp8.per_token_group_quant_fp8(x, 8, dtype=FNUZ, column_major_scales=True)
+    c.put("group_colmajor", "x", x)
+    c.put("group_colmajor", "group_size", np.array(8))
+    c.put("group_colmajor", "ue8m0", np.array(False))
+    c.put("group_colmajor", "column_major", np.array(True))
+    c.put("group_colmajor", "q", q)
+    c.put("group_colmajor", "s", s)
+    seed(321)
+    bs = [4, 8]
+    wq = (torch.randn(10, 24) * 60).clamp(-240, 240).to(FNUZ)
+    ws = torch.rand(3, 3) * 0.1 + 0.01
+    c.put("block_dequant", "q", wq)
+    c.put("block_dequant", "s", ws)
+    c.put("block_dequant", "block", np.array(bs))
+    c.put("block_dequant", "y", fp8.block_dequant(wq, ws, bs))
+    c.save("fnuz.npz")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(1)
-    makers = {"awq": make_awq, "int8": make_int8, "fp8": make_fp8, "sym": make_sym,
-              "fused": make_fused}
+    makers = {"awq": make_awq, "int8": make_int8, "fp8": make_fp8, "fnuz": make_fnuz,
+              "sym": make_sym, "fused": make_fused}
     for name in sys.argv[1:] or list(makers):
         makers[name]()

@@ -10,6 +10,7 @@ import torch
 import tileops_b200 as tob
 from oracle import fp8 as ofp8
 from oracle import int8 as oi8
+from oracle import numerics
 from oracle import sym as osym
 
 pytestmark = pytest.mark.gpu
@@ -18,7 +19,7 @@ _DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 
 
 def _codes(t: torch.Tensor) -> np.ndarray:
-    if t.dtype == torch.float8_e4m3fn:
+    if t.dtype in (torch.float8_e4m3fn, torch.float8_e4m3fnuz):
         return t.view(torch.uint8).cpu().numpy()
     return t.cpu().numpy()
 
@@ -295,3 +296,70 @@ def test_block_dequant_vs_oracle(cuda, n, k, bn, bk):
     y = tob.block_dequant_fp8(qf.to(cuda), s.to(cuda), [bn, bk])
     want = ofp8.block_dequant(qf.view(torch.uint8).numpy(), s.numpy(), (bn, bk))
     assert np.array_equal(y.cpu().numpy(), want)
+
+
+# ------------------------------------------------------------------ FP8 e4m3fnuz codes
+_FNUZ = torch.float8_e4m3fnuz
+_FNUZ_DT = ("float32", "float16", "bfloat16")
+
+
+@pytest.mark.parametrize("name", [f"input_{k}{dt}" for k in ("", "nan_", "zeros_")
+                                  for dt in _FNUZ_DT])
+def test_input_to_float8_fnuz_golden(cuda, golden, name):
+    c = golden("fnuz.npz")[name]
+    q, s = tob.input_to_float8(c.tensor("x", cuda), dtype=_FNUZ)
+    assert q.dtype == _FNUZ
+    assert np.array_equal(_codes(q), c["q"])
+    assert _same(s, c["s"])
+
+
+@pytest.mark.parametrize("name", [f"group_{dt}{u}" for dt in _FNUZ_DT for u in ("", "_ue8m0")]
+                         + ["group_colmajor"])
+def test_per_token_group_quant_fp8_fnuz_golden(cuda, golden, name):
+    c = golden("fnuz.npz")[name]
+    q, s = tob.per_token_group_quant_fp8(c.tensor("x", cuda), int(c["group_size"]), dtype=_FNUZ,
+                                         column_major_scales=bool(c["column_major"]),
+                                         use_ue8m0=bool(c["ue8m0"]))
+    assert q.dtype == _FNUZ
+    assert np.array_equal(_codes(q), c["q"])
+    assert _same(s, c["s"])
+
+
+def test_block_dequant_fnuz_golden(cuda, golden):
+    c = golden("fnuz.npz")["block_dequant"]
+    y = tob.block_dequant_fp8(c.tensor("q", cuda), c.tensor("s", cuda),
+                              [int(v) for v in c["block"]])
+    assert np.array_equal(y.cpu().numpy(), c["y"])
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("n", [37, 4099, (1 << 20) + 13])
+def test_fnuz_quantisers_vs_oracle(cuda, dtype, n):
+    """Both e4m3fnuz quantisers against the oracle, with NaN and inf inside (every NaN code
+    0x80), and every code decoded back by block_dequant."""
+    g = torch.Generator().manual_seed(n + 17)
+    x = (torch.randn(n, generator=g) * 9).to(_DT[dtype])
+    x[torch.randint(0, n, (2,), generator=g)] = float("nan")
+    x[torch.randint(0, n, (1,), generator=g)] = float("inf")
+    q, s = tob.input_to_float8(x.to(cuda), dtype=_FNUZ)
+    wq, ws = ofp8.input_to_float8(_f(x), dtype, fnuz=True)
+    assert np.array_equal(_codes(q), wq)
+    assert _same(s, ws)
+    x2 = x[: (n // 16) * 16].view(-1, 16) if n >= 16 else x.view(1, -1)
+    g2 = x2.shape[-1]
+    for ue8m0 in (False, True):
+        q, s = tob.per_token_group_quant_fp8(x2.to(cuda), g2, dtype=_FNUZ, use_ue8m0=ue8m0)
+        wq, ws = ofp8.group_quant(_f(x2), g2, use_ue8m0=ue8m0, fnuz=True)
+        assert np.array_equal(_codes(q), wq)
+        assert _same(s, ws)
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8).view(1, 256)
+    y = tob.block_dequant_fp8(codes.view(_FNUZ).to(cuda), torch.ones(1, 1, device=cuda),
+                              [1, 256])
+    assert _same(y.cpu().numpy().reshape(-1), numerics.e4m3fnuz_to_f32(np.arange(256)))
+
+
+def test_fnuz_gemm_rejected(cuda):
+    a = torch.zeros(4, 16, device=cuda).to(_FNUZ)
+    s = torch.ones(4, 1, device=cuda)
+    with pytest.raises(NotImplementedError):
+        tob.w8a8_block_fp8_matmul(a, a, s, s, [16, 16])

@@ -71,6 +71,22 @@ def _worker(rank, world, port, q):
                 float(np.abs(want).max()),
             )
         layer.close()
+        # a long-K layer at 40 tokens: the stream-K tensor-core kernel gathers
+        k2 = 8192
+        w2 = torch.randint(0, 16, (k2, n), generator=g)
+        z2 = torch.randint(0, 16, (k2 // gs, n), generator=g)
+        s2 = ((torch.rand(k2 // gs, n, generator=g) * 0.018 + 0.002).bfloat16()).to(dev)
+        qw2 = torch.from_numpy(oawq.pack(w2.numpy())).to(dev)
+        qz2 = torch.from_numpy(oawq.pack(z2.numpy())).to(dev)
+        layer2 = sharded.ShardedAWQLinear(qw2, s2, qz2)
+        x = torch.randn(40, k2, generator=g).bfloat16().to(dev)
+        full = tob.awq_gemm(x, qw2, s2, qz2, 1)
+        y1 = layer2.gathered(x).clone()
+        y2 = layer2.gathered(x)
+        torch.cuda.synchronize()
+        report["sk40"] = (float((y1.float() - full.float()).abs().max()), bool(torch.equal(y1, y2)),
+                          0.0, float(full.float().abs().max()))
+        layer2.close()
         # gate_up with silu_and_mul in the decode kernel, gathered: this rank's slice of the
         # interleaved weights holds gate and up blocks of the same columns
         qw_i, s_i, qz_i = tob.awq_interleave_gate_up(qw, s, qz)

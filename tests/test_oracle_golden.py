@@ -6,6 +6,7 @@ from __future__ import annotations
 
 import numpy as np
 import pytest
+import torch
 
 from oracle import awq, fp8, fused, int8, numerics, sym
 
@@ -184,6 +185,49 @@ def test_block_dequant_fp8(golden):
     c = golden("fp8.npz")["block_dequant"]
     y = fp8.block_dequant(_np(c, "q"), _np(c, "s"), list(_np(c, "block")))
     assert np.array_equal(y, _np(c, "y"))
+
+
+_FNUZ_DT = ("float32", "float16", "bfloat16")
+
+
+@pytest.mark.parametrize("name", [f"input_{k}{dt}" for k in ("", "nan_", "zeros_")
+                                  for dt in _FNUZ_DT])
+def test_input_to_float8_fnuz(golden, name):
+    c = golden("fnuz.npz")[name]
+    q, s = fp8.input_to_float8(_np(c, "x"), c.dtype_name("x"), fnuz=True)
+    assert np.array_equal(q, _np(c, "q"))
+    assert _same(s, _np(c, "s"))
+
+
+@pytest.mark.parametrize("name", [f"group_{dt}{u}" for dt in _FNUZ_DT for u in ("", "_ue8m0")]
+                         + ["group_colmajor"])
+def test_group_quant_fp8_fnuz(golden, name):
+    c = golden("fnuz.npz")[name]
+    q, s = fp8.group_quant(_np(c, "x"), int(c["group_size"]), use_ue8m0=bool(c["ue8m0"]),
+                           column_major=bool(c["column_major"]), fnuz=True)
+    assert np.array_equal(q, _np(c, "q"))
+    assert _same(s, _np(c, "s"))
+
+
+def test_block_dequant_fp8_fnuz(golden):
+    c = golden("fnuz.npz")["block_dequant"]
+    y = fp8.block_dequant(_np(c, "q"), _np(c, "s"), list(_np(c, "block")), fnuz=True)
+    assert np.array_equal(y, _np(c, "y"))
+
+
+def test_fnuz_encoding_matches_torch():
+    """The oracle's e4m3fnuz rounding against torch's CPU cast (the reference's conversion),
+    over ties, subnormals, zero signs and the top of the range."""
+    g = torch.Generator().manual_seed(7)
+    x = torch.cat([torch.randn(50000, generator=g) * 40, torch.randn(20000, generator=g) * 1e-3,
+                   torch.linspace(-240, 240, 48001),
+                   torch.tensor([0.0, -0.0, 232.0, -232.0, 2.0 ** -11, -2.0 ** -11])])
+    x = x.clamp(-240, 240)
+    want = x.to(torch.float8_e4m3fnuz).view(torch.uint8).numpy()
+    assert np.array_equal(numerics.f32_to_e4m3fnuz(x.numpy()), want)
+    codes = np.arange(256, dtype=np.uint8)
+    back = torch.from_numpy(codes).view(torch.float8_e4m3fnuz).float().numpy()
+    assert _same(numerics.e4m3fnuz_to_f32(codes), back)
 
 
 def test_w8a8_fp8(golden):

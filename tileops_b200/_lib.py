@@ -55,11 +55,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_input_quant_workspace_size": (_S, []),
     "to_input_to_int8": (_I, [_P, _I, _L, _P, _P, _P, _S, _P]),
     "to_input_to_fp8": (_I, [_P, _I, _L, _P, _P, _P, _S, _P]),
+    "to_input_to_fp8_fnuz": (_I, [_P, _I, _L, _P, _P, _P, _S, _P]),
     "to_input_to_fp8_noalloc": (_I, [_P, _I, _L, _P, _P, _P]),
     "to_per_token_group_quant_i8": (_I, [_P, _I, _L, _L, _F, _P, _P, _P]),
     "to_per_token_group_quant_fp8": (_I, [_P, _I, _L, _L, _F, _I, _L, _L, _P, _P, _P]),
+    "to_per_token_group_quant_fp8_fnuz": (_I, [_P, _I, _L, _L, _F, _I, _L, _L, _P, _P, _P]),
     "to_block_dequant_i8": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),
     "to_block_dequant_fp8": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),
+    "to_block_dequant_fp8_fnuz": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),
     "to_awq_pack": (_I, [_P, _I, _P, _L, _L, _P]),
     "to_awq_unpack": (_I, [_P, _I, _P, _L, _L, _P]),
     "to_awq_dequant": (_I, [_P, _P, _I, _P, _P, _L, _L, _L, _P]),

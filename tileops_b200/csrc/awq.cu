@@ -679,18 +679,23 @@ bool decode_enabled() {
   return on;
 }
 
-// Token counts the stream-K tensor-core kernel takes: 33-128 (below, the decode kernel's
-// register-operand MMAs stream faster). Measurement switch TOB_AWQ_SK: "0" off, "all" for every
-// M <= 128.
+// Shapes the stream-K tensor-core kernel takes: 33-128 tokens on layers of long K (>= 8192)
+// and few 256-column tiles (<= 32), where the tile GEMM leaves most SMs idle for the whole K and
+// the register-MMA kernel runs out of token tiles. Measured on the 4096 x 14336 down projection:
+// 57 us at M = 64 (register-MMA kernel 82 us) and 90 us at M = 128 (tile GEMM 131 us). On the
+// other decode layers it is slower than both: each SM expands one 64 x 256 weight block per
+// ~1.2 us, so its rate stays near 1.1 TB/s (below, the decode kernel's register-operand MMAs
+// stream faster). Measurement switch TOB_AWQ_SK: "0" never, "all" for every M <= 128.
 constexpr int64_t kSkMinM = 33, kSkMaxM = 128;
-bool sk_wanted(int64_t M) {
+bool sk_wanted(int64_t M, int64_t K, int64_t N) {
   static const int mode = [] {
     const char* v = tuning_env("TOB_AWQ_SK");
     if (v == nullptr) return 1;
     return v[0] == '0' ? 0 : (v[0] == 'a' ? 2 : 1);
   }();
   if (mode == 0 || M > kSkMaxM) return false;
-  return mode == 2 || M >= kSkMinM;
+  if (mode == 2) return true;
+  return M >= kSkMinM && K >= 8192 && ceil_div(N, 256) <= 32;
 }
 
 // Used by the tensor-core GEMM translation unit when it must stream small M.
@@ -772,7 +777,7 @@ int to_awq_dequant(const int32_t* qweight, const void* scales, int s_dtype, cons
 size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_t group_size) {
   if (M <= 0 || K <= 0 || N <= 0 || group_size <= 0 || N % 8 != 0 || K % group_size != 0)
     return 0;
-  if (sk_wanted(M)) return awq_sk_workspace(M, K, N, group_size, TO_F16);
+  if (sk_wanted(M, K, N)) return awq_sk_workspace(M, K, N, group_size, TO_F16);
   if (!decode_enabled()) return 0;
   return awq_decode_workspace(M, K, N, group_size, TO_F16);
 }
@@ -789,7 +794,7 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
   // GEMM; 33 <= M <= 64 on the TMA-fed register-MMA kernel when the tcgen05 tiles would leave
   // most SMs idle; the shapes none of them takes (ragged N, unaligned rows) on the streaming
   // SIMT kernels.
-  if (sk_wanted(M)) {
+  if (sk_wanted(M, K, N)) {
     rc = awq_sk_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size, workspace,
                        workspace_bytes, (cudaStream_t)stream, -1);
     if (rc != TO_EUNSUPPORTED) return rc;
@@ -816,7 +821,7 @@ int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s
                            (cudaStream_t)stream);
 }
 
-// The gate_up linear with its activation: the decode (1-32 tokens) and stream-K (33-128) kernels
+// The gate_up linear with its activation: the decode and stream-K kernels
 // apply it in their epilogue, on the shapes to_awq_gemm routes to them; other shapes run
 // to_awq_gemm into the front of the workspace ([M, N] in the scales' dtype, 256-byte aligned
 // size) and the activation over it. Either way the result is to_awq_gemm's output on these
@@ -853,7 +858,7 @@ int to_awq_gemm_act(const void* x, const int32_t* qweight, const void* scales, i
   char* tmp = static_cast<char*>(workspace);
   char* gemm_ws = tmp + act_tmp_bytes(M, N);
   const size_t gemm_ws_bytes = workspace_bytes - act_tmp_bytes(M, N);
-  if (sk_wanted(M)) {
+  if (sk_wanted(M, K, N)) {
     rc = awq_sk_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size, gemm_ws,
                        gemm_ws_bytes, st, act);
     if (rc != TO_EUNSUPPORTED) return rc;
@@ -887,7 +892,7 @@ int to_awq_gemm_act_gather(const void* x, const int32_t* qweight, const void* sc
   if (!aligned16(scales) || !aligned16(x))
     return fail(TO_EINVAL, "awq_gemm_act_gather: x and scales must be 16-byte aligned");
   rc = TO_EUNSUPPORTED;
-  if (sk_wanted(M))
+  if (sk_wanted(M, K, N))
     rc = awq_sk_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M, K, N,
                               group_size, workspace, workspace_bytes, (cudaStream_t)stream, act);
   else if (M <= 32 && decode_enabled())
@@ -896,8 +901,8 @@ int to_awq_gemm_act_gather(const void* x, const int32_t* qweight, const void* sc
                                   (cudaStream_t)stream, act);
   if (rc == TO_EUNSUPPORTED)
     return fail(TO_EUNSUPPORTED,
-                "awq_gemm_act_gather: only the decode and stream-K kernels (1-128 tokens) gather "
-                "the activation; run to_awq_gemm_act and an all-gather instead");
+                "awq_gemm_act_gather: only the decode and stream-K kernels gather the activation; "
+                "run to_awq_gemm_act and an all-gather instead");
   return rc;
 }
 
@@ -918,7 +923,7 @@ int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales
   // Decode-sized M on the stream-K decode kernel, the rest on the tensor-core GEMM; both store
   // each finished tile into every rank's output.
   rc = TO_EUNSUPPORTED;
-  if (sk_wanted(M))
+  if (sk_wanted(M, K, N))
     rc = awq_sk_gather_launch(x, qweight, scales, s_dtype, qzeros, y_ranks, world, rank, M, K, N,
                               group_size, workspace, workspace_bytes, (cudaStream_t)stream, -1);
   else if (M <= 32 && decode_enabled())

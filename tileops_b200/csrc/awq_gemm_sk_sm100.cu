@@ -20,7 +20,10 @@
 //     layer). The owner reaches that tile at the end of its range and the other CTAs at the
 //     start of theirs, so its wait is short; every wait is bounded.
 // Roles (448 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 expansion, warps 10-13
-// epilogue.
+// epilogue. Each SM expands about one 64 x 256 block per 1.2 us here (tensor pipe ~30 % busy,
+// 0.4 eligible warps per scheduler), so the kernel pays off only where the alternatives leave
+// SMs idle for a long K: the dispatch (awq.cu) sends it 33-128 tokens on layers of K >= 8192 and
+// at most 32 column tiles.
 #include <string.h>
 
 #include <algorithm>
@@ -57,6 +60,10 @@ constexpr uint32_t kSkBLbo = 8192, kSkBSbo = 1024;
 constexpr int kSkRowStep = (32 * kSkDqWarps) / kSkWords;    // 8 rows apart per thread
 constexpr int kSkRowsPer = kSkBK / kSkRowStep;              // 8 rows per thread
 constexpr int kSkMaxOut = 8;
+// Row stride (floats) of the owner's sum of the later parts in shared memory: 16 bytes of
+// padding per row, so a warp's lanes (one row each) read the same columns conflict-free.
+constexpr int kSkRedLd = kSkBN + 4;
+static_assert(128 * kSkRedLd * 4 <= kSkStages * kSkStageBytes, "owner sums fit in the ring");
 static_assert(kSkSmem <= 232448, "shared memory");
 static_assert(kSkStageBytes % 1024 == 0, "stages keep the 1 KB alignment of the swizzled x");
 
@@ -112,7 +119,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   uint64_t* tfull = bfree + kSkBBufs;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* redbar = drain + 1;  // the epilogue threads' sums of later parts are in place
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(redbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   auto sA = [&](int s) { return stage0 + (size_t)s * kSkStageBytes; };
   auto sW = [&](int s) { return stage0 + (size_t)s * kSkStageBytes + kSkABytes; };
@@ -139,6 +147,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       mbar_init(tempty + b, 4);
     }
     mbar_init(drain, 1);
+    mbar_init(redbar, 128);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmX);
@@ -346,14 +355,19 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         __syncwarp();
         if (lane == 0) sk_st_release(flags + ((size_t)cur_t * maxc + slot) * 4 + q, epoch);
       } else {
-        // The owner: wait for the later parts, add them in K order, store.
+        // The owner. Later parts exist (nc > 0) only in this CTA's last part, when its stage
+        // ring is idle: wait for their flags, then the four epilogue warps add them column-
+        // parallel (thread e takes float4 e, e + 128, ... of the [M, 256] tile, the
+        // contributors' values of one float4 loaded together and added in K order) into
+        // shared memory, and each lane adds its row of that sum to its own TMEM row.
         const int nc = (int)(sk_cta_of((int64_t)cur_t * kbn + kbn - 1, units, gridDim.x) - owner);
-        unsigned long long* fl = flags + (size_t)cur_t * maxc * 4 + q;
+        unsigned long long* fl = flags + (size_t)cur_t * maxc * 4;
+        float* red = reinterpret_cast<float*>(stage0);
         if (nc > 0) {
           const uint64_t t0 = globaltimer_ns();
           while (true) {
             bool mine = true;
-            for (int c = lane; c < nc; c += 32) mine &= sk_ld_relaxed(fl + 4 * c) == epoch;
+            for (int c = lane; c < 4 * nc; c += 32) mine &= sk_ld_relaxed(fl + c) == epoch;
             if (__all_sync(0xffffffffu, mine)) break;
             if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
               if (!*abort_flag) {
@@ -365,8 +379,40 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             }
           }
           __threadfence();
+          fence_proxy_async_smem();  // the ring's last TMA writes are ordered before these
+          if (ok) {
+            const int e = threadIdx.x - kSkEpiWarp0 * 32;
+            const float* src0 = part + (size_t)cur_t * maxc * slab;
+            const int nf = M * (kSkBN / 4);
+            const int cols = min(kSkBN, N - cur_t * kSkBN);
+            for (int f = e; f < nf; f += 128) {
+              const int mm = f / (kSkBN / 4), c4 = f % (kSkBN / 4);
+              if (c4 * 4 >= cols) continue;
+              const float4* src = reinterpret_cast<const float4*>(src0) + f;
+              const size_t cs = slab / 4;  // float4s per part
+              float4 acc = src[0];
+              int c = 1;
+              for (; c + 3 < nc; c += 4) {
+                const float4 a0 = src[c * cs], a1 = src[(c + 1) * cs], a2 = src[(c + 2) * cs],
+                             a3 = src[(c + 3) * cs];
+                acc.x = (((acc.x + a0.x) + a1.x) + a2.x) + a3.x;
+                acc.y = (((acc.y + a0.y) + a1.y) + a2.y) + a3.y;
+                acc.z = (((acc.z + a0.z) + a1.z) + a2.z) + a3.z;
+                acc.w = (((acc.w + a0.w) + a1.w) + a2.w) + a3.w;
+              }
+              for (; c < nc; ++c) {
+                const float4 a = src[c * cs];
+                acc.x += a.x;
+                acc.y += a.y;
+                acc.z += a.z;
+                acc.w += a.w;
+              }
+              *reinterpret_cast<float4*>(red + (size_t)mm * kSkRedLd + c4 * 4) = acc;
+            }
+          }
+          mbar_arrive(redbar);  // every epilogue thread, once per launch
+          if (!mbar_wait(redbar, 0, abort_flag, err)) ok = false;
         }
-        const float* src0 = part + (size_t)cur_t * maxc * slab + (size_t)m * kSkBN;
 #pragma unroll 1
         for (int c0 = 0; ok && c0 < kSkBN; c0 += 32) {
           uint32_t r[32];
@@ -379,18 +425,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-#pragma unroll 1
-          for (int c = 0; c < nc; ++c) {
-            const float4* src = reinterpret_cast<const float4*>(src0 + (size_t)c * slab + c0);
-            float4 a[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] = src[j];
+          if (nc > 0) {
+            const float4* rs = reinterpret_cast<const float4*>(red + (size_t)m * kSkRedLd + c0);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              v[4 * j] += a[j].x;
-              v[4 * j + 1] += a[j].y;
-              v[4 * j + 2] += a[j].z;
-              v[4 * j + 3] += a[j].w;
+              const float4 a = rs[j];
+              v[4 * j] += a.x;
+              v[4 * j + 1] += a.y;
+              v[4 * j + 2] += a.z;
+              v[4 * j + 3] += a.w;
             }
           }
           if (out.act < 0) {
@@ -425,7 +468,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           }
         }
         __syncwarp();
-        for (int c = lane; c < nc; c += 32) fl[4 * c] = 0ull;  // ready for the next launch
+        if (q == 0)
+          for (int c = lane; c < 4 * nc; c += 32) fl[c] = 0ull;  // ready for the next launch
       }
       tc_fence_before();
       __syncwarp();

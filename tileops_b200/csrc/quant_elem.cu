@@ -162,6 +162,27 @@ __device__ __forceinline__ float ue8m0_round(float s) {
   return ldexpf(1.0f, (int)ceilf(l));
 }
 
+// Output codes of the quantisers: int8, OCP float8_e4m3fn, or float8_e4m3fnuz (the encoding
+// with exponent bias 8, no infinities, no negative zero and one NaN, 0x80; the reference's
+// `dtype` argument accepts it, tileops/quant_fp8.py:19-45).
+enum QKind : int { kQI8 = 0, kQE4M3 = 1, kQE4M3Fnuz = 2 };
+
+// fp32 -> e4m3fnuz, round to nearest even, for |v| <= 240 (the quantisers clamp first). The
+// fnuz grid is the e4m3fn grid halved (bias 8 against 7, same mantissa), so the code is the
+// e4m3fn code of 2v, except: above 232 (the tie between 224 and 240) the nearest fnuz value is
+// 240, code 0x7F, which e4m3fn spends on NaN; and e4m3fn's -0 (0x80) is fnuz's NaN, so a
+// result of zero is +0.
+__device__ __forceinline__ uint8_t f32_to_e4m3fnuz(float v) {
+  uint8_t b = f32_to_e4m3(2.0f * v);
+  if (fabsf(v) > 232.0f) b = (uint8_t)(((__float_as_uint(v) >> 24) & 0x80u) | 0x7Fu);
+  return b == 0x80 ? (uint8_t)0 : b;
+}
+__device__ __forceinline__ float e4m3fnuz_to_f32(uint8_t b) {
+  if (b == 0x80) return __uint_as_float(0x7FC00000u);
+  if ((b & 0x7F) == 0x7F) return (b & 0x80) ? -240.0f : 240.0f;
+  return 0.5f * e4m3_to_f32(b);
+}
+
 // e4m3 code of a NaN quotient x / scale, as the reference's fp32 division and cast produce it
 // on the x86 host it is pinned to: with a NaN scale (a NaN in the group) the quotient is the
 // NaN operand that comes first -- x itself when x is NaN, else the scale's sign-clear NaN --
@@ -179,7 +200,7 @@ __device__ __forceinline__ bool sign_of(float v) { return __float_as_uint(v) >> 
 __device__ __forceinline__ bool sign_of(__half v) { return __half_as_ushort(v) >> 15; }
 __device__ __forceinline__ bool sign_of(__nv_bfloat16 v) { return __bfloat16_as_ushort(v) >> 15; }
 
-template <typename T, bool FP8, int V, int MAXV>
+template <typename T, int Q, int V, int MAXV>
 __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
                                                      uint8_t* __restrict__ qout,
                                                      float* __restrict__ scales, int64_t n_groups,
@@ -191,7 +212,9 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
   const int team_id = threadIdx.x >> team_log2;
   const int nvec = G / V;
   __shared__ unsigned red[32];
-  const float qmax = FP8 ? 448.0f : 127.0f;
+  constexpr bool FP8 = Q != kQI8;
+  // clamp bounds: int8 127; e4m3fn 448; e4m3fnuz 224 (get_fp8_min_max's override)
+  const float qmax = Q == kQE4M3 ? 448.0f : (Q == kQE4M3Fnuz ? 224.0f : 127.0f);
 
   for (int64_t g0 = (int64_t)blockIdx.x * teams_per_cta; g0 < n_groups;
        g0 += (int64_t)gridDim.x * teams_per_cta) {
@@ -241,9 +264,11 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
       for (int j = 0; j < V; ++j) {
         const float xv = to_f32(t.v[j]);
         const float y = __fdiv_rn(xv, scale);
-        if (FP8) {
+        if (Q == kQE4M3) {
           o.v[j] = isnan(y) ? nan_code_div(xv, sign_of(t.v[j]), nan_group)
                             : f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
+        } else if (Q == kQE4M3Fnuz) {
+          o.v[j] = isnan(y) ? (uint8_t)0x80 : f32_to_e4m3fnuz(fminf(fmaxf(y, -224.f), 224.f));
         } else {
           o.v[j] = (uint8_t)rne_clamp_i8(y);
         }
@@ -260,7 +285,7 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
   }
 }
 
-template <typename T, bool FP8>
+template <typename T, int Q>
 int launch_group_quant(const void* x, int64_t n_groups, int64_t G, float eps, int ue8m0,
                        ScaleLayout sl, void* q, float* scales, cudaStream_t st) {
   constexpr int VV = 16 / sizeof(T);
@@ -279,12 +304,12 @@ int launch_group_quant(const void* x, int64_t n_groups, int64_t G, float eps, in
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   if (vec)
-    k_group_quant<T, FP8, VV, 4><<<(unsigned)blocks, threads, 0, st>>>(
+    k_group_quant<T, Q, VV, 4><<<(unsigned)blocks, threads, 0, st>>>(
         (const T*)x, (uint8_t*)q, scales, n_groups, (int)G, team_log2, eps, ue8m0, sl);
   else
-    k_group_quant<T, FP8, 1, 8><<<(unsigned)blocks, threads, 0, st>>>(
+    k_group_quant<T, Q, 1, 8><<<(unsigned)blocks, threads, 0, st>>>(
         (const T*)x, (uint8_t*)q, scales, n_groups, (int)G, team_log2, eps, ue8m0, sl);
-  return check_launch(FP8 ? "per_token_group_quant_fp8" : "per_token_group_quant_int8");
+  return check_launch(Q != kQI8 ? "per_token_group_quant_fp8" : "per_token_group_quant_int8");
 }
 
 // ------------------------------------------------------------------ tensor-wide dynamic quant
@@ -331,13 +356,15 @@ __device__ __forceinline__ uint8_t nan_code_mul(int64_t i, int64_t n_blocked, bo
 // the int8 cast makes them 0, the e4m3 cast a NaN code (nan_code_mul). In float16 the 1e-12
 // floor rounds to 0, so an all-zero tensor has s = inf and NaN products 0 * inf.
 // The int8 cast truncates toward zero (torch .to(int8)); the fp8 cast rounds to nearest even.
-template <typename T, bool FP8, int V>
+template <typename T, int Q, int V>
 __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__ x, int64_t n,
                                                           const unsigned* __restrict__ amax_bits,
                                                           uint8_t* __restrict__ q,
                                                           float* __restrict__ dq_scale) {
-  const float qmax = FP8 ? 448.0f : 127.0f;
-  const float qmin = FP8 ? -448.0f : -128.0f;
+  constexpr bool FP8 = Q != kQI8;
+  // finfo bounds: int8 [-128, 127]; e4m3fn +-448; e4m3fnuz +-240
+  const float qmax = Q == kQE4M3 ? 448.0f : (Q == kQE4M3Fnuz ? 240.0f : 127.0f);
+  const float qmin = Q == kQE4M3 ? -448.0f : (Q == kQE4M3Fnuz ? -240.0f : -128.0f);
   const float amax_raw = __uint_as_float(*amax_bits);
   const bool nan_scale = isnan(amax_raw);
   const float amax = nan_scale ? amax_raw : round_to<T>(fmaxf(amax_raw, 1e-12f));
@@ -347,8 +374,12 @@ __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__
   if (blockIdx.x == 0 && threadIdx.x == 0) *dq_scale = __frcp_rn(s);
   auto quant1 = [&](float xv, int64_t i) -> uint8_t {
     float y = round_to<T>(__fmul_rn(xv, s));
-    if (isnan(y)) return FP8 ? nan_code_mul<T>(i, n_blocked, nan_scale) : (uint8_t)0;
+    if (isnan(y)) {
+      if (Q == kQE4M3Fnuz) return (uint8_t)0x80;  // fnuz's only NaN
+      return FP8 ? nan_code_mul<T>(i, n_blocked, nan_scale) : (uint8_t)0;
+    }
     y = fminf(fmaxf(y, qmin), qmax);
+    if (Q == kQE4M3Fnuz) return f32_to_e4m3fnuz(y);
     if (FP8) return f32_to_e4m3(y);
     return (uint8_t)(int8_t)(int)y;  // truncation toward zero
   };
@@ -365,7 +396,7 @@ __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__
     q[i] = quant1(to_f32(x[i]), i);
 }
 
-template <typename T, bool FP8>
+template <typename T, int Q>
 int launch_tensor_quant(const void* x, int64_t n, void* q, float* dq_scale, unsigned* ws,
                         cudaStream_t st) {
   constexpr int V = 16 / sizeof(T);
@@ -381,14 +412,14 @@ int launch_tensor_quant(const void* x, int64_t n, void* q, float* dq_scale, unsi
   if (rc) return rc;
   grid = grid_for(ceil_div(n, V), kThreads, 8);
   if (vec)
-    k_tensor_quant<T, FP8, V><<<grid, kThreads, 0, st>>>((const T*)x, n, ws, (uint8_t*)q, dq_scale);
+    k_tensor_quant<T, Q, V><<<grid, kThreads, 0, st>>>((const T*)x, n, ws, (uint8_t*)q, dq_scale);
   else
-    k_tensor_quant<T, FP8, 1><<<grid, kThreads, 0, st>>>((const T*)x, n, ws, (uint8_t*)q, dq_scale);
+    k_tensor_quant<T, Q, 1><<<grid, kThreads, 0, st>>>((const T*)x, n, ws, (uint8_t*)q, dq_scale);
   return check_launch("tensor-wide quant: quantize");
 }
 
 // ------------------------------------------------------------------ block dequant
-template <bool FP8>
+template <int Q>
 __global__ void __launch_bounds__(kThreads) k_block_dequant(const uint8_t* __restrict__ q,
                                                            const float* __restrict__ s,
                                                            float* __restrict__ y, int64_t n,
@@ -400,12 +431,13 @@ __global__ void __launch_bounds__(kThreads) k_block_dequant(const uint8_t* __res
     const int64_t r = i / k;
     const int64_t c = i - r * k;
     const uint8_t v = q[i];
-    const float f = FP8 ? e4m3_to_f32(v) : (float)(int8_t)v;
+    const float f = Q == kQE4M3 ? e4m3_to_f32(v)
+                                : (Q == kQE4M3Fnuz ? e4m3fnuz_to_f32(v) : (float)(int8_t)v);
     y[i] = __fmul_rn(f, __ldg(s + (r / bn) * k_tiles + c / bk));
   }
 }
 
-int launch_block_dequant(bool fp8, const void* q, const float* s, float* y, int64_t n, int64_t k,
+int launch_block_dequant(int kind, const void* q, const float* s, float* y, int64_t n, int64_t k,
                          int64_t bn, int64_t bk, cudaStream_t st) {
   if (n < 0 || k < 0 || bn <= 0 || bk <= 0)
     return fail(TO_EINVAL, "block_dequant: invalid sizes n=%lld k=%lld block=[%lld,%lld]",
@@ -413,10 +445,13 @@ int launch_block_dequant(bool fp8, const void* q, const float* s, float* y, int6
   if (n == 0 || k == 0) return TO_OK;
   const int64_t kt = ceil_div(k, bk);
   unsigned grid = grid_for(n * k, kThreads, 8);
-  if (fp8)
-    k_block_dequant<true><<<grid, kThreads, 0, st>>>((const uint8_t*)q, s, y, n, k, bn, bk, kt);
+  if (kind == kQE4M3)
+    k_block_dequant<kQE4M3><<<grid, kThreads, 0, st>>>((const uint8_t*)q, s, y, n, k, bn, bk, kt);
+  else if (kind == kQE4M3Fnuz)
+    k_block_dequant<kQE4M3Fnuz><<<grid, kThreads, 0, st>>>((const uint8_t*)q, s, y, n, k, bn, bk,
+                                                          kt);
   else
-    k_block_dequant<false><<<grid, kThreads, 0, st>>>((const uint8_t*)q, s, y, n, k, bn, bk, kt);
+    k_block_dequant<kQI8><<<grid, kThreads, 0, st>>>((const uint8_t*)q, s, y, n, k, bn, bk, kt);
   return check_launch("block_dequant");
 }
 
@@ -514,9 +549,11 @@ int launch_tensor_quant_fp8_noalloc(const void* x, int64_t n, void* q, float* dq
   if (rc) return rc;
   const unsigned grid = grid_for(ceil_div(n, V), kThreads, 8);
   if (vec)
-    k_tensor_quant<T, true, V><<<grid, kThreads, 0, st>>>((const T*)x, n, amax, (uint8_t*)q, dq_scale);
+    k_tensor_quant<T, kQE4M3, V><<<grid, kThreads, 0, st>>>((const T*)x, n, amax, (uint8_t*)q,
+                                                           dq_scale);
   else
-    k_tensor_quant<T, true, 1><<<grid, kThreads, 0, st>>>((const T*)x, n, amax, (uint8_t*)q, dq_scale);
+    k_tensor_quant<T, kQE4M3, 1><<<grid, kThreads, 0, st>>>((const T*)x, n, amax, (uint8_t*)q,
+                                                           dq_scale);
   return check_launch("input_to_float8 (no-alloc): quantize");
 }
 
@@ -580,7 +617,7 @@ int to_input_to_int8(const void* x, int x_dtype, int64_t n, int8_t* q, float* dq
     return fail(TO_ENOSPACE, "input_to_int8: workspace of %zu bytes is too small",
                 workspace_bytes);
   TOB_DISPATCH_FLOAT(x_dtype, T,
-                     return launch_tensor_quant<T, false>(x, n, q, dq_scale, (unsigned*)workspace,
+                     return launch_tensor_quant<T, kQI8>(x, n, q, dq_scale, (unsigned*)workspace,
                                                           (cudaStream_t)stream));
   return TO_OK;
 }
@@ -592,8 +629,22 @@ int to_input_to_fp8(const void* x, int x_dtype, int64_t n, void* q, float* dq_sc
     return fail(TO_ENOSPACE, "input_to_float8: workspace of %zu bytes is too small",
                 workspace_bytes);
   TOB_DISPATCH_FLOAT(x_dtype, T,
-                     return launch_tensor_quant<T, true>(x, n, q, dq_scale, (unsigned*)workspace,
-                                                         (cudaStream_t)stream));
+                     return launch_tensor_quant<T, kQE4M3>(x, n, q, dq_scale,
+                                                           (unsigned*)workspace,
+                                                           (cudaStream_t)stream));
+  return TO_OK;
+}
+
+int to_input_to_fp8_fnuz(const void* x, int x_dtype, int64_t n, void* q, float* dq_scale,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (n <= 0) return fail(TO_EINVAL, "input_to_float8: empty input");
+  if (!workspace || workspace_bytes < sizeof(unsigned))
+    return fail(TO_ENOSPACE, "input_to_float8: workspace of %zu bytes is too small",
+                workspace_bytes);
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_tensor_quant<T, kQE4M3Fnuz>(x, n, q, dq_scale,
+                                                               (unsigned*)workspace,
+                                                               (cudaStream_t)stream));
   return TO_OK;
 }
 
@@ -622,14 +673,16 @@ int to_per_token_group_quant_i8(const void* x, int x_dtype, int64_t n_groups, in
   if (n_groups == 0) return TO_OK;
   ScaleLayout sl{0, 1};
   TOB_DISPATCH_FLOAT(x_dtype, T,
-                     return launch_group_quant<T, false>(x, n_groups, group_size, eps, 0, sl, q,
+                     return launch_group_quant<T, kQI8>(x, n_groups, group_size, eps, 0, sl, q,
                                                          scales, (cudaStream_t)stream));
   return TO_OK;
 }
 
-int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups, int64_t group_size,
-                                 float eps, int ue8m0, int64_t cm_rows, int64_t cm_groups, void* q,
-                                 float* scales, void* stream) {
+namespace tob {
+namespace {
+int group_quant_fp8_entry(int kind, const void* x, int x_dtype, int64_t n_groups,
+                          int64_t group_size, float eps, int ue8m0, int64_t cm_rows,
+                          int64_t cm_groups, void* q, float* scales, cudaStream_t st) {
   if (n_groups < 0 || group_size <= 0 || group_size > (int64_t)1 << 30)
     return fail(TO_EINVAL, "per_token_group_quant_fp8: invalid groups=%lld size=%lld",
                 (long long)n_groups, (long long)group_size);
@@ -638,20 +691,47 @@ int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups, i
                 "tile %lld groups", (long long)cm_rows, (long long)cm_groups, (long long)n_groups);
   if (n_groups == 0) return TO_OK;
   ScaleLayout sl{cm_rows, cm_groups > 0 ? cm_groups : 1};
-  TOB_DISPATCH_FLOAT(x_dtype, T,
-                     return launch_group_quant<T, true>(x, n_groups, group_size, eps, ue8m0, sl, q,
-                                                        scales, (cudaStream_t)stream));
+  if (kind == kQE4M3Fnuz) {
+    TOB_DISPATCH_FLOAT(x_dtype, T,
+                       return launch_group_quant<T, kQE4M3Fnuz>(x, n_groups, group_size, eps,
+                                                                ue8m0, sl, q, scales, st));
+  } else {
+    TOB_DISPATCH_FLOAT(x_dtype, T,
+                       return launch_group_quant<T, kQE4M3>(x, n_groups, group_size, eps, ue8m0,
+                                                            sl, q, scales, st));
+  }
   return TO_OK;
+}
+}  // namespace
+}  // namespace tob
+
+int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups, int64_t group_size,
+                                 float eps, int ue8m0, int64_t cm_rows, int64_t cm_groups, void* q,
+                                 float* scales, void* stream) {
+  return group_quant_fp8_entry(kQE4M3, x, x_dtype, n_groups, group_size, eps, ue8m0, cm_rows,
+                               cm_groups, q, scales, (cudaStream_t)stream);
+}
+
+int to_per_token_group_quant_fp8_fnuz(const void* x, int x_dtype, int64_t n_groups,
+                                      int64_t group_size, float eps, int ue8m0, int64_t cm_rows,
+                                      int64_t cm_groups, void* q, float* scales, void* stream) {
+  return group_quant_fp8_entry(kQE4M3Fnuz, x, x_dtype, n_groups, group_size, eps, ue8m0, cm_rows,
+                               cm_groups, q, scales, (cudaStream_t)stream);
 }
 
 int to_block_dequant_i8(const int8_t* q, const float* s, float* y, int64_t n, int64_t k,
                         int64_t block_n, int64_t block_k, void* stream) {
-  return launch_block_dequant(false, q, s, y, n, k, block_n, block_k, (cudaStream_t)stream);
+  return launch_block_dequant(kQI8, q, s, y, n, k, block_n, block_k, (cudaStream_t)stream);
 }
 
 int to_block_dequant_fp8(const void* q, const float* s, float* y, int64_t n, int64_t k,
                          int64_t block_n, int64_t block_k, void* stream) {
-  return launch_block_dequant(true, q, s, y, n, k, block_n, block_k, (cudaStream_t)stream);
+  return launch_block_dequant(kQE4M3, q, s, y, n, k, block_n, block_k, (cudaStream_t)stream);
+}
+
+int to_block_dequant_fp8_fnuz(const void* q, const float* s, float* y, int64_t n, int64_t k,
+                              int64_t block_n, int64_t block_k, void* stream) {
+  return launch_block_dequant(kQE4M3Fnuz, q, s, y, n, k, block_n, block_k, (cudaStream_t)stream);
 }
 
 }  // extern "C"

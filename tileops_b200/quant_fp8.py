@@ -1,9 +1,10 @@
 """FP8 e4m3 facade: dynamic quantisation and block-scaled W8A8 FP8 matmul on sm_100a.
 
 Drop-in for tileops/quant_fp8.py (names, arguments, dequant-scale convention, UE8M0 option,
-column-major scale layout and error types). The device format is ``torch.float8_e4m3fn``;
-``float8_e4m3fnuz`` (an AMD encoding with no sm_100 conversion) is rejected with
-NotImplementedError.
+column-major scale layout and error types). The quantisers and block_dequant take both
+``torch.float8_e4m3fn`` and ``torch.float8_e4m3fnuz`` (the reference's ``dtype`` argument);
+the W8A8 GEMMs take e4m3fn only -- sm_100's tensor cores have no e4m3fnuz operand -- and raise
+NotImplementedError for e4m3fnuz.
 """
 
 from __future__ import annotations
@@ -51,15 +52,28 @@ def _require_e4m3fn(dtype: torch.dtype, op: str) -> None:
                                   f"(got {dtype})")
 
 
+_FNUZ = getattr(torch, "float8_e4m3fnuz", None)
+
+
+def _entry(dtype: torch.dtype, op: str, base: str) -> str:
+    """The C entry of `base` for an FP8 code dtype: e4m3fn, or its _fnuz form."""
+    if dtype == torch.float8_e4m3fn:
+        return base
+    if _FNUZ is not None and dtype == _FNUZ:
+        return base + "_fnuz"
+    raise NotImplementedError(f"{op}: unsupported FP8 dtype {dtype}")
+
+
 def input_to_float8(
     x: torch.Tensor,
     dtype: Optional[torch.dtype] = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Tensor-wide dynamic quant -> ``(q, dequant_scale)`` (quant_fp8.py:52-63), arithmetic in
-    ``x.dtype``: ``s = (1/amax) * 448``, ``q = e4m3(clamp(x * s, +-448))``."""
+    ``x.dtype``: ``s = (1/amax) * fmax``, ``q = fp8(clamp(x * s, +-fmax))`` with fmax =
+    finfo(dtype).max (448 for e4m3fn, 240 for e4m3fnuz)."""
     op = "input_to_float8"
     dtype = dtype if dtype is not None else default_fp8_dtype()
-    _require_e4m3fn(dtype, op)
+    entry = _entry(dtype, op, "to_input_to_fp8")
     _lib.ensure_device(x, op)
     if x.dtype not in _FLOATS:
         raise TypeError(f"{op}: unsupported input dtype {x.dtype}")
@@ -71,7 +85,7 @@ def input_to_float8(
     lib = _lib.load()
     ws_bytes = lib.to_input_quant_workspace_size()
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
-    _lib.call("to_input_to_fp8", xc.data_ptr(), _lib.DTYPE_CODES[x.dtype], xc.numel(),
+    _lib.call(entry, xc.data_ptr(), _lib.DTYPE_CODES[x.dtype], xc.numel(),
               q.data_ptr(), s.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_ptr())
     return q, s
 
@@ -87,8 +101,9 @@ def per_token_group_quant_fp8(
     use_ue8m0: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-token-group dynamic FP8 quant along the last dim (quant_fp8.py:83-140):
-    ``scale = max(absmax, eps) / 448`` (optionally rounded up to a power of two),
-    ``q = e4m3(clamp(x / scale, +-448))``."""
+    ``scale = max(absmax, eps) / fmax`` (optionally rounded up to a power of two),
+    ``q = fp8(clamp(x / scale, +-fmax))`` with get_fp8_min_max's fmax (448 for e4m3fn, 224
+    for e4m3fnuz)."""
     if tma_aligned_scales:
         raise NotImplementedError(
             "per_token_group_quant_fp8: tma_aligned_scales is not implemented "
@@ -105,7 +120,7 @@ def per_token_group_quant_fp8(
     if x.stride(-1) != 1:
         raise ValueError("`x` groups must be contiguous along the last dimension")
     op = "per_token_group_quant_fp8"
-    _require_e4m3fn(dtype, op)
+    entry = _entry(dtype, op, "to_per_token_group_quant_fp8")
     _lib.ensure_device(x, op)
     if x.dtype not in _FLOATS:
         raise TypeError(f"{op}: unsupported input dtype {x.dtype}")
@@ -133,7 +148,7 @@ def per_token_group_quant_fp8(
     else:
         x_s = torch.empty(*lead, num_groups, dtype=torch.float32, device=x.device)
         cm_rows, cm_groups = 0, 0
-    _lib.call("to_per_token_group_quant_fp8", x.data_ptr(), _lib.DTYPE_CODES[x.dtype], n_groups,
+    _lib.call(entry, x.data_ptr(), _lib.DTYPE_CODES[x.dtype], n_groups,
               group_size, eps, 1 if use_ue8m0 else 0, cm_rows, cm_groups, q.data_ptr(),
               x_s.data_ptr(), _lib.stream_ptr())
     if out_q is not None and not direct:
@@ -160,13 +175,13 @@ def block_dequant(
             f"block grid ({n_tiles}, {k_tiles}) for {tuple(x_q_block.shape)}"
         )
     op = "block_dequant"
-    _require_e4m3fn(x_q_block.dtype, op)
+    entry = _entry(x_q_block.dtype, op, "to_block_dequant_fp8")
     _lib.ensure_device(x_q_block, op)
     _lib.same_device(op, x_q_block, x_s)
     q = x_q_block.contiguous()
     s = x_s.to(torch.float32).contiguous()
     y = torch.empty(n, k, dtype=torch.float32, device=q.device)
-    _lib.call("to_block_dequant_fp8", q.data_ptr(), s.data_ptr(), y.data_ptr(), n, k, block_n,
+    _lib.call(entry, q.data_ptr(), s.data_ptr(), y.data_ptr(), n, k, block_n,
               block_k, _lib.stream_ptr())
     return y
 
