@@ -269,9 +269,9 @@ TO_API int to_w8a8_fp8_gemm(const void* a, const void* b, const float* a_s, cons
 
 /* ---- dense GEMM and GEMV (tileops/blas/gemm.py, tileops/blas/gemv.py) ---------------------
  * replaces tileops/blas/gemm.py:31 gemm (and its mm alias, :71): C [M,N] = A [M,K] @ B [K,N],
- * all row-major, dtype F16 or BF16 for A, B and C, fp32 accumulation, C rounded once. Runs on
- * the tcgen05 tiles when K % 8 == 0, N % 64 == 0 and the pointers are 16-byte aligned; other
- * shapes return TO_EUNSUPPORTED with nothing launched. */
+ * all row-major, dtype F32, F16 or BF16 for A, B and C, fp32 accumulation, C rounded once. 16-bit
+ * operands run on the tcgen05 tiles when K % 8 == 0, N % 64 == 0 and the pointers are 16-byte
+ * aligned; other shapes, alignments and fp32 on 64 x 64 SIMT tiles. */
 TO_API int to_gemm(const void* a, const void* b, void* c, int dtype, int64_t M, int64_t N,
                    int64_t K, void* stream);
 /* replaces tileops/blas/gemv.py:22 gemv (and its mv alias, :60): y [M] = A [M,K] @ x [K], A

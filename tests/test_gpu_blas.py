@@ -1,7 +1,7 @@
 """GPU parity of the dense GEMM and GEMV (tileops.gemm / mm, tileops.gemv / mv): the tcgen05
 tiles with B read MN-major and the streaming GEMV against an fp32 (fp64 for GEMV) torch product of
 the same inputs (rtol = atol = 1e-2 on 16-bit outputs of unit scale, 1e-4 on fp32 GEMV), ragged
-shapes, out= and the library fallback for other GEMM shapes."""
+shapes, out= and the SIMT tiles for the GEMM shapes and dtypes outside the tcgen05 tiles."""
 
 from __future__ import annotations
 
@@ -46,11 +46,30 @@ def test_gemm_deterministic_and_out(cuda):
     assert torch.equal(ot, c1)
 
 
-def test_gemm_other_shapes_and_errors(cuda):
-    a, b = _inputs(33, 50, 20, torch.float16, 4)  # N % 64 != 0: library GEMM
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [(33, 50, 20), (1, 1, 1), (130, 70, 1001), (300, 200, 64),
+                                   (64, 64, 7)])
+def test_gemm_simt_tiles_vs_fp64(cuda, dt, m, n, k):
+    """Shapes outside the tcgen05 tiles (N % 64, K % 8) and fp32 run on the SIMT tiles."""
+    a, b = _inputs(m, n, k, dt, m * 3 + n + k)
     c = tob.gemm(a.to(cuda), b.to(cuda))
+    assert c.dtype == dt and c.shape == (m, n)
+    want = (a.double() @ b.double()).numpy()
+    tol = 1e-5 if dt == torch.float32 else 1e-2
+    np.testing.assert_allclose(c.double().cpu().numpy(), want, rtol=tol, atol=tol)
+
+
+def test_gemm_other_shapes_and_errors(cuda):
+    a, b = _inputs(33, 64, 24, torch.float16, 4)
+    # an unaligned view of B (offset by one element) leaves the tensor-core tiles too
+    bb = torch.empty(24 * 64 + 1, dtype=torch.float16, device=cuda)[1:].view(24, 64)
+    bb.copy_(b.to(cuda))
+    c = tob.gemm(a.to(cuda), bb)
     np.testing.assert_allclose(c.float().cpu().numpy(), (a.float() @ b.float()).numpy(),
                                rtol=1e-2, atol=1e-2)
+    with pytest.raises(ValueError):
+        tob.gemm(torch.zeros(2, 3, device=cuda, dtype=torch.int32),
+                 torch.zeros(3, 5, device=cuda, dtype=torch.int32))
     with pytest.raises(ValueError):
         tob.gemm(torch.zeros(2, 3, device=cuda), torch.zeros(4, 5, device=cuda))
     with pytest.raises(TypeError):

@@ -6,7 +6,7 @@ B (K, N) row-major, and ``y = A @ x``; fp32 accumulation, results in the inputs'
 This is the dense comparator of the quantized layers: the same tcgen05 tiles as the W8A8 GEMMs
 (kind::f16, A K-major, B read MN-major as 64-column strips, no scales). float16 and bfloat16
 run on those tiles when K % 8 == 0 and N % 64 == 0 with 16-byte aligned operands; other
-shapes (and float32) go to the plain library GEMM of torch (cuBLAS) on the same device.
+shapes, and float32, run on the library's SIMT tiles (fp32 FMA).
 GEMV runs on its own streaming kernel for float32, float16 and bfloat16 at every shape.
 """
 
@@ -29,6 +29,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
         raise ValueError(f"gemm: incompatible shapes {tuple(a.shape)} @ {tuple(b.shape)}")
     if a.dtype != b.dtype:
         raise TypeError("gemm: A and B dtypes must match")
+    if a.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        # ValueError, as tileops/runtime/__init__.py:130 raises for a dtype outside these three
+        raise ValueError(f"Unsupported dtype {a.dtype}; expected one of torch.float32, "
+                         "torch.float16, torch.bfloat16")
     _lib.ensure_device(a, "gemm")
     _lib.same_device("gemm", a, b)
     aa = a.contiguous()
@@ -41,14 +45,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
         if out.dtype != a.dtype or out.device != a.device:
             raise TypeError("gemm: out dtype/device must match A")
     cc = out.contiguous()
-    rc = _lib.TO_EUNSUPPORTED
-    if a.dtype in (torch.float16, torch.bfloat16):
-        rc = _lib.load().to_gemm(aa.data_ptr(), bb.data_ptr(), cc.data_ptr(),
-                                 _lib.DTYPE_CODES[a.dtype], m, n, k, _lib.stream_ptr())
-    if rc == _lib.TO_EUNSUPPORTED:
-        torch.mm(aa, bb, out=cc)  # shapes outside the tcgen05 tiles: the library GEMM
-    else:
-        _lib.check(rc, "gemm")
+    _lib.call("to_gemm", aa.data_ptr(), bb.data_ptr(), cc.data_ptr(), _lib.DTYPE_CODES[a.dtype],
+              m, n, k, _lib.stream_ptr())
     if cc.data_ptr() != out.data_ptr():
         out.copy_(cc)
     return out

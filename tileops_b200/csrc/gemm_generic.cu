@@ -107,7 +107,72 @@ __global__ void __launch_bounds__(kThreads) k_w8a8_generic(
   }
 }
 
+// Dense C[M, N] = A[M, K] @ B[K, N] (row-major, T = fp32, fp16 or bf16; fp32 accumulation, C
+// rounded once) for the shapes the tcgen05 tiles do not take (N % 64, K % 8, unaligned rows,
+// fp32; tileops/blas/gemm.py:31). 64 x 64 output tiles, 16 x 16 threads of 4 x 4 outputs, K in
+// steps of 32 through shared memory; every product in fp32 with fmaf in increasing k.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) k_gemm_dense_simt(const T* __restrict__ a,
+                                                             const T* __restrict__ b,
+                                                             T* __restrict__ c, int M, int N,
+                                                             int K) {
+  __shared__ float As[kTK][kTM + 4];  // transposed: As[k][m]
+  __shared__ float Bs[kTK][kTN + 4];  // Bs[k][n]
+  const int tm = threadIdx.x / 16, tn = threadIdx.x % 16;
+  const int m0 = blockIdx.y * kTM, n0 = blockIdx.x * kTN;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += kTK) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kTM * kTK; i += kThreads) {
+      const int r = i / kTK, kk = i % kTK;  // A: consecutive threads along k of one row
+      const int gm = m0 + r, gk = k0 + kk;
+      As[kk][r] = (gm < M && gk < K) ? to_f32(a[(int64_t)gm * K + gk]) : 0.f;
+    }
+    for (int i = threadIdx.x; i < kTK * kTN; i += kThreads) {
+      const int kk = i / kTN, cc = i % kTN;  // B: consecutive threads along n of one row
+      const int gk = k0 + kk, gn = n0 + cc;
+      Bs[kk][cc] = (gk < K && gn < N) ? to_f32(b[(int64_t)gk * N + gn]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kTK; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][tm + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tn + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + tm + 16 * i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tn + 16 * j;
+      if (gn < N) c[(int64_t)gm * N + gn] = from_f32<T>(acc[i][j]);
+    }
+  }
+}
+
 }  // namespace
+
+int gemm_dense_simt_launch(const void* a, const void* b, void* c, int dtype, int64_t M, int64_t N,
+                           int64_t K, cudaStream_t st) {
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
+    return fail(TO_EUNSUPPORTED, "gemm: dimensions too large");
+  dim3 grid((unsigned)ceil_div(N, kTN), (unsigned)ceil_div(M, kTM));
+  if (grid.y > 65535) return fail(TO_EUNSUPPORTED, "gemm: M too large for the SIMT tiles");
+  TOB_DISPATCH_FLOAT(dtype, T, {
+    k_gemm_dense_simt<T><<<grid, kThreads, 0, st>>>((const T*)a, (const T*)b, (T*)c, (int)M,
+                                                     (int)N, (int)K);
+  });
+  return check_launch("gemm (SIMT tiles)");
+}
 
 int w8a8_generic_launch(bool fp8, const void* a, const void* b, const float* a_s, const float* b_s,
                         void* c, int c_dtype, const void* bias, int32_t* acc_out, int64_t M,

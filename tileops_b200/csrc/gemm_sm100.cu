@@ -1688,6 +1688,9 @@ int w8a8_tc_launch(bool fp8, const void* a, const void* b, const float* a_s, con
   return sm100::launch_gemm<sm100::Kind::I8>(a, b, M, N, K, ep, st);
 }
 
+int gemm_dense_simt_launch(const void* a, const void* b, void* c, int dtype, int64_t M, int64_t N,
+                           int64_t K, cudaStream_t st);
+
 }  // namespace tob
 
 extern "C" {
@@ -1698,21 +1701,22 @@ int to_gemm(const void* a, const void* b, void* c, int dtype, int64_t M, int64_t
   if (M < 0 || N < 0 || K < 0)
     return fail(TO_EINVAL, "gemm: invalid shape M=%lld N=%lld K=%lld", (long long)M,
                 (long long)N, (long long)K);
-  if (dtype != TO_F16 && dtype != TO_BF16)
-    return fail(TO_EUNSUPPORTED, "gemm: dtype %s (float16 and bfloat16 are supported)",
+  if (dtype != TO_F16 && dtype != TO_BF16 && dtype != TO_F32)
+    return fail(TO_EUNSUPPORTED, "gemm: dtype %s (float32, float16 and bfloat16 are supported)",
                 dtype_name(dtype));
   if (M == 0 || N == 0) return TO_OK;
+  if (!a || !b || !c) return fail(TO_EINVAL, "gemm: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   if (K == 0) {
-    const cudaError_t e = cudaMemsetAsync(c, 0, (size_t)(M * N * 2), st);
+    const size_t elem = dtype == TO_F32 ? 4 : 2;
+    const cudaError_t e = cudaMemsetAsync(c, 0, (size_t)(M * N) * elem, st);
     return e == cudaSuccess ? TO_OK : cuda_fail(e, "gemm: zero fill");
   }
-  // TMA constraints of the tcgen05 tiles: 16-byte rows of A, whole 64-column strips of B.
-  if (K % 8 != 0 || N % 64 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX ||
-      !aligned16(a) || !aligned16(b) || !aligned16(c))
-    return fail(TO_EUNSUPPORTED,
-                "gemm: shape or alignment outside the tensor-core tiles (K %% 8 == 0, N %% 64 "
-                "== 0, 16-byte aligned operands needed)");
+  // TMA constraints of the tcgen05 tiles: 16-bit operands, 16-byte rows of A, whole 64-column
+  // strips of B; everything else on the SIMT tiles.
+  if (dtype == TO_F32 || K % 8 != 0 || N % 64 != 0 || M > INT32_MAX || N > INT32_MAX ||
+      K > INT32_MAX || !aligned16(a) || !aligned16(b) || !aligned16(c))
+    return gemm_dense_simt_launch(a, b, c, dtype, M, N, K, st);
   sm100::Epi ep;
   memset(&ep, 0, sizeof(ep));
   ep.a_s = nullptr;  // unscaled: the epilogue multiplies by 1
