@@ -293,6 +293,17 @@ TO_API int to_silu_and_mul(const void* a, const void* b, void* c, int dtype, int
  * act(x) = 0.5 x (1 + tanh(0.7978845608028654 (x + 0.044715 x^3))). */
 TO_API int to_gelu_and_mul(const void* a, const void* b, void* c, int dtype, int64_t rows,
                            int64_t cols, int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+/* Library extension (no reference counterpart; it fuses the two): the gated activation of
+ * to_silu_and_mul / to_gelu_and_mul (act TO_ACT_SILU or TO_ACT_GELU_TANH) quantised per token
+ * group as tileops/quant_fp8.py:83 per_token_group_quant_fp8 (q_dtype TO_E4M3; ue8m0 and
+ * column_major as there) or tileops/quant_int8.py:109 per_token_group_quant_int8 (TO_I8), without
+ * writing the activation: q [rows, cols] codes, scales [rows, cols / group_size] (column_major:
+ * the reference's column-major layout). Each activation value is rounded to dtype first, so the
+ * result equals the activation kernel followed by the quantiser, bit for bit. */
+TO_API int to_act_and_mul_group_quant(const void* a, const void* b, int dtype, int64_t rows,
+                                      int64_t cols, int64_t lda, int64_t ldb, int act,
+                                      int64_t group_size, float eps, int ue8m0, int column_major,
+                                      int q_dtype, void* q, float* scales, void* stream);
 
 #ifdef __cplusplus
 }

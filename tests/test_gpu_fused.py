@@ -98,3 +98,34 @@ def test_validation(cuda):
         tob.silu_and_mul(a.to(torch.int32), a.to(torch.int32))
     e = torch.empty(0, 5, device=cuda)
     assert tob.silu_and_mul(e, e).shape == (0, 5)
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu"])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("rows,f,g,opts", [
+    (16, 14336, 128, {}),                                 # the decode step's gate_up, FP8
+    (7, 512, 64, {"use_ue8m0": True}),
+    (33, 1024, 128, {"column_major_scales": True}),
+    (5, 768, 128, {"dtype": torch.int8}),
+    (300, 96, 32, {}),                                    # odd group size: scalar loads
+])
+def test_act_and_mul_group_quant_equals_the_two_ops(cuda, act, dt, rows, f, g, opts):
+    """The fused activation + per-token-group quantiser against silu_and_mul / gelu_and_mul
+    followed by per_token_group_quant_fp8 / _int8, bit for bit, on the gate and up halves of a
+    gate_up output read in place; and against the oracle."""
+    gen = torch.Generator().manual_seed(rows * 13 + f + g)
+    u = (torch.randn(rows, 2 * f, generator=gen) * 3).to(dt).to(cuda)
+    u[0, 3] = float("nan")
+    gate, up = u[:, :f], u[:, f:]
+    q, s = tob.act_and_mul_group_quant(gate, up, g, act=act, **opts)
+    y = (tob.silu_and_mul if act == "silu" else tob.gelu_and_mul)(gate, up)
+    if opts.get("dtype") == torch.int8:
+        wq, ws = tob.per_token_group_quant_int8(y, g)
+    else:
+        wq, ws = tob.per_token_group_quant_fp8(
+            y, g, column_major_scales=opts.get("column_major_scales", False),
+            use_ue8m0=opts.get("use_ue8m0", False))
+    assert q.dtype == wq.dtype and q.shape == wq.shape and s.shape == ws.shape
+    assert torch.equal(q.view(torch.uint8) if q.dtype != torch.int8 else q,
+                       wq.view(torch.uint8) if wq.dtype != torch.int8 else wq)
+    assert np.array_equal(s.cpu().numpy(), ws.cpu().numpy(), equal_nan=True)

@@ -48,7 +48,7 @@ from .quant_int8 import (
 )
 from ._lib import set_launch_overlap, version
 from .blas import gemm, gemv, mm, mv
-from .fused import gelu_and_mul, silu_and_mul
+from .fused import act_and_mul_group_quant, gelu_and_mul, silu_and_mul
 
 __all__ = [
     "set_launch_overlap",
@@ -76,6 +76,7 @@ __all__ = [
     "REVERSE_AWQ_ORDER",
     "awq_dequantize",
     "awq_dequantize_triton",
+    "act_and_mul_group_quant",
     "awq_gemm",
     "awq_gemm_gelu_and_mul",
     "awq_gemm_silu_and_mul",

@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_awq_gemm_act": (_I, [_P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _I, _P, _S, _P]),
     "to_awq_gemm_act_gather": (_I, [_P, _P, _P, _I, _P, ctypes.POINTER(_P), _I, _I, _L, _L, _L,
                                     _L, _I, _P, _S, _P]),
+    "to_act_and_mul_group_quant": (_I, [_P, _P, _I, _L, _L, _L, _L, _I, _L, _F, _I, _I, _I, _P,
+                                        _P, _P]),
     "to_peer_flags_bytes": (_S, []),
     "to_peer_barrier": (_I, [ctypes.POINTER(_P), _I, _I, _P, _P]),
     "to_ipc_alloc": (_I, [_S, ctypes.POINTER(_P), _P]),

@@ -9,6 +9,7 @@
 #include <mutex>
 #include <type_traits>
 
+#include "act.cuh"
 #include "common.cuh"
 
 namespace tob {
@@ -200,8 +201,35 @@ __device__ __forceinline__ bool sign_of(float v) { return __float_as_uint(v) >> 
 __device__ __forceinline__ bool sign_of(__half v) { return __half_as_ushort(v) >> 15; }
 __device__ __forceinline__ bool sign_of(__nv_bfloat16 v) { return __bfloat16_as_ushort(v) >> 15; }
 
-template <typename T, int Q, int V, int MAXV>
-__global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
+// Where the quantiser's groups come from: a contiguous x (groups back to back), or the gated
+// activation act(gate) * up of a gate_up output given as [rows, cols] views with row strides
+// (cols = groups per row x G), each value rounded to T exactly as the activation kernel writes
+// it -- the activation that produces the next layer's input, fused into its quantiser.
+template <typename T, int ACT> struct GroupSrc {
+  const T* a;
+  const T* b;
+  int64_t lda, ldb, gpr;  // row strides, groups per row
+  template <int V>
+  __device__ __forceinline__ Pack<T, V> load(int64_t g, int G, int v) const {
+    const int64_t r = g / gpr;
+    const int64_t c = (g - r * gpr) * G + (int64_t)v * V;
+    const Pack<T, V> pa = ld_pack<T, V>(a + r * lda + c), pb = ld_pack<T, V>(b + r * ldb + c);
+    Pack<T, V> o;
+#pragma unroll
+    for (int j = 0; j < V; ++j) o.v[j] = act_mul<T, ACT>(pa.v[j], pb.v[j]);
+    return o;
+  }
+};
+template <typename T> struct GroupSrc<T, -1> {
+  const T* x;
+  template <int V>
+  __device__ __forceinline__ Pack<T, V> load(int64_t g, int G, int v) const {
+    return ld_pack<T, V>(x + g * (int64_t)G + (int64_t)v * V);
+  }
+};
+
+template <typename T, int Q, int V, int MAXV, int ACT = -1>
+__global__ void __launch_bounds__(1024) k_group_quant(const GroupSrc<T, ACT> src,
                                                      uint8_t* __restrict__ qout,
                                                      float* __restrict__ scales, int64_t n_groups,
                                                      int G, int team_log2, float eps, int ue8m0,
@@ -220,20 +248,19 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
        g0 += (int64_t)gridDim.x * teams_per_cta) {
     const int64_t g = g0 + team_id;
     const bool active = g < n_groups;
-    const T* xg = x + g * (int64_t)G;
     Pack<T, V> cache[MAXV];
     unsigned amax = 0u;  // abs_key of the group's largest |x|; a NaN anywhere makes it NaN
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
       const int v = lane + i * team;
       if (active && v < nvec) {
-        cache[i] = ld_pack<T, V>(xg + (int64_t)v * V);
+        cache[i] = src.template load<V>(g, G, v);
 #pragma unroll
         for (int j = 0; j < V; ++j) amax = max(amax, abs_key(to_f32(cache[i].v[j])));
       }
     }
     for (int v = lane + MAXV * team; active && v < nvec; v += team) {
-      Pack<T, V> t = ld_pack<T, V>(xg + (int64_t)v * V);
+      Pack<T, V> t = src.template load<V>(g, G, v);
 #pragma unroll
       for (int j = 0; j < V; ++j) amax = max(amax, abs_key(to_f32(t.v[j])));
     }
@@ -281,8 +308,28 @@ __global__ void __launch_bounds__(1024) k_group_quant(const T* __restrict__ x,
       if (active && v < nvec) emit(v, cache[i]);
     }
     for (int v = lane + MAXV * team; active && v < nvec; v += team)
-      emit(v, ld_pack<T, V>(xg + (int64_t)v * V));
+      emit(v, src.template load<V>(g, G, v));
   }
+}
+
+// Threads per group (a power of two up to 1024) and grid for n_groups groups of nvec vectors.
+struct GroupGrid {
+  int team_log2, threads;
+  int64_t blocks;
+};
+inline GroupGrid group_grid(int64_t n_groups, int64_t nvec, int maxv) {
+  GroupGrid gg;
+  const int64_t want = ceil_div(nvec, maxv);
+  gg.team_log2 = 0;
+  while ((1 << gg.team_log2) < want && gg.team_log2 < 10) ++gg.team_log2;
+  const int team = 1 << gg.team_log2;
+  gg.threads = team > kThreads ? team : kThreads;
+  const int64_t teams_per_cta = gg.threads / team;
+  gg.blocks = ceil_div(n_groups, teams_per_cta);
+  const int64_t cap = (int64_t)sm_count() * 64;
+  if (gg.blocks > cap) gg.blocks = cap;
+  if (gg.blocks < 1) gg.blocks = 1;
+  return gg;
 }
 
 template <typename T, int Q>
@@ -290,26 +337,35 @@ int launch_group_quant(const void* x, int64_t n_groups, int64_t G, float eps, in
                        ScaleLayout sl, void* q, float* scales, cudaStream_t st) {
   constexpr int VV = 16 / sizeof(T);
   const bool vec = (G % VV == 0) && aligned16(x) && aligned_to(q, VV);
-  const int V = vec ? VV : 1;
-  const int64_t nvec = G / V;
-  const int maxv = vec ? 4 : 8;
-  int64_t want = ceil_div(nvec, maxv);
-  int team_log2 = 0;
-  while ((1 << team_log2) < want && team_log2 < 10) ++team_log2;
-  const int team = 1 << team_log2;
-  const int threads = team > kThreads ? team : kThreads;
-  const int64_t teams_per_cta = threads / team;
-  int64_t blocks = ceil_div(n_groups, teams_per_cta);
-  const int64_t cap = (int64_t)sm_count() * 64;
-  if (blocks > cap) blocks = cap;
-  if (blocks < 1) blocks = 1;
+  const GroupGrid gg = group_grid(n_groups, G / (vec ? VV : 1), vec ? 4 : 8);
+  GroupSrc<T, -1> src{(const T*)x};
   if (vec)
-    k_group_quant<T, Q, VV, 4><<<(unsigned)blocks, threads, 0, st>>>(
-        (const T*)x, (uint8_t*)q, scales, n_groups, (int)G, team_log2, eps, ue8m0, sl);
+    k_group_quant<T, Q, VV, 4><<<(unsigned)gg.blocks, gg.threads, 0, st>>>(
+        src, (uint8_t*)q, scales, n_groups, (int)G, gg.team_log2, eps, ue8m0, sl);
   else
-    k_group_quant<T, Q, 1, 8><<<(unsigned)blocks, threads, 0, st>>>(
-        (const T*)x, (uint8_t*)q, scales, n_groups, (int)G, team_log2, eps, ue8m0, sl);
+    k_group_quant<T, Q, 1, 8><<<(unsigned)gg.blocks, gg.threads, 0, st>>>(
+        src, (uint8_t*)q, scales, n_groups, (int)G, gg.team_log2, eps, ue8m0, sl);
   return check_launch(Q != kQI8 ? "per_token_group_quant_fp8" : "per_token_group_quant_int8");
+}
+
+// The quantiser of act(gate) * up ([rows, cols] views a, b with row strides lda, ldb).
+template <typename T, int Q, int ACT>
+int launch_act_group_quant(const void* a, const void* b, int64_t rows, int64_t cols, int64_t lda,
+                           int64_t ldb, int64_t G, float eps, int ue8m0, ScaleLayout sl, void* q,
+                           float* scales, cudaStream_t st) {
+  constexpr int VV = 16 / sizeof(T);
+  const bool vec = (G % VV == 0) && lda % VV == 0 && ldb % VV == 0 && aligned16(a) &&
+                   aligned16(b) && aligned_to(q, VV);
+  const int64_t n_groups = rows * (cols / G);
+  const GroupGrid gg = group_grid(n_groups, G / (vec ? VV : 1), vec ? 4 : 8);
+  GroupSrc<T, ACT> src{(const T*)a, (const T*)b, lda, ldb, cols / G};
+  if (vec)
+    k_group_quant<T, Q, VV, 4, ACT><<<(unsigned)gg.blocks, gg.threads, 0, st>>>(
+        src, (uint8_t*)q, scales, n_groups, (int)G, gg.team_log2, eps, ue8m0, sl);
+  else
+    k_group_quant<T, Q, 1, 8, ACT><<<(unsigned)gg.blocks, gg.threads, 0, st>>>(
+        src, (uint8_t*)q, scales, n_groups, (int)G, gg.team_log2, eps, ue8m0, sl);
+  return check_launch("act_and_mul_group_quant");
 }
 
 // ------------------------------------------------------------------ tensor-wide dynamic quant
@@ -717,6 +773,52 @@ int to_per_token_group_quant_fp8_fnuz(const void* x, int x_dtype, int64_t n_grou
                                       int64_t cm_groups, void* q, float* scales, void* stream) {
   return group_quant_fp8_entry(kQE4M3Fnuz, x, x_dtype, n_groups, group_size, eps, ue8m0, cm_rows,
                                cm_groups, q, scales, (cudaStream_t)stream);
+}
+
+int to_act_and_mul_group_quant(const void* a, const void* b, int dtype, int64_t rows,
+                               int64_t cols, int64_t lda, int64_t ldb, int act,
+                               int64_t group_size, float eps, int ue8m0, int column_major,
+                               int q_dtype, void* q, float* scales, void* stream) {
+  if (rows < 0 || cols < 0 || group_size <= 0 || group_size > (int64_t)1 << 30 ||
+      (cols % group_size) != 0 || (rows > 1 && (lda < cols || ldb < cols)))
+    return fail(TO_EINVAL,
+                "act_and_mul_group_quant: invalid shape rows=%lld cols=%lld group=%lld "
+                "strides=(%lld, %lld)", (long long)rows, (long long)cols, (long long)group_size,
+                (long long)lda, (long long)ldb);
+  if (act != kSilu && act != kGeluTanh)
+    return fail(TO_EINVAL, "act_and_mul_group_quant: unknown activation %d", act);
+  if (q_dtype != TO_E4M3 && q_dtype != TO_I8)
+    return fail(TO_EUNSUPPORTED, "act_and_mul_group_quant: codes %s (float8_e4m3fn or int8)",
+                dtype_name(q_dtype));
+  if (q_dtype == TO_I8 && (ue8m0 || column_major))
+    return fail(TO_EINVAL, "act_and_mul_group_quant: ue8m0 / column-major scales are FP8 options");
+  if (rows == 0 || cols == 0) return TO_OK;
+  if (!a || !b || !q || !scales) return fail(TO_EINVAL, "act_and_mul_group_quant: null pointer");
+  ScaleLayout sl{column_major ? rows : 0, column_major ? cols / group_size : 1};
+  cudaStream_t st = (cudaStream_t)stream;
+  auto run = [&](auto tag) -> int {
+    using T = decltype(tag);
+    if (q_dtype == TO_E4M3)
+      return act == kSilu
+                 ? launch_act_group_quant<T, kQE4M3, kSilu>(a, b, rows, cols, lda, ldb,
+                                                            group_size, eps, ue8m0, sl, q,
+                                                            scales, st)
+                 : launch_act_group_quant<T, kQE4M3, kGeluTanh>(a, b, rows, cols, lda, ldb,
+                                                                group_size, eps, ue8m0, sl, q,
+                                                                scales, st);
+    return act == kSilu
+               ? launch_act_group_quant<T, kQI8, kSilu>(a, b, rows, cols, lda, ldb, group_size,
+                                                        eps, 0, sl, q, scales, st)
+               : launch_act_group_quant<T, kQI8, kGeluTanh>(a, b, rows, cols, lda, ldb,
+                                                            group_size, eps, 0, sl, q, scales,
+                                                            st);
+  };
+  switch (dtype) {
+    case TO_F32: return run(0.0f);
+    case TO_F16: return run(__half{});
+    case TO_BF16: return run(__nv_bfloat16{});
+  }
+  return fail(TO_EUNSUPPORTED, "act_and_mul_group_quant: dtype %s", dtype_name(dtype));
 }
 
 int to_block_dequant_i8(const int8_t* q, const float* s, float* y, int64_t n, int64_t k,

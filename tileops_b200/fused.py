@@ -102,4 +102,51 @@ def gelu_and_mul(a: torch.Tensor, b: torch.Tensor, *,
     return _act_mul("gelu_and_mul", "to_gelu_and_mul", a, b, out)
 
 
-__all__ = ["gelu_and_mul", "silu_and_mul"]
+def act_and_mul_group_quant(a: torch.Tensor, b: torch.Tensor, group_size: int, *,
+                            act: str = "silu", dtype: Optional[torch.dtype] = None,
+                            eps: float = 1e-10, column_major_scales: bool = False,
+                            use_ue8m0: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """Library extension (no reference counterpart): ``silu_and_mul(a, b)`` (or gelu with
+    ``act="gelu"``) quantised per token group -- ``per_token_group_quant_fp8`` of it
+    (tileops/quant_fp8.py:83; dtype ``torch.float8_e4m3fn``, the default) or
+    ``per_token_group_quant_int8`` (tileops/quant_int8.py:109; dtype ``torch.int8``) -- in one
+    kernel that never writes the activation. Returns the same ``(q, scales)`` as the two ops
+    run one after the other, bit for bit: the input of a W8A8 down projection straight from
+    the gate and up halves of the gate_up output."""
+    op = "act_and_mul_group_quant"
+    _validate_fused(a, b, None, op)
+    if act not in ("silu", "gelu"):
+        raise ValueError(f"{op}: act must be 'silu' or 'gelu' (got {act!r})")
+    dtype = torch.float8_e4m3fn if dtype is None else dtype
+    if dtype not in (torch.float8_e4m3fn, torch.int8):
+        raise TypeError(f"{op}: codes must be torch.float8_e4m3fn or torch.int8 (got {dtype})")
+    if dtype == torch.int8 and (use_ue8m0 or column_major_scales):
+        raise ValueError(f"{op}: use_ue8m0 and column_major_scales are FP8 options")
+    _lib.ensure_device(a, op)
+    if a.dtype not in _DTYPES:
+        raise TypeError(f"{op}: unsupported dtype {a.dtype} (float32, float16 and bfloat16 are "
+                        "supported)")
+    if a.dim() == 0 or a.shape[-1] % group_size != 0:
+        raise ValueError(f"the last dimension of `a` must be divisible by `group_size` "
+                         f"{group_size}")
+    if column_major_scales and a.dim() != 2:
+        raise ValueError(f"{op}: column_major_scales needs 2-D inputs")
+    cols = a.shape[-1]
+    rows = a.numel() // cols if cols else 0
+    lda, ldb = _row_stride(a), _row_stride(b)
+    if lda is None:
+        a, lda = a.contiguous(), cols
+    if ldb is None:
+        b, ldb = b.contiguous(), cols
+    q = torch.empty(a.shape, dtype=dtype, device=a.device)
+    groups = cols // group_size
+    s = torch.empty(*a.shape[:-1], groups, dtype=torch.float32, device=a.device)
+    if a.numel():
+        _lib.call("to_act_and_mul_group_quant", a.data_ptr(), b.data_ptr(),
+                  _lib.DTYPE_CODES[a.dtype], rows, cols, lda, ldb, 0 if act == "silu" else 1,
+                  group_size, eps, 1 if use_ue8m0 else 0, 1 if column_major_scales else 0,
+                  _lib.DTYPE_CODES[dtype], q.data_ptr(), s.data_ptr(), _lib.stream_ptr())
+    return q, s
+
+
+__all__ = ["act_and_mul_group_quant", "gelu_and_mul", "silu_and_mul"]
