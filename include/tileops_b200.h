@@ -143,6 +143,15 @@ TO_API int to_per_token_group_quant_i8(const void* x, int x_dtype, int64_t n_gro
 TO_API int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups,
                                  int64_t group_size, float eps, int ue8m0, int64_t cm_rows,
                                  int64_t cm_groups, void* q, float* scales, void* stream);
+/* Library extension: per_token_group_quant_fp8 of a 2-D x [rows, cols] (e4m3fn) with the scales
+ * in the TMA-aligned column-major layout the reference leaves unimplemented (its
+ * tma_aligned_scales option raises, quant_fp8.py:94-98): the scale of row r, group j at
+ * scales[j * scales_ld + r], scales_ld >= rows rounded up to a multiple of 4 (16-byte columns).
+ * Codes and scale values as per_token_group_quant_fp8. */
+TO_API int to_per_token_group_quant_fp8_tma(const void* x, int x_dtype, int64_t rows,
+                                            int64_t cols, int64_t group_size, float eps,
+                                            int ue8m0, void* q, float* scales, int64_t scales_ld,
+                                            void* stream);
 /* The same two quantisers with dtype = torch.float8_e4m3fnuz (quant_fp8.py:52, :83 with that
  * dtype): codes in the e4m3fnuz encoding (exponent bias 8, max 240, no negative zero, NaN 0x80).
  * The tensor-wide form scales to finfo(e4m3fnuz).max = 240 and clamps to +-240; the group form

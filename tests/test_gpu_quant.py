@@ -363,3 +363,20 @@ def test_fnuz_gemm_rejected(cuda):
     s = torch.ones(4, 1, device=cuda)
     with pytest.raises(NotImplementedError):
         tob.w8a8_block_fp8_matmul(a, a, s, s, [16, 16])
+
+
+@pytest.mark.parametrize("rows,k,g,ue8m0", [(5, 256, 128, False), (33, 7168, 128, True),
+                                            (128, 512, 64, False), (1, 128, 128, False)])
+def test_group_quant_fp8_tma_aligned_scales(cuda, rows, k, g, ue8m0):
+    """The TMA-aligned column-major scale layout: the same codes and scale values as the row
+    layout, each group's column of scales 16-byte aligned (leading dimension rows rounded up to
+    4)."""
+    gen = torch.Generator().manual_seed(rows + k)
+    x = (torch.randn(rows, k, generator=gen) * 3).bfloat16().to(cuda)
+    q, s = tob.per_token_group_quant_fp8_tma_aligned(x, g, use_ue8m0=ue8m0)
+    wq, ws = tob.per_token_group_quant_fp8(x, g, use_ue8m0=ue8m0)
+    ld = (rows + 3) // 4 * 4
+    assert s.shape == (rows, k // g) and s.stride() == (1, ld)
+    assert s.data_ptr() % 16 == 0
+    assert torch.equal(q.view(torch.uint8), wq.view(torch.uint8))
+    assert torch.equal(s, ws)

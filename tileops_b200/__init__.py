@@ -34,6 +34,7 @@ from .quant_fp8 import (
     input_to_float8,
     is_fp8,
     per_token_group_quant_fp8,
+    per_token_group_quant_fp8_tma_aligned,
     w8a8_block_fp8_matmul,
     w8a8_triton_block_scaled_mm,
 )
@@ -64,6 +65,7 @@ __all__ = [
     "per_token_quant_int8",
     "per_token_group_quant_int8",
     "per_token_group_quant_fp8",
+    "per_token_group_quant_fp8_tma_aligned",
     "block_dequant",
     "block_dequant_fp8",
     "w8a8_block_int8_matmul",

@@ -60,6 +60,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_per_token_group_quant_i8": (_I, [_P, _I, _L, _L, _F, _P, _P, _P]),
     "to_per_token_group_quant_fp8": (_I, [_P, _I, _L, _L, _F, _I, _L, _L, _P, _P, _P]),
     "to_per_token_group_quant_fp8_fnuz": (_I, [_P, _I, _L, _L, _F, _I, _L, _L, _P, _P, _P]),
+    "to_per_token_group_quant_fp8_tma": (_I, [_P, _I, _L, _L, _L, _F, _I, _P, _P, _L, _P]),
     "to_block_dequant_i8": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),
     "to_block_dequant_fp8": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),
     "to_block_dequant_fp8_fnuz": (_I, [_P, _P, _P, _L, _L, _L, _L, _P]),

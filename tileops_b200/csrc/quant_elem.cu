@@ -140,13 +140,21 @@ int launch_dequant_sym(const int8_t* q, const float* scale, void* y, int64_t n, 
 struct ScaleLayout {
   int64_t cm_rows;    // > 0: the reference's column_major_scales layout (see scale_offset)
   int64_t cm_groups;  // groups per row
+  int64_t tma_ld = 0;  // > 0: TMA-aligned column-major scales, cm_groups groups per row
 };
 
 // Position of group g's scale. Natural order is g. With column_major_scales the reference
 // returns s_flat.reshape(..., G_, M).transpose(-2, -1).contiguous() (quant_fp8.py:129-136):
 // within each batch of M rows x G_ groups, flat scale t lands at row t % M, column t / M of
 // a contiguous [M, G_] tensor.
+// With tma_ld > 0 (the layout DeepGEMM-style kernels load with TMA): the scale of row r, group
+// j of a 2-D input sits at j * tma_ld + r, tma_ld being the row count rounded up to 4 floats
+// (16 bytes) so that every column starts 16-byte aligned.
 __device__ __forceinline__ int64_t scale_offset(int64_t g, const ScaleLayout& sl) {
+  if (sl.tma_ld > 0) {
+    const int64_t r = g / sl.cm_groups;
+    return (g - r * sl.cm_groups) * sl.tma_ld + r;
+  }
   if (sl.cm_rows <= 0) return g;
   const int64_t per_batch = sl.cm_rows * sl.cm_groups;
   const int64_t b = g / per_batch;
@@ -766,6 +774,24 @@ int to_per_token_group_quant_fp8(const void* x, int x_dtype, int64_t n_groups, i
                                  float* scales, void* stream) {
   return group_quant_fp8_entry(kQE4M3, x, x_dtype, n_groups, group_size, eps, ue8m0, cm_rows,
                                cm_groups, q, scales, (cudaStream_t)stream);
+}
+
+int to_per_token_group_quant_fp8_tma(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                     int64_t group_size, float eps, int ue8m0, void* q,
+                                     float* scales, int64_t scales_ld, void* stream) {
+  if (rows < 0 || cols < 0 || group_size <= 0 || cols % group_size != 0 ||
+      scales_ld < ((rows + 3) / 4) * 4)
+    return fail(TO_EINVAL, "per_token_group_quant_fp8: TMA-aligned scales need cols %% group == 0 "
+                "and a leading dimension >= rows rounded up to 4 (rows=%lld cols=%lld group=%lld "
+                "ld=%lld)", (long long)rows, (long long)cols, (long long)group_size,
+                (long long)scales_ld);
+  if (rows == 0 || cols == 0) return TO_OK;
+  ScaleLayout sl{0, cols / group_size, scales_ld};
+  TOB_DISPATCH_FLOAT(x_dtype, T,
+                     return launch_group_quant<T, kQE4M3>(x, rows * (cols / group_size),
+                                                          group_size, eps, ue8m0, sl, q, scales,
+                                                          (cudaStream_t)stream));
+  return TO_OK;
 }
 
 int to_per_token_group_quant_fp8_fnuz(const void* x, int x_dtype, int64_t n_groups,

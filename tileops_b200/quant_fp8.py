@@ -157,6 +157,40 @@ def per_token_group_quant_fp8(
     return q, x_s
 
 
+def per_token_group_quant_fp8_tma_aligned(
+    x: torch.Tensor,
+    group_size: int,
+    eps: float = 1e-10,
+    use_ue8m0: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Library extension: ``per_token_group_quant_fp8`` of a 2-D ``x`` [M, K] (e4m3fn codes)
+    with the scales in the TMA-aligned column-major layout that the reference's
+    ``tma_aligned_scales=True`` leaves unimplemented (quant_fp8.py:94-98): a [M, K/G] view with
+    strides (1, ld), ld = M rounded up to 4, so every group's column of scales starts 16-byte
+    aligned for a TMA load. Same codes and scale values as per_token_group_quant_fp8."""
+    op = "per_token_group_quant_fp8"
+    if x.dim() != 2:
+        raise ValueError(f"{op}: TMA-aligned scales need a 2-D input")
+    if x.shape[-1] % group_size != 0:
+        raise ValueError(
+            f"the last dimension of `x` {x.shape[-1]} must be divisible "
+            f"by `group_size` {group_size}"
+        )
+    _lib.ensure_device(x, op)
+    if x.dtype not in _FLOATS:
+        raise TypeError(f"{op}: unsupported input dtype {x.dtype}")
+    x = x.contiguous()
+    m, k = x.shape
+    groups = k // group_size
+    ld = (m + 3) // 4 * 4
+    q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    buf = torch.empty(groups, ld, dtype=torch.float32, device=x.device)
+    _lib.call("to_per_token_group_quant_fp8_tma", x.data_ptr(), _lib.DTYPE_CODES[x.dtype], m, k,
+              group_size, eps, 1 if use_ue8m0 else 0, q.data_ptr(), buf.data_ptr(), ld,
+              _lib.stream_ptr())
+    return q, buf.t()[:m]
+
+
 def block_dequant(
     x_q_block: torch.Tensor,
     x_s: torch.Tensor,
@@ -267,6 +301,7 @@ __all__ = [
     "input_to_float8",
     "is_fp8",
     "per_token_group_quant_fp8",
+    "per_token_group_quant_fp8_tma_aligned",
     "w8a8_block_fp8_matmul",
     "w8a8_triton_block_scaled_mm",
 ]
