@@ -768,8 +768,8 @@ class Decode:
         gemm = (lambda *a: self.tob.awq_gemm_silu_and_mul(*a)) if j == 2 else \
             (lambda *a: self.tob.awq_gemm(*a, 1))
         # this library's kernels per call: the GEMM, and the activation after it where the GEMM
-        # has no fused epilogue (gate_up, K = 4096, above 32 tokens)
-        own = 2 if (j == 2 and self.m > 32) else 1
+        # has no fused epilogue (gate_up, K = 4096: 1-2 tokens and above 32 tokens)
+        own = 2 if (j == 2 and (self.m > 32 or self.m <= 2)) else 1
         if self.world == 1:
             self._launches += own
             return gemm(x, *w)

@@ -224,9 +224,10 @@ TO_API int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void*
  * (block 2j = gate columns 8j..8j+7, block 2j + 1 = up columns 8j..8j+7; N = 2F, N % 16 == 0);
  * y[M, F] = act(gate) * up, act TO_ACT_SILU or TO_ACT_GELU_TANH, equal to to_awq_gemm on the
  * un-interleaved weights followed by the activation kernel on its two halves (each GEMM output
- * rounded to the scales' dtype first). The decode and stream-K kernels apply it in their
- * epilogue on the shapes to_awq_gemm routes to them; other shapes run the GEMM into the
- * workspace and the activation after it.
+ * rounded to the scales' dtype first). The decode kernel (3-32 tokens) and the stream-K kernel
+ * apply it in their epilogue on the shapes to_awq_gemm routes to them; other shapes (and 1-2
+ * tokens, whose next layer streams faster after a separate activation launch) run the GEMM
+ * into the workspace and the activation after it.
  * Bit for bit it is to_awq_gemm on these weights followed by the activation. The workspace is
  * to_awq_gemm_act_workspace_size(M, K, N, group_size) bytes, 16-byte aligned. */
 #define TO_ACT_SILU 0

@@ -360,9 +360,10 @@ def test_fnuz_quantisers_vs_oracle(cuda, dtype, n):
 
 def test_fnuz_gemm_rejected(cuda):
     a = torch.zeros(4, 16, device=cuda).to(_FNUZ)
-    s = torch.ones(4, 1, device=cuda)
+    b = torch.zeros(16, 16, device=cuda).to(_FNUZ)
     with pytest.raises(NotImplementedError):
-        tob.w8a8_block_fp8_matmul(a, a, s, s, [16, 16])
+        tob.w8a8_block_fp8_matmul(a, b, torch.ones(4, 1, device=cuda),
+                                  torch.ones(1, 1, device=cuda), [16, 16])
 
 
 @pytest.mark.parametrize("rows,k,g,ue8m0", [(5, 256, 128, False), (33, 7168, 128, True),

@@ -102,9 +102,13 @@ def _worker(rank, world, port, q):
             full = tob.awq_gemm(x, qw, s, qz, 1)
             want = tob.silu_and_mul(full[:, :f], full[:, f:])
             torch.cuda.synchronize()
+            # 16 tokens: the local fused kernel is the gathering one's arithmetic; one token on
+            # a layer this small runs locally on the streaming GEMV instead, so within tolerance
+            same = (torch.equal(ya, local) if m > 2 else
+                    bool(torch.allclose(ya.float(), local.float(), rtol=4e-2, atol=4e-2)))
             report[f"act{m}"] = (
                 float((ya.float() - want.float()).abs().max()),
-                bool(torch.equal(ya, local)),
+                same,
                 0.0,
                 float(want.float().abs().max()),
             )
