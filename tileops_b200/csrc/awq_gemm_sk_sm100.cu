@@ -51,8 +51,11 @@ constexpr int kSkWBytes = kSkBK * kSkWords * 4;             // packed block: 8 K
 constexpr int kSkSZBytes = 2048;                            // scale + zero rows (up to 2)
 constexpr int kSkStageBytes = kSkABytes + kSkWBytes + kSkSZBytes;  // 26 KB
 constexpr int kSkBBytes = kSkBK * kSkBN * 2;                // expanded block: 32 KB
-constexpr int kSkBBufs = 2;
-constexpr int kSkStages = 6;
+#ifndef TOB_SK_BBUFS
+#define TOB_SK_BBUFS 2
+#endif
+constexpr int kSkBBufs = TOB_SK_BBUFS;  // expanded blocks in flight (3: measurement builds)
+constexpr int kSkStages = kSkBBufs == 2 ? 6 : 4;
 constexpr size_t kSkSmem = (size_t)kSkStages * kSkStageBytes + (size_t)kSkBBufs * kSkBBytes + 256;
 // Expanded-weight layout (MN-major, 128B swizzle): 1 KB atoms of 8 K rows x 64 columns; the 8
 // atoms of a 64-column strip are contiguous along K, strips 8 KB apart.
@@ -63,7 +66,9 @@ constexpr int kSkMaxOut = 8;
 // Row stride (floats) of the owner's sum of the later parts in shared memory: 16 bytes of
 // padding per row, so a warp's lanes (one row each) read the same columns conflict-free.
 constexpr int kSkRedLd = kSkBN + 4;
-static_assert(128 * kSkRedLd * 4 <= kSkStages * kSkStageBytes, "owner sums fit in the ring");
+// (the stage ring and the expanded-weight buffers after it, both idle by then)
+static_assert(128 * kSkRedLd * 4 <= kSkStages * kSkStageBytes + kSkBBufs * kSkBBytes,
+              "owner sums fit in the ring");
 static_assert(kSkSmem <= 232448, "shared memory");
 static_assert(kSkStageBytes % 1024 == 0, "stages keep the 1 KB alignment of the swizzled x");
 
@@ -356,7 +361,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         if (lane == 0) sk_st_release(flags + ((size_t)cur_t * maxc + slot) * 4 + q, epoch);
       } else {
         // The owner. Later parts exist (nc > 0) only in this CTA's last part, when its stage
-        // ring is idle: wait for their flags, then the four epilogue warps add them column-
+        // ring and expanded-weight buffers are idle: wait for their flags, then the four epilogue warps add them column-
         // parallel (thread e takes float4 e, e + 128, ... of the [M, 256] tile, the
         // contributors' values of one float4 loaded together and added in K order) into
         // shared memory, and each lane adds its row of that sum to its own TMEM row.

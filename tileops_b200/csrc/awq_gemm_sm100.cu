@@ -33,7 +33,6 @@ namespace sm100 {
 namespace {
 
 constexpr int kAwqBK = 64;
-constexpr int kAwqBBufs = 2;    // dequantised B tiles
 constexpr int kAwqDqWarps = 8;  // dequantising warps
 constexpr int kAwqThreads = 64 + 32 * kAwqDqWarps + 128;
 constexpr int kAwqEpiWarp0 = 2 + kAwqDqWarps;
@@ -47,8 +46,9 @@ constexpr uint32_t kAwqBLbo = 8192, kAwqBSbo = 1024;
 // so each packed weight is expanded once per 128 HALVES rows of x (the expansion's shared-memory
 // stores and the tensor core's B reads bound this kernel; 256-row tiles halve them per MMA).
 // BN = 256, or 224 when 224-column tiles fill the SMs in fewer rounds.
-template <int HALVES, int BN>
+template <int HALVES, int BN, int BBUFS = 2>
 struct AwqCfg {
+  static constexpr int kBBufs = BBUFS;  // dequantised B tiles in flight
   static constexpr int kBM = 128 * HALVES;
   static constexpr int kABytes = kBM * 128;          // x tile, 64 bf16/fp16 per row
   static constexpr int kWBytes = kAwqBK * BN / 2;    // packed words (64 rows x BN / 8)
@@ -59,15 +59,15 @@ struct AwqCfg {
   static constexpr int kAccBufs = kAccCols <= 256 ? 2 : 1;
   static constexpr int kAccStride = kAccBufs == 2 ? 256 : 0;
   static constexpr int kStages =
-      (int)((232448 - 256 - kAwqBBufs * kBBytes - kAwqOutBytes) / kStageBytes) > 5
+      (int)((232448 - 256 - kBBufs * kBBytes - kAwqOutBytes) / kStageBytes) > 5
           ? 5
-          : (int)((232448 - 256 - kAwqBBufs * kBBytes - kAwqOutBytes) / kStageBytes);
+          : (int)((232448 - 256 - kBBufs * kBBytes - kAwqOutBytes) / kStageBytes);
   static constexpr size_t kSmem =
-      (size_t)kStages * kStageBytes + (size_t)kAwqBBufs * kBBytes + kAwqOutBytes + 256;
+      (size_t)kStages * kStageBytes + (size_t)kBBufs * kBBytes + kAwqOutBytes + 256;
   // dequantisation: thread dt owns word column dt % kWords of rows dt / kWords + kRowStep i
   static constexpr int kWords = BN / 8;
   static constexpr int kRowStep = (32 * kAwqDqWarps) / kWords;
-  static_assert(kStages >= 3 && kSmem <= 232448, "shared memory");
+  static_assert(kStages >= 2 && kSmem <= 232448, "shared memory");
   static_assert(BN % 32 == 0 && BN <= 256, "tile width");
 };
 
@@ -83,7 +83,7 @@ __device__ __forceinline__ int awq_k_start(int t, int kblocks) {
   return (int)(((unsigned)t * 5u) % (unsigned)kblocks);
 }
 
-template <typename T, int HALVES, int BN>
+template <typename T, int HALVES, int BN, int BBUFS>
 __global__ void __launch_bounds__(kAwqThreads, 1)
     k_awq_gemm_sm100(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
@@ -91,7 +91,8 @@ __global__ void __launch_bounds__(kAwqThreads, 1)
                      int K, int G, int group_rows, int* err) {
   using H = Half2Of<T>;
   using H2 = typename H::type;
-  using C = AwqCfg<HALVES, BN>;
+  using C = AwqCfg<HALVES, BN, BBUFS>;
+  constexpr int kAwqBBufs = C::kBBufs;
   constexpr Kind KD = std::is_same<T, __half>::value ? Kind::F16 : Kind::BF16;
   using Tr = KindTraits<KD>;
   constexpr int kSBytes = 2 * BN * 2;  // up to 2 scale rows (group 32)
@@ -404,12 +405,12 @@ inline int64_t awq_rounds(int64_t M, int64_t N, int bm, int bn, int64_t sms) {
   return ceil_div(tiles, sms);
 }
 
-template <typename T, int HALVES, int BN>
+template <typename T, int HALVES, int BN, int BBUFS = 2>
 int launch_awq_gemm_cfg(const void* x, const int32_t* qw, const void* s, const int32_t* qz,
                         void* const* ys, int ny, int64_t n_full, int64_t ycol0, int64_t M,
                         int64_t K, int64_t N, int64_t G, int dtype, cudaStream_t st) {
-  using C = AwqCfg<HALVES, BN>;
-  auto kern = k_awq_gemm_sm100<T, HALVES, BN>;
+  using C = AwqCfg<HALVES, BN, BBUFS>;
+  auto kern = k_awq_gemm_sm100<T, HALVES, BN, BBUFS>;
   const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)C::kSmem);
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "awq tcgen05 gemm: shared memory attribute");
   if (ny < 1 || ny > kAwqMaxRanks) return fail(TO_EINVAL, "awq tcgen05 gemm: %d outputs", ny);
@@ -442,11 +443,21 @@ int launch_awq_gemm(const void* x, const int32_t* qw, const void* s, const int32
     const char* v = tuning_env("TOB_AWQ_TILE");
     return v != nullptr && v[0] == '1';
   }();
+  // Measurement switch TOB_AWQ_BBUFS=3: three dequantised B tiles in flight for the 256 x 224
+  // tiles (one TMA stage fewer).
+  static const bool deep = [] {
+    const char* v = tuning_env("TOB_AWQ_BBUFS");
+    return v != nullptr && v[0] == '3';
+  }();
   const int64_t sms = sm_count();
   if (!narrow && M >= 256) {
-    if (awq_rounds(M, N, 256, 224, sms) * 224 < awq_rounds(M, N, 256, 256, sms) * 256)
+    if (awq_rounds(M, N, 256, 224, sms) * 224 < awq_rounds(M, N, 256, 256, sms) * 256) {
+      if (deep)
+        return launch_awq_gemm_cfg<T, 2, 224, 3>(x, qw, s, qz, ys, ny, n_full, ycol0, M, K, N, G,
+                                                 dtype, st);
       return launch_awq_gemm_cfg<T, 2, 224>(x, qw, s, qz, ys, ny, n_full, ycol0, M, K, N, G,
                                             dtype, st);
+    }
     return launch_awq_gemm_cfg<T, 2, 256>(x, qw, s, qz, ys, ny, n_full, ycol0, M, K, N, G, dtype,
                                           st);
   }
