@@ -978,8 +978,11 @@ struct PairCfg {
   static_assert(kSmem <= 232448, "shared memory");
 };
 
-template <Kind KD, int BN, int STAGES, int KC>
-__global__ void __launch_bounds__(kPairThreads, 1)
+// MINB: CTAs per SM the registers are sized for (2 lets a CTA of the next launch in the stream
+// become resident, under launch overlap, while this one still runs -- with a ring that fits
+// twice in shared memory).
+template <Kind KD, int BN, int STAGES, int KC, int MINB>
+__global__ void __launch_bounds__(kPairThreads, MINB)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC16,
                 int M, int N, int K, Epi ep, int* err) {
@@ -1494,11 +1497,11 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
   }
 }
 
-template <Kind KD, int BN, int STAGES, int KC>
+template <Kind KD, int BN, int STAGES, int KC, int MINB = 1>
 int launch_gemm_pair(const void* a, const void* b, int64_t M, int64_t N, int64_t K, const Epi& ep,
                      cudaStream_t st) {
   using C = PairCfg<KD, BN, STAGES, KC>;
-  auto kern = k_gemm_pair<KD, BN, STAGES, KC>;
+  auto kern = k_gemm_pair<KD, BN, STAGES, KC, MINB>;
   const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)C::kSmem);
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "tcgen05 2-CTA gemm: shared memory attribute");
   CUtensorMap ta, tb, tc32, tc16;
@@ -1585,9 +1588,16 @@ int launch_gemm(const void* a, const void* b, int64_t M, int64_t N, int64_t K, c
       const char* v = tuning_env("TOB_PAIR_SLICES");
       return v == nullptr ? 2 : atoi(v);
     }();
+    // Measurement override TOB_PAIR_STAGES=2: a 2-stage ring (104 KB) with registers for two
+    // CTAs per SM, so the next launch's CTAs start during this one's tail.
+    static const int pair_stages = [] {
+      const char* v = tuning_env("TOB_PAIR_STAGES");
+      return v == nullptr ? 4 : atoi(v);
+    }();
     if ((K * KindTraits<KD>::kElemBytes) % 128 != 0 || slices == 1)
       return launch_gemm_pair<KD, 160, 8, 1>(a, b, M, N, K, ep, st);
     if (slices == 4) return launch_gemm_pair<KD, 160, 2, 4>(a, b, M, N, K, ep, st);
+    if (pair_stages == 2) return launch_gemm_pair<KD, 160, 2, 2, 2>(a, b, M, N, K, ep, st);
     return launch_gemm_pair<KD, 160, 4, 2>(a, b, M, N, K, ep, st);
   }
   if (ks2_on && M > 128 && M <= 256 && 2 * tiles(256, 160) <= sms && K >= 2 * (128 / KindTraits<KD>::kElemBytes))
