@@ -381,3 +381,23 @@ def test_group_quant_fp8_tma_aligned_scales(cuda, rows, k, g, ue8m0):
     assert s.data_ptr() % 16 == 0
     assert torch.equal(q.view(torch.uint8), wq.view(torch.uint8))
     assert torch.equal(s, ws)
+
+
+def test_symmetric_quant_captures_in_a_graph(cuda):
+    """quantize_per_tensor inside a CUDA graph capture: the scale's host-side value check (a
+    device read) is skipped while capturing, and replays match eager calls."""
+    x = torch.randn(4096, device=cuda)
+    s = torch.tensor([0.05], device=cuda)
+    want = tob.quantize_per_tensor(x, s)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        tob.quantize_per_tensor(x, s)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = tob.quantize_per_tensor(x, s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    del g

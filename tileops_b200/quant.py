@@ -26,7 +26,9 @@ def _validate_scale_tensor(scale: torch.Tensor, *, op: str, numel: int = 1) -> t
         raise TypeError(f"{op}: scale must be float32 (got {scale.dtype})")
     if scale.numel() != numel:
         raise ValueError(f"{op}: scale must have {numel} element(s), got {scale.numel()}")
-    if torch.any(scale <= 0):
+    # The value check reads the device tensor back (a host sync), as the reference does; inside
+    # a CUDA graph capture, where a sync is not allowed, the values are the caller's contract.
+    if not (scale.is_cuda and torch.cuda.is_current_stream_capturing()) and torch.any(scale <= 0):
         raise ValueError(f"{op}: scale values must be positive")
     return scale.contiguous().reshape(numel)
 
