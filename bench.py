@@ -792,7 +792,7 @@ class Decode:
         self._launches = 0
         for qkv, o, gu, down in self.layers:
             h = self._linear(x, qkv, 0)
-            a = self._linear(h[:, :4096].contiguous(), o, 1)
+            a = self._linear(h[:, :4096], o, 1)  # read in place where the kernel can
             act = self._linear(a, gu, 2)  # silu(gate) * up, [M, 14336]
             x = self._linear(act, down, 3)
         self.launches_per_step = self._launches

@@ -202,6 +202,14 @@ TO_API size_t to_awq_gemm_workspace_size(int64_t M, int64_t K, int64_t N, int64_
 TO_API int to_awq_gemm(const void* x, const int32_t* qweight, const void* scales, int s_dtype,
                 const int32_t* qzeros, void* y, int64_t M, int64_t K, int64_t N,
                 int64_t group_size, void* workspace, size_t workspace_bytes, void* stream);
+/* to_awq_gemm with x rows ldx elements apart (ldx >= K, a multiple of 8): a slice of a wider
+ * activation, such as the first K columns of a fused qkv output, read in place. Runs where
+ * to_awq_gemm would use the decode kernel; TO_EUNSUPPORTED (nothing launched, no error recorded)
+ * for other shapes: make x contiguous and call to_awq_gemm. Library extension. */
+TO_API int to_awq_gemm_strided(const void* x, int64_t ldx, const int32_t* qweight,
+                               const void* scales, int s_dtype, const int32_t* qzeros, void* y,
+                               int64_t M, int64_t K, int64_t N, int64_t group_size,
+                               void* workspace, size_t workspace_bytes, void* stream);
 /* Library extension for N-sharded layers (no reference counterpart; it fuses to_awq_gemm on a
  * rank's column slice with the all-gather that follows it). The group's `world` ranks each
  * hold N = N_full / world output columns of qweight/scales/qzeros; this rank computes its

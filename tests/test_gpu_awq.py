@@ -362,3 +362,18 @@ def test_stream_k_graph_replays_with_new_inputs(cuda):
         torch.cuda.synchronize()
         assert torch.equal(out, tob.awq_gemm(x, qw, s, qz, 1)), i
     del graph
+
+
+@pytest.mark.parametrize("m,k,n", [(16, 4096, 4096), (4, 4096, 6144), (1, 4096, 4096),
+                                   (48, 1024, 2048)])
+def test_gemm_strided_input_read_in_place(cuda, m, k, n):
+    """A row-strided slice of a wider activation (the o projection's input from a fused qkv
+    output): the decode kernel reads it in place through its tensor map, other paths copy it
+    first; the result equals the contiguous input's bit for bit."""
+    gen = torch.Generator().manual_seed(m + k + n)
+    qw, s, qz = (t.to(cuda) for t in make_awq(k, n, 128, torch.float16, gen))
+    wide = torch.randn(m, k + 2048, generator=gen).half().to(cuda)
+    x = wide[:, :k]
+    assert not x.is_contiguous()
+    y = tob.awq_gemm(x, qw, s, qz, 1)
+    assert torch.equal(y, tob.awq_gemm(x.contiguous(), qw, s, qz, 1))

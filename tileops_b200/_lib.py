@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "to_awq_dequant": (_I, [_P, _P, _I, _P, _P, _L, _L, _L, _P]),
     "to_awq_gemm_workspace_size": (_S, [_L, _L, _L, _L]),
     "to_awq_gemm": (_I, [_P, _P, _P, _I, _P, _P, _L, _L, _L, _L, _P, _S, _P]),
+    "to_awq_gemm_strided": (_I, [_P, _L, _P, _P, _I, _P, _P, _L, _L, _L, _L, _P, _S, _P]),
     "to_awq_gemm_gather": (_I, [_P, _P, _P, _I, _P, ctypes.POINTER(_P), _I, _I, _L, _L, _L, _L,
                                 _P, _S, _P]),
     "to_awq_gemm_act_workspace_size": (_S, [_L, _L, _L, _L]),

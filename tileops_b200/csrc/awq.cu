@@ -658,7 +658,8 @@ int awq_decode_gather_launch(const void* x, const int32_t* qw, const void* s, in
                              size_t ws_bytes, cudaStream_t st, int act = -1);
 int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
-                      void* ws, size_t ws_bytes, cudaStream_t st, int act = -1);
+                      void* ws, size_t ws_bytes, cudaStream_t st, int act = -1,
+                      int64_t ldx = 0);
 int act_mul_interleaved_launch(const void* y, void* c, int dtype, int64_t rows, int64_t cols,
                                int64_t ldy, int64_t ldc, int act, cudaStream_t st);
 size_t awq_sk_workspace(int64_t M, int64_t K, int64_t N, int64_t G, int s_dtype);
@@ -909,6 +910,25 @@ int to_awq_gemm_act_gather(const void* x, const int32_t* qweight, const void* sc
                 "awq_gemm_act_gather: only the decode and stream-K kernels gather the activation; "
                 "run to_awq_gemm_act and an all-gather instead");
   return rc;
+}
+
+int to_awq_gemm_strided(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                        int s_dtype, const int32_t* qzeros, void* y, int64_t M, int64_t K,
+                        int64_t N, int64_t group_size, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  int rc = check_awq_shapes("awq_gemm", K, N, group_size);
+  if (rc) return rc;
+  if (M <= 0) return fail(TO_EINVAL, "awq_gemm: invalid M=%lld", (long long)M);
+  if (ldx < K) return fail(TO_EINVAL, "awq_gemm: row stride %lld < K=%lld", (long long)ldx,
+                           (long long)K);
+  // The decode kernel reads x through its tensor map, which takes any 16-byte row stride;
+  // shapes routed elsewhere need x contiguous.
+  if (M <= 32 && !sk_wanted(M, K, N) && decode_enabled() && awq_decode_wanted(M, K, N)) {
+    rc = awq_decode_launch(x, qweight, scales, s_dtype, qzeros, y, M, K, N, group_size, workspace,
+                           workspace_bytes, (cudaStream_t)stream, -1, ldx);
+    if (rc != TO_EUNSUPPORTED) return rc;
+  }
+  return TO_EUNSUPPORTED;
 }
 
 int to_awq_gemm_gather(const void* x, const int32_t* qweight, const void* scales, int s_dtype,

@@ -77,6 +77,7 @@ constexpr int kDecMaxOut = 8;
 struct DecOut {
   void* y[kDecMaxOut];
   int ny, ld, col0, act;
+  int64_t ldx;  // row stride of x in elements (0: K); read by the host side only (TMA map)
 };
 
 struct DecPlan {
@@ -739,7 +740,7 @@ int launch_decode(const void* x, const int32_t* qw, const void* s, const int32_t
   const cudaError_t attr_err = ensure_smem_attr((const void*)kern, (int)plan.smem);
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "awq decode gemm: shared memory attribute");
   CUtensorMap tx, tw, ts, tz;
-  int rc = make_tmap_x_blocks(&tx, x, M, K, 8 * NT, DecGeom<WK>::kRows / 64);
+  int rc = make_tmap_x_blocks(&tx, x, M, K, 8 * NT, DecGeom<WK>::kRows / 64, out.ldx);
   // the packed words as 16-bit pairs, so that a 128-byte swizzled box holds 32 words
   if (!rc) rc = make_tmap_kmajor(&tw, qw, K, N / 4, 2, 256);
   if (!rc) rc = make_tmap_plain(&ts, s, K / G, N, 2, 256, plan.srows);
@@ -911,10 +912,11 @@ int decode_dispatch(const void* x, const int32_t* qw, const void* s, int s_dtype
 // weight interleaved in blocks of 8 columns.
 int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                       const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
-                      void* ws, size_t ws_bytes, cudaStream_t st, int act) {
+                      void* ws, size_t ws_bytes, cudaStream_t st, int act, int64_t ldx) {
   if (!sm100::dec_supported(M, K, N, G, s_dtype)) return TO_EUNSUPPORTED;
   if (!aligned16(x) || !aligned16(qw) || !aligned16(s) || !aligned16(qz) || !aligned16(y))
     return TO_EUNSUPPORTED;
+  if (ldx != 0 && (ldx < K || ldx % 8 != 0)) return TO_EUNSUPPORTED;  // 16-byte row strides
   if (ws != nullptr && !aligned16(ws)) return TO_EUNSUPPORTED;
   sm100::DecOut out = {};
   out.y[0] = y;
@@ -922,6 +924,7 @@ int awq_decode_launch(const void* x, const int32_t* qw, const void* s, int s_dty
   out.ld = (int)(act >= 0 ? N / 2 : N);
   out.col0 = 0;
   out.act = act;
+  out.ldx = ldx;
   return decode_dispatch(x, qw, s, s_dtype, qz, out, M, K, N, G, ws, ws_bytes, st);
 }
 

@@ -1378,30 +1378,31 @@ int make_tmap_plain(CUtensorMap* out, const void* ptr, int64_t rows, int64_t col
   return TO_OK;
 }
 
-// Activations x [M, K] (16-bit, K % 64 == 0) viewed as 64-element blocks: dims
-// {64, M, K/64} with strides {K*2, 128} bytes; one box {64, box_tokens, box_blocks} lands as
-// box_blocks tiles of [box_tokens x 128 B], each in the 128-byte-swizzle layout. Cached.
+// Activations x [M, K] (16-bit, K % 64 == 0, rows ld elements apart) viewed as 64-element
+// blocks: dims {64, M, K/64} with strides {ld*2, 128} bytes; one box {64, box_tokens, box_blocks}
+// lands as box_blocks tiles of [box_tokens x 128 B], each in the 128-byte-swizzle layout. Cached.
 int make_tmap_x_blocks(CUtensorMap* out, const void* ptr, int64_t M, int64_t K, int box_tokens,
-                       int box_blocks) {
+                       int box_blocks, int64_t ld) {
+  if (ld <= 0) ld = K;
   struct Key {
     const void* p;
-    int64_t m, k;
+    int64_t m, k, ld;
     int bt, bb;
     bool operator==(const Key& o) const {
-      return p == o.p && m == o.m && k == o.k && bt == o.bt && bb == o.bb;
+      return p == o.p && m == o.m && k == o.k && ld == o.ld && bt == o.bt && bb == o.bb;
     }
   };
   struct Hash {
     size_t operator()(const Key& k) const {
       return std::hash<const void*>()(k.p) ^ (size_t)(k.m * 1315423911u) ^
-             (size_t)(k.k * 2654435761u) ^ (size_t)(k.bt * 131 + k.bb);
+             (size_t)(k.k * 2654435761u) ^ (size_t)(k.ld * 40503u) ^ (size_t)(k.bt * 131 + k.bb);
     }
   };
   static std::mutex mu;
   static std::unordered_map<Key, CUtensorMap, Hash> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const Key key{(const char*)ptr + ((int64_t)dev << 56), M, K, box_tokens, box_blocks};
+  const Key key{(const char*)ptr + ((int64_t)dev << 56), M, K, ld, box_tokens, box_blocks};
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
@@ -1413,7 +1414,7 @@ int make_tmap_x_blocks(CUtensorMap* out, const void* ptr, int64_t M, int64_t K, 
   EncodeFn encode = get_encode();
   if (!encode) return fail(TO_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   cuuint64_t dims[3] = {64, (cuuint64_t)M, (cuuint64_t)(K / 64)};
-  cuuint64_t strides[2] = {(cuuint64_t)(K * 2), 128};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), 128};
   cuuint32_t box[3] = {64, (cuuint32_t)box_tokens, (cuuint32_t)box_blocks};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(ptr), dims, strides,

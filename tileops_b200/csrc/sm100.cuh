@@ -269,10 +269,11 @@ int make_tmap_out16(CUtensorMap* out, const void* ptr, int64_t rows, int64_t col
 // (elem 2 or 4), inner box bytes a multiple of 16.
 int make_tmap_plain(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int elem,
                     int box_cols, int box_rows);
-// 16-bit activations [M, K] (K % 64 == 0) as {64, M, K/64} blocks: a box of box_tokens rows x
-// box_blocks 64-element blocks lands as box_blocks [box_tokens x 128 B] 128-byte-swizzled tiles.
+// 16-bit activations [M, K] (K % 64 == 0, rows ld >= K elements apart; ld = 0 means K) as
+// {64, M, K/64} blocks: a box of box_tokens rows x box_blocks 64-element blocks lands as
+// box_blocks [box_tokens x 128 B] 128-byte-swizzled tiles.
 int make_tmap_x_blocks(CUtensorMap* out, const void* ptr, int64_t M, int64_t K, int box_tokens,
-                       int box_blocks);
+                       int box_blocks, int64_t ld = 0);
 
 template <Kind K> struct KindTraits;
 template <> struct KindTraits<Kind::I8> {

@@ -177,7 +177,6 @@ def awq_gemm_triton(
     m, k, n, group_size = _gemm_args("awq_gemm_triton", input, qweight, scales, qzeros,
                                      split_k_iters)
     out_dtype = scales.dtype
-    x = input.to(out_dtype).contiguous()
     qw = _as_words(qweight)
     qz = _as_words(qzeros)
     s = scales.contiguous()
@@ -185,6 +184,19 @@ def awq_gemm_triton(
     lib = _lib.load()
     ws_bytes = lib.to_awq_gemm_workspace_size(m, k, n, group_size)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device) if ws_bytes else None
+    if (input.dtype == out_dtype and not input.is_contiguous() and input.stride(1) == 1
+            and input.stride(0) >= k and input.stride(0) % 8 == 0
+            and input.data_ptr() % 16 == 0):
+        # a row-strided slice (the first K columns of a wider activation): read in place where
+        # the kernel takes a row stride
+        rc = lib.to_awq_gemm_strided(input.data_ptr(), input.stride(0), qw.data_ptr(),
+                                     s.data_ptr(), _lib.DTYPE_CODES[out_dtype], qz.data_ptr(),
+                                     y.data_ptr(), m, k, n, group_size, _lib.ptr(ws), ws_bytes,
+                                     _lib.stream_ptr())
+        if rc != _lib.TO_EUNSUPPORTED:
+            _lib.check(rc, "awq_gemm_triton")
+            return y
+    x = input.to(out_dtype).contiguous()
     _lib.call("to_awq_gemm", x.data_ptr(), qw.data_ptr(), s.data_ptr(),
               _lib.DTYPE_CODES[out_dtype], qz.data_ptr(), y.data_ptr(), m, k, n, group_size,
               _lib.ptr(ws), ws_bytes, _lib.stream_ptr())
