@@ -1,5 +1,7 @@
-// Small-M AWQ W4A16 GEMM on sm_100a: y = x @ dequant(W) for 1 <= M <= 32, the decode regime
-// of tileops/quant_awq.py:112-155 (awq_gemm with a handful of tokens).
+// Small-M AWQ W4A16 GEMM on sm_100a: y = x @ dequant(W) for 1 <= M <= 64 (tileops/quant_awq.py:
+// 112-155, awq_gemm with a handful of tokens). The dispatch (awq.cu) sends it 33-64 tokens on
+// layers whose tensor-core tiles would leave most SMs idle, and the 1-32-token shapes the
+// stream-K decode kernel (awq_decode_sm100.cu) does not take.
 //
 // At decode sizes the layer is bound by streaming the packed int4 weights from HBM; the
 // design keeps every SM's share of them in flight and spends as few instructions as possible
@@ -450,7 +452,7 @@ int dispatch_small_m(const void* x, const int32_t* qw, const void* s, const int3
 }  // namespace
 }  // namespace sm100
 
-// Routes 1 <= M <= 32 to the TMA-fed small-M kernel when the shapes meet its TMA constraints;
+// Routes 1 <= M <= 64 to the TMA-fed small-M kernel when the shapes meet its TMA constraints;
 // TO_EUNSUPPORTED (nothing launched, no error recorded) otherwise.
 int awq_small_m_launch(const void* x, const int32_t* qw, const void* s, int s_dtype,
                        const int32_t* qz, void* y, int64_t M, int64_t K, int64_t N, int64_t G,
