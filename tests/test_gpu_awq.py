@@ -374,6 +374,6 @@ def test_gemm_strided_input_read_in_place(cuda, m, k, n):
     qw, s, qz = (t.to(cuda) for t in make_awq(k, n, 128, torch.float16, gen))
     wide = torch.randn(m, k + 2048, generator=gen).half().to(cuda)
     x = wide[:, :k]
-    assert not x.is_contiguous()
+    assert m == 1 or not x.is_contiguous()  # one row of a slice is contiguous
     y = tob.awq_gemm(x, qw, s, qz, 1)
     assert torch.equal(y, tob.awq_gemm(x.contiguous(), qw, s, qz, 1))
