@@ -630,22 +630,29 @@ __global__ void __launch_bounds__(DecGeom<WK>::kThreads, 1) k_awq_decode(
         for (int c = 32 + lane; c < nc; c += 32) fl[4 * c] = 0ull;
         if (!ok) break;
         if (out.act < 0) {
+          // The thread's 8 columns of rows m and m + 1: one 16-byte store per row and
+          // destination (the fewest transactions over NVLink for the peers' copies).
 #pragma unroll
-          for (int tt = 0; tt < NT; ++tt)
+          for (int tt = 0; tt < NT; ++tt) {
+            const int m = 8 * tt + 2 * q;
+            uint32_t r0[4], r1[4];
 #pragma unroll
             for (int p = 0; p < 4; ++p) {
-              const int c = col0 + 2 * p;
-              const int m = 8 * tt + 2 * q;
-              if (c < N) {
-                const H2 v0 = Half2Of<T>::from_floats(acc[p][tt][0], acc[p][tt][2]);
-                const H2 v1 = Half2Of<T>::from_floats(acc[p][tt][1], acc[p][tt][3]);
-                for (int d = 0; d < out.ny; ++d) {
-                  T* yd = static_cast<T*>(out.y[d]) + out.col0 + c;
-                  if (m < M) *reinterpret_cast<H2*>(yd + (size_t)m * out.ld) = v0;
-                  if (m + 1 < M) *reinterpret_cast<H2*>(yd + (size_t)(m + 1) * out.ld) = v1;
-                }
+              r0[p] = bits_of(Half2Of<T>::from_floats(acc[p][tt][0], acc[p][tt][2]));
+              r1[p] = bits_of(Half2Of<T>::from_floats(acc[p][tt][1], acc[p][tt][3]));
+            }
+            if (col0 < N) {
+              for (int d = 0; d < out.ny; ++d) {
+                T* yd = static_cast<T*>(out.y[d]) + out.col0 + col0;
+                if (m < M)
+                  *reinterpret_cast<uint4*>(yd + (size_t)m * out.ld) =
+                      make_uint4(r0[0], r0[1], r0[2], r0[3]);
+                if (m + 1 < M)
+                  *reinterpret_cast<uint4*>(yd + (size_t)(m + 1) * out.ld) =
+                      make_uint4(r1[0], r1[1], r1[2], r1[3]);
               }
             }
+          }
         } else {
           // Gate and up blocks alternate word by word, so this thread's word (g) and the word
           // of lane ^ 4 (g ^ 1) hold the gate and up sums of the same 8 columns. The even lane
@@ -656,7 +663,8 @@ __global__ void __launch_bounds__(DecGeom<WK>::kThreads, 1) k_awq_decode(
           const int pair0 = col0 - (is_gate ? 0 : 8);    // the gate word's first column
           const int a_col = (pair0 >> 1) + (is_gate ? 0 : 4);  // first output column here
 #pragma unroll
-          for (int tt = 0; tt < NT; ++tt)
+          for (int tt = 0; tt < NT; ++tt) {
+            uint32_t w0[2], w1[2];  // rows m, m + 1: outputs a_col .. a_col + 3
 #pragma unroll
             for (int pp = 0; pp < 2; ++pp) {
               float gv[4], uv[4];
@@ -673,21 +681,24 @@ __global__ void __launch_bounds__(DecGeom<WK>::kThreads, 1) k_awq_decode(
                 const T gt = from_f32<T>(gv[e]), ut = from_f32<T>(uv[e]);
                 r[e] = out.act == kSilu ? act_mul<T, kSilu>(gt, ut) : act_mul<T, kGeluTanh>(gt, ut);
               }
-              const int c = a_col + 2 * pp;
-              const int m = 8 * tt + 2 * q;
-              if (pair0 < N) {
-                H2 v0, v1;
-                v0.x = r[0];
-                v0.y = r[2];
-                v1.x = r[1];
-                v1.y = r[3];
-                for (int d = 0; d < out.ny; ++d) {
-                  T* yd = static_cast<T*>(out.y[d]) + out.col0 + c;
-                  if (m < M) *reinterpret_cast<H2*>(yd + (size_t)m * out.ld) = v0;
-                  if (m + 1 < M) *reinterpret_cast<H2*>(yd + (size_t)(m + 1) * out.ld) = v1;
-                }
+              H2 v0, v1;
+              v0.x = r[0];
+              v0.y = r[2];
+              v1.x = r[1];
+              v1.y = r[3];
+              w0[pp] = bits_of(v0);
+              w1[pp] = bits_of(v1);
+            }
+            const int m = 8 * tt + 2 * q;
+            if (pair0 < N) {
+              for (int d = 0; d < out.ny; ++d) {
+                T* yd = static_cast<T*>(out.y[d]) + out.col0 + a_col;
+                if (m < M) *reinterpret_cast<uint2*>(yd + (size_t)m * out.ld) = make_uint2(w0[0], w0[1]);
+                if (m + 1 < M)
+                  *reinterpret_cast<uint2*>(yd + (size_t)(m + 1) * out.ld) = make_uint2(w1[0], w1[1]);
               }
             }
+          }
         }
       }
     }
