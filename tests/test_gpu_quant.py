@@ -401,3 +401,37 @@ def test_symmetric_quant_captures_in_a_graph(cuda):
     torch.cuda.synchronize()
     assert torch.equal(out, want)
     del g
+
+
+def _midpoint_groups() -> np.ndarray:
+    """Groups of 16 fp32 values: the group's absmax A first, then 15 values x whose quotient
+    x / (A / 448) lies on or within four fp32 ulps of an e4m3 rounding midpoint."""
+    vals = np.unique(np.abs(numerics.E4M3_VALUES[~np.isnan(numerics.E4M3_VALUES)]))
+    mids = ((vals[:-1].astype(np.float64) + vals[1:]) / 2).astype(np.float32)
+    gen = np.random.default_rng(21)
+    groups = []
+    for amax in (448.0, 1.0, 3.7, 1e-3, 12345.678, 2.0 ** -20):
+        a = np.float32(amax)
+        scale = np.float32(a / np.float32(448.0))
+        for k in range(-4, 5):
+            x = (mids * scale).astype(np.float32)
+            step = np.float32(np.inf) if k > 0 else np.float32(-np.inf)
+            for _ in range(abs(k)):
+                x = np.nextafter(x, step)
+            x = x * np.where(gen.random(x.size) < 0.5, -1.0, 1.0).astype(np.float32)
+            x = x[np.abs(x) < a]
+            for c in range(0, x.size, 15):
+                chunk = x[c:c + 15]
+                groups.append(np.concatenate([[a], chunk, np.zeros(15 - chunk.size, np.float32)]))
+    return np.stack(groups).astype(np.float32)
+
+
+def test_group_quant_fp8_quotients_at_e4m3_midpoints(cuda):
+    """The kernel forms x / scale as x * (1 / scale) and divides exactly only near an e4m3
+    rounding midpoint: on quotients on and around every midpoint, across the normal and
+    subnormal e4m3 range, its codes must be those of the exact IEEE division (the oracle)."""
+    x = _midpoint_groups()
+    q, s = tob.per_token_group_quant_fp8(torch.from_numpy(x).to(cuda), 16)
+    wq, ws = ofp8.group_quant(x, 16)
+    assert np.array_equal(s.cpu().numpy(), ws)
+    assert np.array_equal(_codes(q), wq)

@@ -204,6 +204,22 @@ __device__ __forceinline__ uint8_t nan_code_div(float x, bool neg_x, bool nan_sc
   return (isnan(x) && neg_x) ? (uint8_t)0xFF : (uint8_t)0x7F;
 }
 
+// x / scale for an e4m3fn code without a division per element. With r = 1 / scale rounded to
+// fp32, the product x * r lies within two ulps of the correctly rounded quotient, and the e4m3
+// code changes only across a rounding midpoint of the e4m3 grid (3 mantissa bits, so a midpoint
+// has bit 19 set and bits 0-18 clear in the fp32 mantissa). The product therefore gives the
+// same code unless it lies within four ulps of such a midpoint, or below 2^-6 where the e4m3
+// grid is subnormal; those take the exact IEEE quotient. (A value within two ulps of a power of
+// two rounds to that power of two either way.)
+__device__ __forceinline__ float quot_for_e4m3(float x, float scale, float r) {
+  const float y = x * r;
+  const uint32_t a = __float_as_uint(y) & 0x7FFFFFFFu;
+  const uint32_t low = a & 0xFFFFFu;  // mantissa bits below the 3 that e4m3 keeps
+  const bool near_mid = low - 0x7FFFCu <= 8u;
+  if (near_mid || a < 0x3C800000u) return __fdiv_rn(x, scale);
+  return y;
+}
+
 // Sign bit of a stored value.
 __device__ __forceinline__ bool sign_of(float v) { return __float_as_uint(v) >> 31; }
 __device__ __forceinline__ bool sign_of(__half v) { return __half_as_ushort(v) >> 15; }
@@ -293,19 +309,37 @@ __global__ void __launch_bounds__(1024) k_group_quant(const GroupSrc<T, ACT> src
     if (FP8 && ue8m0 && !nan_group) scale = ue8m0_round(scale);
     if (active && lane == 0) scales[scale_offset(g, sl)] = scale;
     uint8_t* qg = qout + g * (int64_t)G;
+    // e4m3fn codes from x * (1 / scale) (quot_for_e4m3) when the scale is a normal number whose
+    // reciprocal is one too; otherwise (NaN, inf, 0 or extreme scales) every element divides.
+    const bool fast = Q == kQE4M3 && scale >= 1.2e-38f && scale <= 8.0e37f;
+    const float rcp = fast ? __frcp_rn(scale) : 0.0f;
     auto emit = [&](int v, const Pack<T, V>& t) {
       Pack<uint8_t, V> o;
+      if constexpr (Q == kQE4M3 && V % 2 == 0) {
 #pragma unroll
-      for (int j = 0; j < V; ++j) {
-        const float xv = to_f32(t.v[j]);
-        const float y = __fdiv_rn(xv, scale);
-        if (Q == kQE4M3) {
-          o.v[j] = isnan(y) ? nan_code_div(xv, sign_of(t.v[j]), nan_group)
-                            : f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
-        } else if (Q == kQE4M3Fnuz) {
-          o.v[j] = isnan(y) ? (uint8_t)0x80 : f32_to_e4m3fnuz(fminf(fmaxf(y, -224.f), 224.f));
-        } else {
-          o.v[j] = (uint8_t)rne_clamp_i8(y);
+        for (int j = 0; j < V; j += 2) {
+          const float x0 = to_f32(t.v[j]), x1 = to_f32(t.v[j + 1]);
+          const float y0 = fast ? quot_for_e4m3(x0, scale, rcp) : __fdiv_rn(x0, scale);
+          const float y1 = fast ? quot_for_e4m3(x1, scale, rcp) : __fdiv_rn(x1, scale);
+          const uint16_t pr = f32x2_to_e4m3x2(fminf(fmaxf(y0, -448.f), 448.f),
+                                              fminf(fmaxf(y1, -448.f), 448.f));
+          o.v[j] = isnan(y0) ? nan_code_div(x0, sign_of(t.v[j]), nan_group) : (uint8_t)(pr & 0xFF);
+          o.v[j + 1] =
+              isnan(y1) ? nan_code_div(x1, sign_of(t.v[j + 1]), nan_group) : (uint8_t)(pr >> 8);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          const float xv = to_f32(t.v[j]);
+          const float y = fast ? quot_for_e4m3(xv, scale, rcp) : __fdiv_rn(xv, scale);
+          if (Q == kQE4M3) {
+            o.v[j] = isnan(y) ? nan_code_div(xv, sign_of(t.v[j]), nan_group)
+                              : f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
+          } else if (Q == kQE4M3Fnuz) {
+            o.v[j] = isnan(y) ? (uint8_t)0x80 : f32_to_e4m3fnuz(fminf(fmaxf(y, -224.f), 224.f));
+          } else {
+            o.v[j] = (uint8_t)rne_clamp_i8(y);
+          }
         }
       }
       st_pack<uint8_t, V>(qg + (int64_t)v * V, o);
