@@ -403,16 +403,22 @@ def test_symmetric_quant_captures_in_a_graph(cuda):
     del g
 
 
-def _midpoint_groups() -> np.ndarray:
+def _midpoint_groups(kind: str) -> np.ndarray:
     """Groups of 16 fp32 values: the group's absmax A first, then 15 values x whose quotient
-    x / (A / 448) lies on or within four fp32 ulps of an e4m3 rounding midpoint."""
-    vals = np.unique(np.abs(numerics.E4M3_VALUES[~np.isnan(numerics.E4M3_VALUES)]))
-    mids = ((vals[:-1].astype(np.float64) + vals[1:]) / 2).astype(np.float32)
+    x / scale lies on or within four fp32 ulps of a rounding boundary of the code grid: an e4m3
+    rounding midpoint (scale A / 448) or a half-integer (int8, scale A / 127)."""
+    if kind == "fp8":
+        vals = np.unique(np.abs(numerics.E4M3_VALUES[~np.isnan(numerics.E4M3_VALUES)]))
+        mids = ((vals[:-1].astype(np.float64) + vals[1:]) / 2).astype(np.float32)
+        qmax = np.float32(448.0)
+    else:
+        mids = (np.arange(0, 127, dtype=np.float32) + np.float32(0.5)).astype(np.float32)
+        qmax = np.float32(127.0)
     gen = np.random.default_rng(21)
     groups = []
     for amax in (448.0, 1.0, 3.7, 1e-3, 12345.678, 2.0 ** -20):
         a = np.float32(amax)
-        scale = np.float32(a / np.float32(448.0))
+        scale = np.float32(a / qmax)
         for k in range(-4, 5):
             x = (mids * scale).astype(np.float32)
             step = np.float32(np.inf) if k > 0 else np.float32(-np.inf)
@@ -426,12 +432,34 @@ def _midpoint_groups() -> np.ndarray:
     return np.stack(groups).astype(np.float32)
 
 
-def test_group_quant_fp8_quotients_at_e4m3_midpoints(cuda):
-    """The kernel forms x / scale as x * (1 / scale) and divides exactly only near an e4m3
-    rounding midpoint: on quotients on and around every midpoint, across the normal and
-    subnormal e4m3 range, its codes must be those of the exact IEEE division (the oracle)."""
-    x = _midpoint_groups()
-    q, s = tob.per_token_group_quant_fp8(torch.from_numpy(x).to(cuda), 16)
-    wq, ws = ofp8.group_quant(x, 16)
+@pytest.mark.parametrize("kind", ["fp8", "int8"])
+def test_group_quant_quotients_at_rounding_boundaries(cuda, kind):
+    """The kernel brackets x / scale between x * lo and x * hi (lo, hi just either side of
+    1 / scale) and divides exactly only where the two give different codes: on quotients on
+    and around every rounding boundary, across the normal and subnormal e4m3 range and the
+    int8 range, its codes must be those of the exact IEEE division (the oracle)."""
+    x = _midpoint_groups(kind)
+    xt = torch.from_numpy(x).to(cuda)
+    if kind == "fp8":
+        q, s = tob.per_token_group_quant_fp8(xt, 16)
+        wq, ws = ofp8.group_quant(x, 16)
+        got = _codes(q)
+    else:
+        q, s = tob.per_token_group_quant_int8(xt, 16)
+        wq, ws = oi8.group_quant(x, 16)
+        got = q.cpu().numpy()
     assert np.array_equal(s.cpu().numpy(), ws)
-    assert np.array_equal(_codes(q), wq)
+    assert np.array_equal(got, wq)
+    # The same values one to a thread (an odd row length leaves the vector path).
+    xo = np.concatenate([x, x[:, :1]], axis=1)[:, :17]
+    xo_t = torch.from_numpy(np.ascontiguousarray(xo)).to(cuda)
+    if kind == "fp8":
+        q1, s1 = tob.per_token_group_quant_fp8(xo_t, 17)
+        wq1, ws1 = ofp8.group_quant(xo, 17)
+        got1 = _codes(q1)
+    else:
+        q1, s1 = tob.per_token_group_quant_int8(xo_t, 17)
+        wq1, ws1 = oi8.group_quant(xo, 17)
+        got1 = q1.cpu().numpy()
+    assert np.array_equal(s1.cpu().numpy(), ws1)
+    assert np.array_equal(got1, wq1)

@@ -204,21 +204,118 @@ __device__ __forceinline__ uint8_t nan_code_div(float x, bool neg_x, bool nan_sc
   return (isnan(x) && neg_x) ? (uint8_t)0xFF : (uint8_t)0x7F;
 }
 
-// x / scale for an e4m3fn code without a division per element. With r = 1 / scale rounded to
-// fp32, the product x * r lies within two ulps of the correctly rounded quotient, and the e4m3
-// code changes only across a rounding midpoint of the e4m3 grid (3 mantissa bits, so a midpoint
-// has bit 19 set and bits 0-18 clear in the fp32 mantissa). The product therefore gives the
-// same code unless it lies within four ulps of such a midpoint, or below 2^-6 where the e4m3
-// grid is subnormal; those take the exact IEEE quotient. (A value within two ulps of a power of
-// two rounds to that power of two either way.)
-__device__ __forceinline__ float quot_for_e4m3(float x, float scale, float r) {
-  const float y = x * r;
-  const uint32_t a = __float_as_uint(y) & 0x7FFFFFFFu;
-  const uint32_t low = a & 0xFFFFFu;  // mantissa bits below the 3 that e4m3 keeps
-  const bool near_mid = low - 0x7FFFCu <= 8u;
-  if (near_mid || a < 0x3C800000u) return __fdiv_rn(x, scale);
-  return y;
+// Codes of x / scale without a division per element: the bracket test. With r = 1 / scale
+// rounded to fp32, lo = r (1 - 2^-21) and hi = r (1 + 2^-21), each rounded, the products x lo
+// and x hi enclose both the exact quotient and its fp32 rounding: r, lo, hi and a rounded
+// product are each off by at most 2^-24 relatively, 4 x 2^-24 in all, inside the 8 x 2^-24
+// margin. Rounding onto the code grid (e4m3fn RNE with saturation, or RNE to an integer) is
+// monotone, so when both products give the same code the correctly rounded quotient gives it
+// too; a pack where they differ takes the IEEE division for every value. The test holds on the
+// e4m3 subnormal grid and at saturation alike. It needs a scale whose reciprocal is a normal
+// fp32 number and a group without NaN or infinity (a finite absmax); a scale within
+// [1.2e-38, 8e37] implies both.
+struct Bracket {
+  float lo, hi;
+};
+__device__ __forceinline__ Bracket make_bracket(float scale) {
+  const float r = __frcp_rn(scale);
+  return {__fmul_rn(r, 1.0f - 0x1p-21f), __fmul_rn(r, 1.0f + 0x1p-21f)};
 }
+
+// RNE integer of the exact product x * m plus 1.5 x 2^23: for |x m| < 2^22 the sum's low bits
+// are the integer in two's complement (its low byte is the int8 code).
+__device__ __forceinline__ uint32_t rne_int_bits(float x, float m) {
+  return __float_as_uint(__fmaf_rn(x, m, 12582912.0f));
+}
+
+// Codes of a pack by the bracket test; false when the two ends disagree anywhere in the pack.
+// e4m3fn: a pair converts in one cvt.rn.satfinite.e4m3x2. int8: |x / scale| <= 127 (1 + 2^-22)
+// on this path (scale = max(absmax, eps) / 127 rounded), so no value reaches the clamp.
+template <int Q, typename T, int V>
+__device__ __forceinline__ bool bracket_codes(const Pack<T, V>& t, const Bracket& b,
+                                              Pack<uint8_t, V>& o) {
+  uint32_t diff = 0u;
+  if constexpr (V == 1) {
+    const float x = to_f32(t.v[0]);
+    if constexpr (Q == kQE4M3) {
+      const uint32_t c = f32x2_to_e4m3x2(__fmul_rn(x, b.lo), __fmul_rn(x, b.hi));
+      diff = (c ^ (c >> 8)) & 0xFFu;
+      o.v[0] = (uint8_t)c;
+    } else {
+      const uint32_t l = rne_int_bits(x, b.lo), h = rne_int_bits(x, b.hi);
+      diff = l ^ h;
+      o.v[0] = (uint8_t)l;
+    }
+  } else {
+    static_assert(V % 4 == 0, "bracket_codes packs four codes to a word");
+    uint32_t* w = reinterpret_cast<uint32_t*>(o.v);
+#pragma unroll
+    for (int k = 0; k < V / 4; ++k) {
+      float x[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] = to_f32(t.v[4 * k + j]);
+      if constexpr (Q == kQE4M3) {
+        const uint32_t l01 = f32x2_to_e4m3x2(__fmul_rn(x[0], b.lo), __fmul_rn(x[1], b.lo));
+        const uint32_t h01 = f32x2_to_e4m3x2(__fmul_rn(x[0], b.hi), __fmul_rn(x[1], b.hi));
+        const uint32_t l23 = f32x2_to_e4m3x2(__fmul_rn(x[2], b.lo), __fmul_rn(x[3], b.lo));
+        const uint32_t h23 = f32x2_to_e4m3x2(__fmul_rn(x[2], b.hi), __fmul_rn(x[3], b.hi));
+        diff |= (l01 ^ h01) | (l23 ^ h23);
+        w[k] = __byte_perm(l01, l23, 0x5410);
+      } else {
+        uint32_t l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          l[j] = rne_int_bits(x[j], b.lo);
+          diff |= l[j] ^ rne_int_bits(x[j], b.hi);
+        }
+        w[k] = __byte_perm(__byte_perm(l[0], l[1], 0x0040), __byte_perm(l[2], l[3], 0x0040),
+                           0x5410);
+      }
+    }
+  }
+  return diff == 0u;
+}
+
+// Running maximum of |x| over packs, read out as the abs_key of the largest |x|. 16-bit types
+// keep the sign-cleared bit patterns two to a word and take halfword-wise unsigned maxima
+// (max.u16x2): patterns of non-negative values order as the values, with NaNs above infinity,
+// and the largest converts to the same fp32 key the per-value path finds.
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <typename T> struct AbsMax {
+  unsigned k = 0u;
+  template <int V> __device__ __forceinline__ void add(const Pack<T, V>& p) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) k = max(k, abs_key(to_f32(p.v[j])));
+  }
+  __device__ __forceinline__ unsigned key() const { return k; }
+};
+__device__ __forceinline__ unsigned short bits16(__half v) { return __half_as_ushort(v); }
+__device__ __forceinline__ unsigned short bits16(__nv_bfloat16 v) { return __bfloat16_as_ushort(v); }
+template <typename T> struct AbsMax16 {
+  uint32_t k2 = 0u;
+  template <int V> __device__ __forceinline__ void add(const Pack<T, V>& p) {
+    if constexpr (V % 2 == 0) {
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(p.v);
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) k2 = max_u16x2(k2, w[i] & 0x7FFF7FFFu);
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j)
+        k2 = max(k2, (uint32_t)(bits16(p.v[j]) & 0x7FFFu));
+    }
+  }
+  __device__ __forceinline__ unsigned key() const {
+    const unsigned short m = (unsigned short)max(k2 & 0xFFFFu, k2 >> 16);
+    if constexpr (std::is_same<T, __half>::value) return abs_key(__half2float(__ushort_as_half(m)));
+    else return abs_key(__bfloat162float(__ushort_as_bfloat16(m)));
+  }
+};
+template <> struct AbsMax<__half> : AbsMax16<__half> {};
+template <> struct AbsMax<__nv_bfloat16> : AbsMax16<__nv_bfloat16> {};
 
 // Sign bit of a stored value.
 __device__ __forceinline__ bool sign_of(float v) { return __float_as_uint(v) >> 31; }
@@ -273,21 +370,18 @@ __global__ void __launch_bounds__(1024) k_group_quant(const GroupSrc<T, ACT> src
     const int64_t g = g0 + team_id;
     const bool active = g < n_groups;
     Pack<T, V> cache[MAXV];
-    unsigned amax = 0u;  // abs_key of the group's largest |x|; a NaN anywhere makes it NaN
+    AbsMax<T> am;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
       const int v = lane + i * team;
       if (active && v < nvec) {
         cache[i] = src.template load<V>(g, G, v);
-#pragma unroll
-        for (int j = 0; j < V; ++j) amax = max(amax, abs_key(to_f32(cache[i].v[j])));
+        am.add(cache[i]);
       }
     }
-    for (int v = lane + MAXV * team; active && v < nvec; v += team) {
-      Pack<T, V> t = src.template load<V>(g, G, v);
-#pragma unroll
-      for (int j = 0; j < V; ++j) amax = max(amax, abs_key(to_f32(t.v[j])));
-    }
+    for (int v = lane + MAXV * team; active && v < nvec; v += team)
+      am.add(src.template load<V>(g, G, v));
+    unsigned amax = am.key();  // abs_key of the group's largest |x|; a NaN anywhere makes it NaN
     if (team <= 32) {
       amax = warp_max_key(amax, team);
     } else {
@@ -309,29 +403,18 @@ __global__ void __launch_bounds__(1024) k_group_quant(const GroupSrc<T, ACT> src
     if (FP8 && ue8m0 && !nan_group) scale = ue8m0_round(scale);
     if (active && lane == 0) scales[scale_offset(g, sl)] = scale;
     uint8_t* qg = qout + g * (int64_t)G;
-    // e4m3fn codes from x * (1 / scale) (quot_for_e4m3) when the scale is a normal number whose
-    // reciprocal is one too; otherwise (NaN, inf, 0 or extreme scales) every element divides.
-    const bool fast = Q == kQE4M3 && scale >= 1.2e-38f && scale <= 8.0e37f;
-    const float rcp = fast ? __frcp_rn(scale) : 0.0f;
+    // e4m3fn and int8 codes come from the bracket test when the scale allows it; otherwise
+    // (NaN, inf, 0 or extreme scales, e4m3fnuz, a pack whose bracket straddles a rounding
+    // boundary) every value divides.
+    const bool fast = (Q == kQE4M3 || Q == kQI8) && scale >= 1.2e-38f && scale <= 8.0e37f;
+    const Bracket br = fast ? make_bracket(scale) : Bracket{0.0f, 0.0f};
     auto emit = [&](int v, const Pack<T, V>& t) {
       Pack<uint8_t, V> o;
-      if constexpr (Q == kQE4M3 && V % 2 == 0) {
-#pragma unroll
-        for (int j = 0; j < V; j += 2) {
-          const float x0 = to_f32(t.v[j]), x1 = to_f32(t.v[j + 1]);
-          const float y0 = fast ? quot_for_e4m3(x0, scale, rcp) : __fdiv_rn(x0, scale);
-          const float y1 = fast ? quot_for_e4m3(x1, scale, rcp) : __fdiv_rn(x1, scale);
-          const uint16_t pr = f32x2_to_e4m3x2(fminf(fmaxf(y0, -448.f), 448.f),
-                                              fminf(fmaxf(y1, -448.f), 448.f));
-          o.v[j] = isnan(y0) ? nan_code_div(x0, sign_of(t.v[j]), nan_group) : (uint8_t)(pr & 0xFF);
-          o.v[j + 1] =
-              isnan(y1) ? nan_code_div(x1, sign_of(t.v[j + 1]), nan_group) : (uint8_t)(pr >> 8);
-        }
-      } else {
+      if (!(fast && bracket_codes<Q>(t, br, o))) {
 #pragma unroll
         for (int j = 0; j < V; ++j) {
           const float xv = to_f32(t.v[j]);
-          const float y = fast ? quot_for_e4m3(xv, scale, rcp) : __fdiv_rn(xv, scale);
+          const float y = __fdiv_rn(xv, scale);
           if (Q == kQE4M3) {
             o.v[j] = isnan(y) ? nan_code_div(xv, sign_of(t.v[j]), nan_group)
                               : f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
