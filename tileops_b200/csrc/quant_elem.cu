@@ -228,52 +228,86 @@ __device__ __forceinline__ uint32_t rne_int_bits(float x, float m) {
   return __float_as_uint(__fmaf_rn(x, m, 12582912.0f));
 }
 
-// Codes of a pack by the bracket test; false when the two ends disagree anywhere in the pack.
-// e4m3fn: a pair converts in one cvt.rn.satfinite.e4m3x2. int8: |x / scale| <= 127 (1 + 2^-22)
-// on this path (scale = max(absmax, eps) / 127 rounded), so no value reaches the clamp.
+// The code of the IEEE quotient x / scale (a finite x, a normal scale: no NaN can arise).
+template <int Q> __device__ __forceinline__ uint32_t exact_code(float x, float scale) {
+  const float y = __fdiv_rn(x, scale);
+  if constexpr (Q == kQE4M3) return f32_to_e4m3(fminf(fmaxf(y, -448.f), 448.f));
+  else return (uint8_t)rne_clamp_i8(y);
+}
+
+// Four codes from the two ends' codes wl, wh (byte j for x[j]): where they differ -- a quotient
+// on or next to a rounding boundary, which bf16 inputs hit often since x / scale is then
+// frequently an exact e4m3 midpoint -- that value alone divides.
+template <int Q>
+__device__ __noinline__ uint32_t fix_codes(uint32_t wl, uint32_t wh, float x0, float x1, float x2,
+                                           float x3, float scale) {
+  const float x[4] = {x0, x1, x2, x3};
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (((wl ^ wh) >> (8 * j)) & 0xFFu)
+      wl = (wl & ~(0xFFu << (8 * j))) | (exact_code<Q>(x[j], scale) << (8 * j));
+  return wl;
+}
+
+// Codes of a pack by the bracket test, the products two lanes per instruction (mul.rn.f32x2 /
+// fma.rn.f32x2 round each lane like the scalar forms). e4m3fn: a pair converts in one
+// cvt.rn.satfinite.e4m3x2. int8: |x / scale| <= 127 (1 + 2^-22) on this path (scale =
+// max(absmax, eps) / 127 rounded), so no value reaches the clamp, and the two ends differ by at
+// most one, so their low bytes tell whether they differ. One branch per pack leads to the
+// per-value fix-ups.
 template <int Q, typename T, int V>
-__device__ __forceinline__ bool bracket_codes(const Pack<T, V>& t, const Bracket& b,
+__device__ __forceinline__ void bracket_codes(const Pack<T, V>& t, const Bracket& b, float scale,
                                               Pack<uint8_t, V>& o) {
-  uint32_t diff = 0u;
   if constexpr (V == 1) {
     const float x = to_f32(t.v[0]);
+    uint32_t l, h;
     if constexpr (Q == kQE4M3) {
       const uint32_t c = f32x2_to_e4m3x2(__fmul_rn(x, b.lo), __fmul_rn(x, b.hi));
-      diff = (c ^ (c >> 8)) & 0xFFu;
-      o.v[0] = (uint8_t)c;
+      l = c & 0xFFu;
+      h = c >> 8;
     } else {
-      const uint32_t l = rne_int_bits(x, b.lo), h = rne_int_bits(x, b.hi);
-      diff = l ^ h;
-      o.v[0] = (uint8_t)l;
+      l = rne_int_bits(x, b.lo) & 0xFFu;
+      h = rne_int_bits(x, b.hi) & 0xFFu;
     }
+    o.v[0] = (uint8_t)(l == h ? l : exact_code<Q>(x, scale));
   } else {
     static_assert(V % 4 == 0, "bracket_codes packs four codes to a word");
+    constexpr int W = V / 4;
+    const float2 lo2 = make_float2(b.lo, b.lo), hi2 = make_float2(b.hi, b.hi);
+    uint32_t wl[W], wh[W], diff = 0u;
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      const float2 x01 = make_float2(to_f32(t.v[4 * k]), to_f32(t.v[4 * k + 1]));
+      const float2 x23 = make_float2(to_f32(t.v[4 * k + 2]), to_f32(t.v[4 * k + 3]));
+      if constexpr (Q == kQE4M3) {
+        const float2 l01 = mul2_rn(x01, lo2), h01 = mul2_rn(x01, hi2);
+        const float2 l23 = mul2_rn(x23, lo2), h23 = mul2_rn(x23, hi2);
+        wl[k] = __byte_perm(f32x2_to_e4m3x2(l01.x, l01.y), f32x2_to_e4m3x2(l23.x, l23.y), 0x5410);
+        wh[k] = __byte_perm(f32x2_to_e4m3x2(h01.x, h01.y), f32x2_to_e4m3x2(h23.x, h23.y), 0x5410);
+      } else {
+        const float2 m2 = make_float2(12582912.0f, 12582912.0f);
+        const float2 l01 = fma2_rn(x01, lo2, m2), h01 = fma2_rn(x01, hi2, m2);
+        const float2 l23 = fma2_rn(x23, lo2, m2), h23 = fma2_rn(x23, hi2, m2);
+        wl[k] = __byte_perm(__byte_perm(__float_as_uint(l01.x), __float_as_uint(l01.y), 0x0040),
+                            __byte_perm(__float_as_uint(l23.x), __float_as_uint(l23.y), 0x0040),
+                            0x5410);
+        wh[k] = __byte_perm(__byte_perm(__float_as_uint(h01.x), __float_as_uint(h01.y), 0x0040),
+                            __byte_perm(__float_as_uint(h23.x), __float_as_uint(h23.y), 0x0040),
+                            0x5410);
+      }
+      diff |= wl[k] ^ wh[k];
+    }
+    if (diff != 0u) {
+#pragma unroll
+      for (int k = 0; k < W; ++k)
+        if (wl[k] != wh[k])
+          wl[k] = fix_codes<Q>(wl[k], wh[k], to_f32(t.v[4 * k]), to_f32(t.v[4 * k + 1]),
+                               to_f32(t.v[4 * k + 2]), to_f32(t.v[4 * k + 3]), scale);
+    }
     uint32_t* w = reinterpret_cast<uint32_t*>(o.v);
 #pragma unroll
-    for (int k = 0; k < V / 4; ++k) {
-      float x[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = to_f32(t.v[4 * k + j]);
-      if constexpr (Q == kQE4M3) {
-        const uint32_t l01 = f32x2_to_e4m3x2(__fmul_rn(x[0], b.lo), __fmul_rn(x[1], b.lo));
-        const uint32_t h01 = f32x2_to_e4m3x2(__fmul_rn(x[0], b.hi), __fmul_rn(x[1], b.hi));
-        const uint32_t l23 = f32x2_to_e4m3x2(__fmul_rn(x[2], b.lo), __fmul_rn(x[3], b.lo));
-        const uint32_t h23 = f32x2_to_e4m3x2(__fmul_rn(x[2], b.hi), __fmul_rn(x[3], b.hi));
-        diff |= (l01 ^ h01) | (l23 ^ h23);
-        w[k] = __byte_perm(l01, l23, 0x5410);
-      } else {
-        uint32_t l[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          l[j] = rne_int_bits(x[j], b.lo);
-          diff |= l[j] ^ rne_int_bits(x[j], b.hi);
-        }
-        w[k] = __byte_perm(__byte_perm(l[0], l[1], 0x0040), __byte_perm(l[2], l[3], 0x0040),
-                           0x5410);
-      }
-    }
+    for (int k = 0; k < W; ++k) w[k] = wl[k];
   }
-  return diff == 0u;
 }
 
 // Running maximum of |x| over packs, read out as the abs_key of the largest |x|. 16-bit types
@@ -410,7 +444,14 @@ __global__ void __launch_bounds__(1024) k_group_quant(const GroupSrc<T, ACT> src
     const Bracket br = fast ? make_bracket(scale) : Bracket{0.0f, 0.0f};
     auto emit = [&](int v, const Pack<T, V>& t) {
       Pack<uint8_t, V> o;
-      if (!(fast && bracket_codes<Q>(t, br, o))) {
+      if constexpr (Q == kQE4M3 || Q == kQI8) {
+        if (fast) {
+          bracket_codes<Q>(t, br, scale, o);
+          st_pack<uint8_t, V>(qg + (int64_t)v * V, o);
+          return;
+        }
+      }
+      {
 #pragma unroll
         for (int j = 0; j < V; ++j) {
           const float xv = to_f32(t.v[j]);
@@ -482,10 +523,11 @@ int launch_act_group_quant(const void* a, const void* b, int64_t rows, int64_t c
   const bool vec = (G % VV == 0) && lda % VV == 0 && ldb % VV == 0 && aligned16(a) &&
                    aligned16(b) && aligned_to(q, VV);
   const int64_t n_groups = rows * (cols / G);
-  const GroupGrid gg = group_grid(n_groups, G / (vec ? VV : 1), vec ? 4 : 8);
+  // Two cached vectors per thread: the activation's arithmetic leaves no registers for four.
+  const GroupGrid gg = group_grid(n_groups, G / (vec ? VV : 1), vec ? 2 : 8);
   GroupSrc<T, ACT> src{(const T*)a, (const T*)b, lda, ldb, cols / G};
   if (vec)
-    k_group_quant<T, Q, VV, 4, ACT><<<(unsigned)gg.blocks, gg.threads, 0, st>>>(
+    k_group_quant<T, Q, VV, 2, ACT><<<(unsigned)gg.blocks, gg.threads, 0, st>>>(
         src, (uint8_t*)q, scales, n_groups, (int)G, gg.team_log2, eps, ue8m0, sl);
   else
     k_group_quant<T, Q, 1, 8, ACT><<<(unsigned)gg.blocks, gg.threads, 0, st>>>(
