@@ -661,6 +661,7 @@ class DenseGemv:
         import tileops_b200 as tob
 
         self.tob = tob
+        tob.set_launch_overlap(True)  # as the int4 GEMV line: call i+1 streams A under call i
         M, K = self.M, self.K
         g = torch.Generator().manual_seed(1234 + 8 + rank)
         self.sets = [torch.randn(M, K, generator=g).half().to(dev) for _ in range(self.SETS)]
@@ -693,7 +694,8 @@ class DenseGemv:
         return {"workload": "dense fp16 GEMV y[4096] = A[4096,4096] @ x (the AWQ GEMV layer with "
                             "dense weights): the comparator of the int4 GEMV",
                 "M": self.M, "K": self.K, "parallelism": f"replicas x{world}",
-                "l2": "8 rotating weight sets x 33.6 MB > L2"}
+                "l2": "8 rotating weight sets x 33.6 MB > L2",
+                "launch_overlap": "programmatic dependent launch between consecutive calls"}
 
     @classmethod
     def cpu_reference(cls, threads):

@@ -160,8 +160,14 @@ def test_gemm_deterministic(cuda):
     (40, 14336, 512, 128),    # x of a long K chunk does not fit: 32 + 8 tokens
     (33, 200, 256, 200),      # K % 64 != 0: the tcgen05 kernel takes it instead
     (5, 256, 96, 256),        # 12 words: a partial column tile, G == K
-    # prefetching SIMT stream (M <= 2, and shapes the TMA kernel does not take)
+    # prefetching SIMT stream (M <= 2 below the decode kernel's layer size)
+    (1, 4096, 4096, 128),     # the GEMV layer: 32 tiles x K split 8
+    (2, 4096, 6144, 64),      # two tokens, 48 tiles
+    (1, 1024, 2048, 32),      # 256-row chunks, eight groups per chunk
+    (1, 3072, 1024, 3072),    # K split 6, one group over all chunks (G == K)
+    (2, 3200, 2048, 128),     # K split 7, the last chunk 128 rows: idle warps
     (1, 4096, 28672, 128),    # 32-word column tiles
+    (1, 2432, 1040, 128),     # 130 words (partial tile), K split 5: slices of ceil(128 / 5)
     (2, 14336, 4096, 128),    # several row blocks per warp
     (3, 1000, 256, 1000),     # K % 64 != 0, K tail inside the last row block
     (2, 100, 64, 100),        # K not a multiple of 8 (scalar x staging), G == K

@@ -393,6 +393,65 @@ int launch_gemv_any_m(const void* x, const int32_t* qw, const void* s, const int
 //     after the wait);
 //   * warp sums -> CTA sums in shared memory (fixed order) -> cluster reduction over the
 //     K-chunks through distributed shared memory into cluster rank 0 (deterministic).
+// The end of both GEMV kernels: each thread holds acc[m][c] for its lane-row's 2 words
+// (16 columns) of the CTA's CW-word tile. Sum over the lane-rows of a warp, then over the 8
+// warps in a fixed order; with a K split, cluster rank r reduces column slice r over all ranks
+// (fixed order) and stores it, so the remote loads and the stores are spread over the cluster.
+template <typename T, int MT, int CW>
+__device__ __forceinline__ void gemv_reduce_store(const float (&acc)[MT][16], float* part,
+                                                  float* tot, T* __restrict__ y, int M, int N,
+                                                  int ksplit) {
+  constexpr int LPR = CW / 2;  // lanes per row
+  constexpr int COLS = CW * 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rl = lane / LPR, lw = lane - rl * LPR;
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      float v = acc[m][c];
+#pragma unroll
+      for (int o = LPR; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (rl == 0) part[(warp * MT + m) * COLS + lw * 16 + c] = v;
+    }
+  __syncthreads();
+  for (int i = threadIdx.x; i < MT * COLS; i += kThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w * MT * COLS + i];
+    tot[i] = s;
+  }
+  const int rows = min(M, MT);
+  if (ksplit > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    // ceil(COLS / ksplit) columns per rank: the K split need not divide the tile (K = 3072
+    // in 512-row chunks is a split of 6).
+    const int per = (COLS + ksplit - 1) / ksplit;
+    const int c0 = blockIdx.y * per;
+    const int cn = min(per, COLS - c0);
+    for (int i = threadIdx.x; i < rows * cn; i += kThreads) {
+      const int m = i / cn, c = c0 + (i - m * cn);
+      float v[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) v[r] = r < ksplit ? cluster.map_shared_rank(tot, r)[m * COLS + c] : 0.f;
+      float s = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) s += v[r];
+      const int col = blockIdx.x * COLS + c;
+      if (col < N) y[(int64_t)m * N + col] = from_f32<T>(s);
+    }
+    cluster.sync();  // peers keep their shared memory until every slice has been read
+  } else {
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * COLS; i += kThreads) {
+      const int m = i / COLS, c = i - m * COLS;
+      const int col = blockIdx.x * COLS + c;
+      if (col < N) y[(int64_t)m * N + col] = from_f32<T>(tot[i]);
+    }
+  }
+}
+
 template <typename T, int CW, int LPT>
 struct GemvBlock {
   uint2 w[LPT];
@@ -516,52 +575,7 @@ k_awq_gemv_stream(const T* __restrict__ x, const uint32_t* __restrict__ qw,
     }
   }
 
-  // Sum over the RPL lane-rows of a warp, then over the 8 warps in a fixed order.
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int c = 0; c < WPL * 8; ++c) {
-      float v = acc[m][c];
-#pragma unroll
-      for (int o = LPR; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (rl == 0) part[(warp * MT + m) * COLS + lw * WPL * 8 + c] = v;
-    }
-  __syncthreads();
-  for (int i = threadIdx.x; i < MT * COLS; i += kThreads) {
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) s += part[w * MT * COLS + i];
-    tot[i] = s;
-  }
-
-  // With a K split, cluster rank r reduces column slice r over all ranks (fixed order) and
-  // stores it, so the remote loads and the stores are spread over the cluster.
-  const int rows = min(M, MT);
-  if (ksplit > 1) {
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    const int per = COLS / ksplit;
-    const int c0 = blockIdx.y * per;
-    for (int i = threadIdx.x; i < rows * per; i += kThreads) {
-      const int m = i / per, c = c0 + (i - m * per);
-      float v[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) v[r] = r < ksplit ? cluster.map_shared_rank(tot, r)[m * COLS + c] : 0.f;
-      float s = 0.f;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) s += v[r];
-      const int col = blockIdx.x * COLS + c;
-      if (col < N) y[(int64_t)m * N + col] = from_f32<T>(s);
-    }
-    cluster.sync();  // peers keep their shared memory until every slice has been read
-  } else {
-    __syncthreads();
-    for (int i = threadIdx.x; i < rows * COLS; i += kThreads) {
-      const int m = i / COLS, c = i - m * COLS;
-      const int col = blockIdx.x * COLS + c;
-      if (col < N) y[(int64_t)m * N + col] = from_f32<T>(tot[i]);
-    }
-  }
+  gemv_reduce_store<T, MT, CW>(acc, part, tot, y, M, N, ksplit);
 }
 
 template <typename T, int MT, int CW, int LPT>

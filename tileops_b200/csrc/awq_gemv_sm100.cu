@@ -321,9 +321,11 @@ __global__ void __launch_bounds__(kSmThreads, kSmCtasPerSm) k_awq_small_m(
   if (ksplit > 1) {
     cg::cluster_group cluster = cg::this_cluster();
     cluster_sync_all();
-    const int per = kVals / ksplit;
+    // ceil(kVals / ksplit) values per rank: the K split need not divide them.
+    const int per = (kVals + ksplit - 1) / ksplit;
     const int i0 = blockIdx.y * per;
-    for (int i = i0 + threadIdx.x; i < i0 + per; i += kSmThreads) {
+    const int i1 = min(kVals, i0 + per);
+    for (int i = i0 + threadIdx.x; i < i1; i += kSmThreads) {
       int m, n;
       coords(i, m, n);
       if (m >= M || n >= N) continue;
