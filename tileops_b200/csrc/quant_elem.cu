@@ -543,15 +543,12 @@ __global__ void __launch_bounds__(kThreads) k_absmax(const T* __restrict__ x, in
                                                     unsigned* __restrict__ amax_bits) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t nvec = n / V;
-  unsigned m = 0u;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
-    Pack<T, V> v = ld_pack<T, V>(x + i * V);
-#pragma unroll
-    for (int j = 0; j < V; ++j) m = max(m, abs_key(to_f32(v.v[j])));
-  }
+  AbsMax<T> am;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride)
+    am.add(ld_pack<T, V>(x + i * V));
   for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    m = max(m, abs_key(to_f32(x[i])));
-  m = warp_max_key(m, 32);
+    am.add(ld_pack<T, 1>(x + i));
+  unsigned m = warp_max_key(am.key(), 32);
   __shared__ unsigned red[kThreads / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
