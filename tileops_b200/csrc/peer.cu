@@ -10,6 +10,12 @@
 // captured the barrier replays it correctly; every rank must run the same sequence of
 // barriers. Waits are bounded: after the library's wait limit the kernel records a timeout in
 // the device error word and returns (a rank that left, or one that never launched its part).
+//
+// With launch overlap on, the barrier is launched as a programmatic dependent of the GEMM: it
+// is resident before the GEMM ends and starts at griddepcontrol.wait (the GEMM complete, its
+// stores visible), then lets the next kernel in the stream launch at once, so that kernel's
+// weight stream, which reads nothing the ranks exchange, overlaps the flag round trip; the
+// next kernel's own griddepcontrol.wait still waits for this barrier to finish.
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -24,6 +30,8 @@ struct PeerFlags {
 __global__ void __launch_bounds__(32) k_peer_barrier(PeerFlags flags, int world, int rank,
                                                      unsigned long long* counter, int* err) {
   const int lane = threadIdx.x;
+  grid_dependency_wait();
+  grid_dependents_launch();
   unsigned long long target = 0;
   if (lane == 0) {
     target = *counter + 1;
@@ -70,8 +78,19 @@ int to_peer_barrier(unsigned long long* const* flag_ranks, int world, int rank,
     f.f[r] = flag_ranks[r];
   }
   int* err = tob::device_error_ptr();
-  tob::k_peer_barrier<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, world, rank, counter,
-                                                                     err);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(32, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  if (tob::launch_overlap()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, tob::k_peer_barrier, f, world, rank, counter, err);
+  if (e != cudaSuccess) return tob::cuda_fail(e, "to_peer_barrier launch");
   return tob::check_launch("to_peer_barrier");
 }
 
