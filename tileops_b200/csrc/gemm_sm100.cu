@@ -48,6 +48,7 @@ struct Epi {
   int policy_a;      // L2 policy for A loads: 0 normal, 1 evict_first, 2 evict_last
   int policy_b;
   int tma_store;     // 16-bit C written through shared-memory staging + TMA stores
+  int band = 16;     // M tiles per band of the tile order (tile_band)
 };
 
 // warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue (two per TMEM lane quarter)
@@ -224,19 +225,27 @@ __device__ __forceinline__ void store_direct(const float* v, const Epi& ep, int6
 // only within rounding.
 __device__ __forceinline__ int k_start(int t, int kblocks) { return (int)(((unsigned)t * 5u) % (unsigned)kblocks); }
 
-// Output tile t -> (M tile, N tile). Tiles run in bands of kTileBand M tiles, M fastest within a
-// band: the ~148 tiles in flight then share ~16 M tiles of A and ~9 N tiles of B, so each band
-// streams B once and keeps its A rows in L2, instead of re-reading all of A on every wave (the
-// plain M-fastest order does that once M spans more tiles than a wave). Problems of at most
-// kTileBand M tiles keep the plain order.
-constexpr int kTileBand = 16;
-__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
-  const int band_tiles = kTileBand * n_tiles;
-  const int band = t / band_tiles;
-  const int rows = min(kTileBand, m_tiles - band * kTileBand);  // M tiles in this band
-  const int local = t - band * band_tiles;
-  mt = band * kTileBand + local % rows;
+// Output tile t -> (M tile, N tile). Tiles run in bands of `band` M tiles, M fastest within a
+// band: the ~148 tiles in flight then share the band's M tiles of A and a few N tiles of B, so
+// each band streams B once and keeps its A rows in L2, instead of re-reading all of A on every
+// wave (the plain M-fastest order does that once M spans more tiles than a wave). Problems of at
+// most `band` M tiles keep the plain order.
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int band, int& mt,
+                                            int& nt) {
+  const int band_tiles = band * n_tiles;
+  const int b = t / band_tiles;
+  const int rows = min(band, m_tiles - b * band);  // M tiles in this band
+  const int local = t - b * band_tiles;
+  mt = b * band + local % rows;
   nt = local / rows;
+}
+
+// The band: the most M tiles (16 or 32) whose A rows stay within 32 MB, so that they and the
+// B blocks in flight stay in L2 next to the output being written. FP8 8192^3 (128-row tiles,
+// K = 8192): 32 tiles, B read twice instead of four times (262 MB read per GEMM against 360);
+// 64 tiles (all of A, 64 MB) thrashed L2 (733 MB read).
+inline int tile_band(int bm, int64_t K, int elem) {
+  return (int64_t)32 * bm * K * elem <= ((int64_t)32 << 20) ? 32 : 16;
 }
 
 // Bytes of one 128-row half's partial sums in the exchange layout [chunk][j / 4][row][4] (32-bit
@@ -271,7 +280,7 @@ __device__ __forceinline__ void ks2_epilogue(uint32_t tmem, uint8_t* sA, uint64_
   const int eg = (warp - 2) >> 2;  // which of the two warps on that quarter
   const int mine = rank, other = rank ^ 1;
   int mt, nt;
-  tile_coords(t, m_tiles, n_tiles, mt, nt);
+  tile_coords(t, m_tiles, n_tiles, ep.band, mt, nt);
   float sbt[(BN + 31) / 32];
   load_tile_col_scales<BN>(sbt, ep, nt * BN, N, lane);
   const int row0 = mt * BM + mine * 128 + q * 32;  // first row of this warp's 32-row slab
@@ -467,7 +476,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       pol_a = make_policy(ep.policy_a);
       pol_b = make_policy(ep.policy_b);
       int mt, nt;
-      tile_coords(t0, m_tiles, n_tiles, mt, nt);
+      tile_coords(t0, m_tiles, n_tiles, ep.band, mt, nt);
       // The dense form's B (larger than L2) is shared by the M tiles of a band: they walk K in
       // step, so each B block is read from DRAM once.
       const int k0 = BMN ? 0 : k_start(t0, kb_n);
@@ -507,7 +516,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int step = pre;
       for (int t = t0; ok && t < tiles; t += tstride) {
         int mt, nt;
-        tile_coords(t, m_tiles, n_tiles, mt, nt);
+        tile_coords(t, m_tiles, n_tiles, ep.band, mt, nt);
         const int k0 = BMN ? 0 : k_start(t, kb_n);
         for (int it = (t == t0 ? pre : 0); it < kb_n; ++it, ++step) {
           const int kb = kb_lo + (k0 + it) % kb_n;
@@ -605,7 +614,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t aph = (uint32_t)(i / C::kAccBufs) & 1u;
       // Scales of this tile, loaded while the main loop still runs.
       int mt, nt;
-      tile_coords(t, m_tiles, n_tiles, mt, nt);
+      tile_coords(t, m_tiles, n_tiles, ep.band, mt, nt);
       float sbt[(BN + 31) / 32];
       load_tile_col_scales<BN>(sbt, ep, nt * BN, N, lane);
       float sat[C::kHalves];
@@ -1434,6 +1443,7 @@ int launch_gemm_cfg(const void* a, const void* b, int64_t M, int64_t N, int64_t 
            : make_tmap_kmajor(&tb, b, N, K, C::kElem, BN);
   if (rc) return rc;
   Epi e2 = ep;
+  e2.band = tile_band(BM, K, C::kElem);
   memset(&tc32, 0, sizeof(tc32));
   memset(&tc16, 0, sizeof(tc16));
   if (e2.tma_store) {
