@@ -544,10 +544,19 @@ __global__ void __launch_bounds__(kThreads) k_absmax(const T* __restrict__ x, in
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t nvec = n / V;
   AbsMax<T> am;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride)
-    am.add(ld_pack<T, V>(x + i * V));
-  for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    am.add(ld_pack<T, 1>(x + i));
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  // Four loads in flight per thread (64 bytes): one 16-byte load at a time leaves too few
+  // bytes in flight per SM to cover DRAM latency.
+  for (; i + 3 * stride < nvec; i += 4 * stride) {
+    Pack<T, V> p[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) p[u] = ld_pack<T, V>(x + (i + u * stride) * V);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) am.add(p[u]);
+  }
+  for (; i < nvec; i += stride) am.add(ld_pack<T, V>(x + i * V));
+  for (int64_t j = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += stride)
+    am.add(ld_pack<T, 1>(x + j));
   unsigned m = warp_max_key(am.key(), 32);
   __shared__ unsigned red[kThreads / 32];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
@@ -605,15 +614,22 @@ __global__ void __launch_bounds__(kThreads) k_tensor_quant(const T* __restrict__
   };
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t nvec = n / V;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
-    Pack<T, V> v = ld_pack<T, V>(x + i * V);
+  auto quant_pack = [&](const Pack<T, V>& v, int64_t i) {
     Pack<uint8_t, V> o;
 #pragma unroll
     for (int j = 0; j < V; ++j) o.v[j] = quant1(to_f32(v.v[j]), i * V + j);
     st_pack<uint8_t, V>(q + i * V, o);
+  };
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + stride < nvec; i += 2 * stride) {  // two loads in flight per thread
+    const Pack<T, V> v0 = ld_pack<T, V>(x + i * V);
+    const Pack<T, V> v1 = ld_pack<T, V>(x + (i + stride) * V);
+    quant_pack(v0, i);
+    quant_pack(v1, i + stride);
   }
-  for (int64_t i = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    q[i] = quant1(to_f32(x[i]), i);
+  for (; i < nvec; i += stride) quant_pack(ld_pack<T, V>(x + i * V), i);
+  for (int64_t j = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += stride)
+    q[j] = quant1(to_f32(x[j]), j);
 }
 
 template <typename T, int Q>
