@@ -78,8 +78,8 @@ TO_API int to_ipc_free(void* ptr);
  * usable. out (device memory, 2 x u64) receives {completed ? 1 : 0, nanoseconds waited}.
  * Asynchronous on stream. */
 TO_API int to_wait_limit_selftest(int limit_us, int arrive, unsigned long long* out, void* stream);
-/* Launch overlap for the streaming small-M AWQ kernels, the 2-CTA W8A8 kernel and to_gemv
- * (programmatic dependent launch; the GEMV's A counts as its weights): with
+/* Launch overlap for the streaming small-M AWQ kernels, the 2-CTA W8A8 kernel, to_gemv and
+ * to_peer_barrier (programmatic dependent launch; the GEMV's A counts as its weights): with
  * enable = 1, a launch may start reading its weights, zeros and scales while the previous
  * kernel in the stream is still running; x is read and y written only after that kernel has
  * completed. Use it for chains of layers whose weights no kernel in the stream writes (a
@@ -264,7 +264,10 @@ TO_API int to_awq_gemm_act_gather(const void* x, const int32_t* qweight, const v
  * slot in every array to the next count and waits until every rank's slot in its own array
  * has reached it; work queued after it on `stream` sees every rank's earlier stores. Every
  * rank runs the same sequence of barriers; a wait that reaches the library's limit records a
- * timeout in the device error word instead of hanging. */
+ * timeout in the device error word instead of hanging. With launch overlap on
+ * (to_set_launch_overlap) the barrier starts when the previous kernel in the stream completes
+ * and lets the next kernel begin streaming its weights during the flag exchange; that
+ * kernel's activations and output still wait for the barrier. */
 TO_API size_t to_peer_flags_bytes(void);
 TO_API int to_peer_barrier(unsigned long long* const* flag_ranks, int world, int rank,
                            unsigned long long* counter, void* stream);
