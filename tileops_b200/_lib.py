@@ -139,27 +139,77 @@ def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
 
 
+# torch's raw accessors of the current device and stream: the public torch.cuda.current_device()
+# and current_stream() re-run their lazy-initialisation and index checks on every call, which
+# costs several microseconds per library call in a decode loop. The public forms stand in where
+# a torch build lacks them.
+_get_device = getattr(torch._C, "_cuda_getDevice", None) or torch.cuda.current_device
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def ensure_device(t: torch.Tensor, op: str) -> int:
     """Requires a CUDA tensor on an sm_100 device and makes that device current."""
-    if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
         dev = t.device if isinstance(t, torch.Tensor) else type(t).__name__
         raise TypeError(f"{op}: tileops_b200 runs on CUDA tensors only (got {dev})")
-    idx = t.device.index if t.device.index is not None else torch.cuda.current_device()
+    idx = t.get_device()
     if idx not in _checked_devices:
         check(load().to_device_check(idx), op)
         _checked_devices.add(idx)
-    if torch.cuda.current_device() != idx:
+    if _get_device() != idx:
         torch.cuda.set_device(idx)
     return idx
 
 
 def same_device(op: str, ref: torch.Tensor, *others: torch.Tensor | None) -> None:
+    dev = ref.get_device()
     for o in others:
-        if o is not None and o.device != ref.device:
+        if o is not None and o.get_device() != dev:
             raise TypeError(f"{op}: all tensors must be on {ref.device} (got {o.device})")
 
 
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+_WS_LOCK = threading.Lock()
+_WS_BYTES: dict[tuple, int] = {}
+
+
+def workspace_bytes(query: str, *shape: int) -> int:
+    """The library's workspace size for these shapes (a pure function of them), queried once."""
+    key = (query, *shape)
+    v = _WS_BYTES.get(key)
+    if v is None:
+        v = int(getattr(load(), query)(*shape))
+        _WS_BYTES[key] = v
+    return v
+
+
+def workspace(nbytes: int, device: int) -> torch.Tensor | None:
+    """Scratch of at least `nbytes` for a call about to be queued on the current stream of
+    `device`. One buffer per (device, stream) serves consecutive calls: every kernel that takes a
+    workspace touches it only after the previous kernel in its stream has completed (the
+    decode kernel waits on griddepcontrol.wait first, the others are ordinary launches), and
+    its flags are per-launch epochs left at zero once consumed. While the stream is being
+    captured into a CUDA graph each call gets its own buffer from the graph's memory pool."""
+    if nbytes <= 0:
+        return None
+    if torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", device))
+    key = (device, stream_ptr(device))
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        with _WS_LOCK:
+            ws = _WORKSPACES.get(key)
+            if ws is None or ws.numel() < nbytes:
+                ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8,
+                                 device=torch.device("cuda", device))
+                _WORKSPACES[key] = ws
+    return ws
+
+
 def stream_ptr(device: int | None = None) -> int:
+    """The current stream of `device` (default: the current device) as a cudaStream_t."""
+    if _raw_stream is not None:
+        return _raw_stream(_get_device() if device is None else device)
     return torch.cuda.current_stream(device).cuda_stream
 
 

@@ -182,8 +182,8 @@ def awq_gemm_triton(
     s = scales.contiguous()
     y = torch.empty(m, n, dtype=out_dtype, device=input.device)
     lib = _lib.load()
-    ws_bytes = lib.to_awq_gemm_workspace_size(m, k, n, group_size)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device) if ws_bytes else None
+    ws_bytes = _lib.workspace_bytes("to_awq_gemm_workspace_size", m, k, n, group_size)
+    ws = _lib.workspace(ws_bytes, input.get_device())
     if (input.dtype == out_dtype and not input.is_contiguous() and input.stride(1) == 1
             and input.stride(0) >= k and input.stride(0) % 8 == 0
             and input.data_ptr() % 16 == 0):
@@ -243,9 +243,8 @@ def _gemm_act(op: str, act: int, input, qweight, scales, qzeros, split_k_iters) 
     qz = _as_words(qzeros)
     s = scales.contiguous()
     y = torch.empty(m, n // 2, dtype=out_dtype, device=input.device)
-    lib = _lib.load()
-    ws_bytes = lib.to_awq_gemm_act_workspace_size(m, k, n, group_size)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device) if ws_bytes else None
+    ws_bytes = _lib.workspace_bytes("to_awq_gemm_act_workspace_size", m, k, n, group_size)
+    ws = _lib.workspace(ws_bytes, input.get_device())
     _lib.call("to_awq_gemm_act", x.data_ptr(), qw.data_ptr(), s.data_ptr(),
               _lib.DTYPE_CODES[out_dtype], qz.data_ptr(), y.data_ptr(), m, k, n, group_size,
               act, _lib.ptr(ws), ws_bytes, _lib.stream_ptr())

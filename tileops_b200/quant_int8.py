@@ -38,9 +38,8 @@ def input_to_int8(
     xc = x.contiguous()
     q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
     s = torch.empty((), dtype=torch.float32, device=x.device)
-    lib = _lib.load()
-    ws_bytes = lib.to_input_quant_workspace_size()
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    ws_bytes = _lib.workspace_bytes("to_input_quant_workspace_size")
+    ws = _lib.workspace(ws_bytes, x.get_device())
     _lib.call("to_input_to_int8", xc.data_ptr(), _lib.DTYPE_CODES[x.dtype], xc.numel(),
               q.data_ptr(), s.data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_ptr())
     return q, s

@@ -264,8 +264,8 @@ def gathered_gemm(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     n_local = qweight.shape[1] * 8
     group_size = k // qzeros.shape[0]
     lib = _lib.load()
-    ws_bytes = lib.to_awq_gemm_workspace_size(m, k, n_local, group_size)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    ws_bytes = _lib.workspace_bytes("to_awq_gemm_workspace_size", m, k, n_local, group_size)
+    ws = _lib.workspace(ws_bytes, x.get_device())
     table = (ctypes.c_void_p * world)(*bufs.ptrs[b])
     rc = lib.to_awq_gemm_gather(xx.data_ptr(), qw.data_ptr(), scales.data_ptr(),
                                 _lib.DTYPE_CODES[dtype], qz.data_ptr(), table, world, rank, m, k,
@@ -298,8 +298,8 @@ def gathered_gemm_act(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tens
     n_local = qweight.shape[1] * 8
     group_size = k // qzeros.shape[0]
     lib = _lib.load()
-    ws_bytes = lib.to_awq_gemm_workspace_size(m, k, n_local, group_size)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    ws_bytes = _lib.workspace_bytes("to_awq_gemm_workspace_size", m, k, n_local, group_size)
+    ws = _lib.workspace(ws_bytes, x.get_device())
     table = (ctypes.c_void_p * world)(*bufs.ptrs[b])
     rc = lib.to_awq_gemm_act_gather(xx.data_ptr(), qw.data_ptr(), scales.data_ptr(),
                                     _lib.DTYPE_CODES[dtype], qz.data_ptr(), table, world, rank,
