@@ -183,18 +183,19 @@ def workspace_bytes(query: str, *shape: int) -> int:
     return v
 
 
-def workspace(nbytes: int, device: int) -> torch.Tensor | None:
+def workspace(nbytes: int, device: int, stream: int | None = None) -> torch.Tensor | None:
     """Scratch of at least `nbytes` for a call about to be queued on the current stream of
     `device`. One buffer per (device, stream) serves consecutive calls: every kernel that takes a
     workspace touches it only after the previous kernel in its stream has completed (the
     decode kernel waits on griddepcontrol.wait first, the others are ordinary launches), and
     its flags are per-launch epochs left at zero once consumed. While the stream is being
-    captured into a CUDA graph each call gets its own buffer from the graph's memory pool."""
+    captured into a CUDA graph each call gets its own buffer from the graph's memory pool.
+    `stream` is that current stream (stream_ptr(device)) when the caller has it already."""
     if nbytes <= 0:
         return None
     if torch.cuda.is_current_stream_capturing():
         return torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", device))
-    key = (device, stream_ptr(device))
+    key = (device, stream_ptr(device) if stream is None else stream)
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
         with _WS_LOCK:

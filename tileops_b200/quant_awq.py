@@ -131,16 +131,18 @@ def _gemm_args(op: str, input: torch.Tensor, qweight: torch.Tensor, scales: torc
     if input.ndim != 2:
         raise ValueError(f"{op}: input must be 2-D [M, K]")
     m, k = input.shape
-    if qweight.shape[0] != k:
-        raise ValueError(f"{op}: qweight rows {qweight.shape[0]} != K={k}")
-    n = qweight.shape[1] * 8
-    num_groups = qzeros.shape[0]
+    qws = qweight.shape
+    if qws[0] != k:
+        raise ValueError(f"{op}: qweight rows {qws[0]} != K={k}")
+    n = qws[1] * 8
+    qzs = qzeros.shape
+    num_groups = qzs[0]
     group_size = _infer_group_size(k, num_groups)
     if n <= 0 or m <= 0:
         raise ValueError(f"{op}: invalid M={m}, N={n}, K={k}")
-    if qweight.shape[1] != n // 8:
+    if qws[1] != n // 8:
         raise ValueError(f"{op}: qweight column count mismatch")
-    if qzeros.shape[1] != n // 8:
+    if qzs[1] != n // 8:
         raise ValueError(f"{op}: qzeros column count mismatch")
     if scales.shape != (num_groups, n):
         raise ValueError(
@@ -180,11 +182,15 @@ def awq_gemm_triton(
     qw = _as_words(qweight)
     qz = _as_words(qzeros)
     s = scales.contiguous()
-    y = torch.empty(m, n, dtype=out_dtype, device=input.device)
+    dev = input.get_device()
+    y = torch.empty(m, n, dtype=out_dtype, device=dev)
     lib = _lib.load()
+    st = _lib.stream_ptr(dev)
     ws_bytes = _lib.workspace_bytes("to_awq_gemm_workspace_size", m, k, n, group_size)
-    ws = _lib.workspace(ws_bytes, input.get_device())
-    if (input.dtype == out_dtype and not input.is_contiguous() and input.stride(1) == 1
+    ws = _lib.workspace(ws_bytes, dev, st)
+    same_dtype = input.dtype == out_dtype
+    contiguous = input.is_contiguous()
+    if (same_dtype and not contiguous and input.stride(1) == 1
             and input.stride(0) >= k and input.stride(0) % 8 == 0
             and input.data_ptr() % 16 == 0):
         # a row-strided slice (the first K columns of a wider activation): read in place where
@@ -192,14 +198,14 @@ def awq_gemm_triton(
         rc = lib.to_awq_gemm_strided(input.data_ptr(), input.stride(0), qw.data_ptr(),
                                      s.data_ptr(), _lib.DTYPE_CODES[out_dtype], qz.data_ptr(),
                                      y.data_ptr(), m, k, n, group_size, _lib.ptr(ws), ws_bytes,
-                                     _lib.stream_ptr())
+                                     st)
         if rc != _lib.TO_EUNSUPPORTED:
             _lib.check(rc, "awq_gemm_triton")
             return y
-    x = input.to(out_dtype).contiguous()
+    x = input if same_dtype and contiguous else input.to(out_dtype).contiguous()
     _lib.call("to_awq_gemm", x.data_ptr(), qw.data_ptr(), s.data_ptr(),
               _lib.DTYPE_CODES[out_dtype], qz.data_ptr(), y.data_ptr(), m, k, n, group_size,
-              _lib.ptr(ws), ws_bytes, _lib.stream_ptr())
+              _lib.ptr(ws), ws_bytes, st)
     return y
 
 
@@ -238,16 +244,19 @@ def _gemm_act(op: str, act: int, input, qweight, scales, qzeros, split_k_iters) 
     if n % 16 != 0:
         raise ValueError(f"{op}: N={n} is not a multiple of 16 (gate and up blocks of 8)")
     out_dtype = scales.dtype
-    x = input.to(out_dtype).contiguous()
+    x = input if input.dtype == out_dtype and input.is_contiguous() else \
+        input.to(out_dtype).contiguous()
     qw = _as_words(qweight)
     qz = _as_words(qzeros)
     s = scales.contiguous()
-    y = torch.empty(m, n // 2, dtype=out_dtype, device=input.device)
+    dev = input.get_device()
+    y = torch.empty(m, n // 2, dtype=out_dtype, device=dev)
+    st = _lib.stream_ptr(dev)
     ws_bytes = _lib.workspace_bytes("to_awq_gemm_act_workspace_size", m, k, n, group_size)
-    ws = _lib.workspace(ws_bytes, input.get_device())
+    ws = _lib.workspace(ws_bytes, dev, st)
     _lib.call("to_awq_gemm_act", x.data_ptr(), qw.data_ptr(), s.data_ptr(),
               _lib.DTYPE_CODES[out_dtype], qz.data_ptr(), y.data_ptr(), m, k, n, group_size,
-              act, _lib.ptr(ws), ws_bytes, _lib.stream_ptr())
+              act, _lib.ptr(ws), ws_bytes, st)
     return y
 
 
